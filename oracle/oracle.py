@@ -1,0 +1,316 @@
+"""CPU oracle for nim-lowprec's dequant-GEMV/GEMM hot path -- TEST INFRASTRUCTURE.
+
+This module is the checker, never the product.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm may
+import it.  The product library (``nim_lowprec_b200``) never loads it and has no
+CPU fallback.
+
+It wraps ``lowprec_oracle.c`` (a C restatement of the reference's scalar
+branches; every function there cites the reference file:line it follows) with
+numpy-facing helpers whose argument order follows the reference's Nim procs.
+
+Parity status: pinned.  The encoders are checked bit-for-bit against gguf-py
+and ml_dtypes goldens produced by the reference's own ``tests/gen_reference.py``
+(fixtures under ``tests/golden/``), and the kernels against the reference
+tests' own exact references (``tests/test_sdot.nim`` intRef/refQ8/refQ4,
+restated in numpy in ``tests/test_oracle_kernels.py``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = os.path.join(HERE, "lowprec_oracle.c")
+LIB = os.path.join(HERE, "liblporacle.so")
+
+QK = 32
+Q8_0_BYTES = 34
+Q4_0_BYTES = 18
+
+CFLAGS = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", "-pthread"]
+
+
+def build(force: bool = False) -> str:
+    """Compile the C restatement into ``oracle/liblporacle.so`` (gcc)."""
+    stale = (not os.path.exists(LIB)) or os.path.getmtime(LIB) < os.path.getmtime(SRC)
+    if force or stale:
+        cmd = ["gcc", *CFLAGS, "-o", LIB, SRC, "-lm"]
+        subprocess.run(cmd, check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB)
+        i64, vp, f32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_float
+        L.lpo_f32_to_f16.restype = ctypes.c_uint16
+        L.lpo_f32_to_f16.argtypes = [f32]
+        L.lpo_f16_to_f32.restype = f32
+        L.lpo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.lpo_to_f4e2m1.restype = ctypes.c_uint8
+        L.lpo_to_f4e2m1.argtypes = [f32]
+        L.lpo_f4e2m1_to_f32.restype = f32
+        L.lpo_f4e2m1_to_f32.argtypes = [ctypes.c_uint8]
+        L.lpo_to_e8m0.restype = ctypes.c_uint8
+        L.lpo_to_e8m0.argtypes = [f32]
+        L.lpo_e8m0_to_f32.restype = f32
+        L.lpo_e8m0_to_f32.argtypes = [ctypes.c_uint8]
+        L.lpo_calibrate_symmetric.restype = i64
+        L.lpo_calibrate_symmetric.argtypes = [vp, i64, i64, f32, vp]
+        L.lpo_calibrate_mx.restype = i64
+        L.lpo_calibrate_mx.argtypes = [vp, i64, i64, ctypes.c_int, vp]
+        L.lpo_quantize.argtypes = [vp, i64, vp, i64, ctypes.c_int, vp]
+        L.lpo_quantize_batch.argtypes = [vp, i64, vp, i64, vp]
+        L.lpo_pack_int4.argtypes = [vp, i64, vp]
+        L.lpo_pack_f4.argtypes = [vp, i64, vp]
+        for nm in ("lpo_quantize_q8_0", "lpo_quantize_q4_0"):
+            getattr(L, nm).argtypes = [vp, i64, vp]
+        L.lpo_quantize_q8_0_split.argtypes = [vp, i64, vp, vp]
+        for nm in ("lpo_dequantize_q8_0", "lpo_dequantize_q4_0"):
+            getattr(L, nm).argtypes = [vp, i64, vp]
+        L.lpo_pool_init.restype = vp
+        L.lpo_pool_init.argtypes = [ctypes.c_int]
+        L.lpo_pool_shutdown.argtypes = [vp]
+        L.lpo_pool_thread_count.restype = ctypes.c_int
+        L.lpo_pool_thread_count.argtypes = [vp]
+        L.lpo_shard_count.restype = ctypes.c_int
+        L.lpo_shard_count.argtypes = [i64, ctypes.c_int]
+        L.lpo_run.argtypes = [vp, ctypes.c_int, vp, vp, i64, vp, vp, i64, i64, vp, i64]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle buffers must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ------------------------------------------------------------ codecs --
+
+def f32_to_f16(x: float) -> int:
+    return int(lib().lpo_f32_to_f16(float(x)))
+
+
+def f16_to_f32(h: int) -> float:
+    return float(lib().lpo_f16_to_f32(int(h)))
+
+
+def to_f4e2m1(x: float) -> int:
+    return int(lib().lpo_to_f4e2m1(float(x)))
+
+
+def to_e8m0(x: float) -> int:
+    return int(lib().lpo_to_e8m0(float(x)))
+
+
+def e8m0_to_f32(c: int) -> float:
+    return float(lib().lpo_e8m0_to_f32(int(c)))
+
+
+# ---------------------------------------------------------- encoders --
+
+def calibrateSymmetric(x, groupSize: int, qmax: float) -> np.ndarray:
+    x = _c(x, np.float32)
+    n = x.size
+    gs = groupSize if groupSize > 0 else max(n, 1)
+    out = np.empty((n + gs - 1) // gs, np.float32)
+    lib().lpo_calibrate_symmetric(_p(x), n, groupSize, float(qmax), _p(out))
+    return out
+
+
+def calibrateMX(x, blockSize: int, elemEmax: int) -> np.ndarray:
+    x = _c(x, np.float32)
+    out = np.empty((x.size + blockSize - 1) // blockSize, np.float32)
+    lib().lpo_calibrate_mx(_p(x), x.size, blockSize, int(elemEmax), _p(out))
+    return out
+
+
+def quantize(x, scales, groupSize: int, kind: str) -> np.ndarray:
+    """quantize[T] for symmetric QParams; kind in {'i8', 'i4', 'f4'}.
+    'i4' returns one signed value per int8, 'f4' one e2m1 code per uint8."""
+    x = _c(x, np.float32)
+    scales = _c(scales, np.float32)
+    out = np.empty(x.size, np.int8)
+    lib().lpo_quantize(_p(x), x.size, _p(scales), groupSize, {"i8": 0, "i4": 1, "f4": 2}[kind], _p(out))
+    return out.view(np.uint8) if kind == "f4" else out
+
+
+def quantizeBatch(x, scales, groupSize: int) -> np.ndarray:
+    x = _c(x, np.float32)
+    scales = _c(scales, np.float32)
+    out = np.empty(x.size, np.int8)
+    lib().lpo_quantize_batch(_p(x), x.size, _p(scales), groupSize, _p(out))
+    return out
+
+
+def packInt4(vals) -> np.ndarray:
+    vals = _c(vals, np.int8)
+    out = np.zeros((vals.size + 1) // 2, np.uint8)
+    lib().lpo_pack_int4(_p(vals), vals.size, _p(out))
+    return out
+
+
+def packF4(codes) -> np.ndarray:
+    codes = _c(codes, np.uint8)
+    out = np.zeros((codes.size + 1) // 2, np.uint8)
+    lib().lpo_pack_f4(_p(codes), codes.size, _p(out))
+    return out
+
+
+def quantizeQ8_0(src) -> np.ndarray:
+    """Returns raw blocks, shape (n/32, 34) uint8."""
+    src = _c(src, np.float32)
+    assert src.size % QK == 0
+    out = np.empty((src.size // QK, Q8_0_BYTES), np.uint8)
+    lib().lpo_quantize_q8_0(_p(src), src.size, _p(out))
+    return out
+
+
+def quantizeQ8_0Split(src):
+    """quantizeQ8_0 split into (qs int8[n], d float32[n/32]) with d = f32(f16 d)."""
+    src = _c(src, np.float32)
+    assert src.size % QK == 0
+    qs = np.empty(src.size, np.int8)
+    d = np.empty(src.size // QK, np.float32)
+    lib().lpo_quantize_q8_0_split(_p(src), src.size, _p(qs), _p(d))
+    return qs, d
+
+
+def quantizeQ4_0(src) -> np.ndarray:
+    src = _c(src, np.float32)
+    assert src.size % QK == 0
+    out = np.empty((src.size // QK, Q4_0_BYTES), np.uint8)
+    lib().lpo_quantize_q4_0(_p(src), src.size, _p(out))
+    return out
+
+
+def dequantizeQ8_0(blocks) -> np.ndarray:
+    blocks = _c(blocks, np.uint8).reshape(-1, Q8_0_BYTES)
+    out = np.empty(blocks.shape[0] * QK, np.float32)
+    lib().lpo_dequantize_q8_0(_p(blocks), blocks.shape[0], _p(out))
+    return out
+
+
+def dequantizeQ4_0(blocks) -> np.ndarray:
+    blocks = _c(blocks, np.uint8).reshape(-1, Q4_0_BYTES)
+    out = np.empty(blocks.shape[0] * QK, np.float32)
+    lib().lpo_dequantize_q4_0(_p(blocks), blocks.shape[0], _p(out))
+    return out
+
+
+# ----------------------------------------------------------- kernels --
+
+KIND = {"i8": 0, "i4": 1, "f4": 2, "q8_0": 3, "q4_0": 4, "q8": 5, "i4q8": 6,
+        "q8_0q8": 7, "q4_0q8": 8, "gemm_q8": 9, "gemm_i4q8": 10}
+
+
+class Pool:
+    """LpPool restatement (pthreads): initPool / threadCount / shutdown."""
+
+    def __init__(self, threads: int = 0):
+        self._h = lib().lpo_pool_init(int(threads))
+
+    @property
+    def handle(self):
+        return self._h
+
+    def threadCount(self) -> int:
+        return int(lib().lpo_pool_thread_count(self._h)) if self._h else 0
+
+    def shutdown(self) -> None:
+        if self._h:
+            lib().lpo_pool_shutdown(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.shutdown()
+        except Exception:
+            pass
+
+
+def _run(kind, w, ws, gs, x, xs, k, n, rows, pool=None) -> np.ndarray:
+    y = np.empty(rows * max(n, 1), np.float32)
+    keep = [w, ws, x, xs]
+    ptr = [(_p(a) if a is not None else None) for a in keep]
+    lib().lpo_run(pool.handle if pool is not None else None, KIND[kind], ptr[0], ptr[1], int(gs),
+                  ptr[2], ptr[3], int(k), int(n), _p(y), int(rows))
+    return y
+
+
+def dequantGemv(wq, scales, groupSize, x, pool=None):
+    x = _c(x, np.float32); wq = _c(wq, np.int8); scales = _c(scales, np.float32)
+    return _run("i8", wq, scales, groupSize, x, None, x.size, 1, wq.size // x.size, pool)
+
+
+def dequantGemvI4(wpacked, scales, groupSize, x, pool=None):
+    x = _c(x, np.float32); wp = _c(wpacked, np.uint8); scales = _c(scales, np.float32)
+    return _run("i4", wp, scales, groupSize, x, None, x.size, 1, wp.size // (x.size // 2), pool)
+
+
+def dequantGemvF4(wpacked, scales, groupSize, x, pool=None):
+    x = _c(x, np.float32); wp = _c(wpacked, np.uint8); scales = _c(scales, np.float32)
+    return _run("f4", wp, scales, groupSize, x, None, x.size, 1, wp.size // (x.size // 2), pool)
+
+
+def dequantGemvQ8_0(w, blocksPerRow, x, pool=None):
+    x = _c(x, np.float32); w = _c(w, np.uint8).reshape(-1)
+    rows = w.size // (blocksPerRow * Q8_0_BYTES)
+    return _run("q8_0", w, None, blocksPerRow, x, None, x.size, 1, rows, pool)
+
+
+def dequantGemvQ4_0(w, blocksPerRow, x, pool=None):
+    x = _c(x, np.float32); w = _c(w, np.uint8).reshape(-1)
+    rows = w.size // (blocksPerRow * Q4_0_BYTES)
+    return _run("q4_0", w, None, blocksPerRow, x, None, x.size, 1, rows, pool)
+
+
+def dequantGemvQ8(wq, wScales, groupSize, xq, xScales, pool=None):
+    wq = _c(wq, np.int8); ws = _c(wScales, np.float32); xq = _c(xq, np.int8); xs = _c(xScales, np.float32)
+    return _run("q8", wq, ws, groupSize, xq, xs, xq.size, 1, wq.size // xq.size, pool)
+
+
+def dequantGemvI4Q8(wpacked, wScales, groupSize, xq, xScales, pool=None):
+    wp = _c(wpacked, np.uint8); ws = _c(wScales, np.float32); xq = _c(xq, np.int8); xs = _c(xScales, np.float32)
+    return _run("i4q8", wp, ws, groupSize, xq, xs, xq.size, 1, wp.size // (xq.size // 2), pool)
+
+
+def dequantGemvQ8_0Q8(w, blocksPerRow, xq, pool=None):
+    w = _c(w, np.uint8).reshape(-1); xq = _c(xq, np.uint8).reshape(-1)
+    rows = w.size // (blocksPerRow * Q8_0_BYTES)
+    return _run("q8_0q8", w, None, blocksPerRow, xq, None, blocksPerRow * QK, 1, rows, pool)
+
+
+def dequantGemvQ4_0Q8(w, blocksPerRow, xq, pool=None):
+    w = _c(w, np.uint8).reshape(-1); xq = _c(xq, np.uint8).reshape(-1)
+    rows = w.size // (blocksPerRow * Q4_0_BYTES)
+    return _run("q4_0q8", w, None, blocksPerRow, xq, None, blocksPerRow * QK, 1, rows, pool)
+
+
+def dequantGemmQ8(wq, wScales, groupSize, xq, xScales, n, pool=None):
+    wq = _c(wq, np.int8); ws = _c(wScales, np.float32); xq = _c(xq, np.int8); xs = _c(xScales, np.float32)
+    k = xq.size // n
+    return _run("gemm_q8", wq, ws, groupSize, xq, xs, k, n, wq.size // k, pool)
+
+
+def dequantGemmI4Q8(wpacked, wScales, groupSize, xq, xScales, n, pool=None):
+    wp = _c(wpacked, np.uint8); ws = _c(wScales, np.float32); xq = _c(xq, np.int8); xs = _c(xScales, np.float32)
+    k = xq.size // n
+    return _run("gemm_i4q8", wp, ws, groupSize, xq, xs, k, n, wp.size // (k // 2), pool)
+
+
+def shardCount(rows: int, threads: int) -> int:
+    return int(lib().lpo_shard_count(int(rows), int(threads)))

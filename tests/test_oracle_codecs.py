@@ -1,0 +1,148 @@
+"""Pin the oracle's encoders and element codecs to external golden vectors.
+
+Fixtures in tests/golden/ come from the reference's own generator
+(gen_reference.py, via tests/golden/make_golden.py): gguf-py for ggml Q8_0/Q4_0
+and the OCP-MX scheme with ml_dtypes elements.  These are the checks of
+test_scheme_conformance.nim:46-86,117-140, test_mx_conformance.nim and
+test_f16_conformance.nim, run against the oracle.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rd(name, dtype):
+    return np.fromfile(os.path.join(G, name), dtype=dtype)
+
+
+def test_q8_0_quantize_bytes_match_gguf():
+    x = rd("ref_scheme_input.bin", np.float32)
+    want = rd("ref_ggml_q8_0_bytes.bin", np.uint8)
+    got = O.quantizeQ8_0(x).reshape(-1)
+    assert got.size == want.size
+    assert np.array_equal(got, want)
+
+
+def test_q4_0_quantize_bytes_match_gguf():
+    x = rd("ref_scheme_input.bin", np.float32)
+    want = rd("ref_ggml_q4_0_bytes.bin", np.uint8)
+    got = O.quantizeQ4_0(x).reshape(-1)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_ggml_dequant_of_gguf_bytes_bit_exact(fmt):
+    raw = rd(f"ref_ggml_{fmt}_bytes.bin", np.uint8)
+    want = rd(f"ref_ggml_{fmt}_dq.bin", np.uint32)
+    dq = O.dequantizeQ8_0(raw) if fmt == "q8_0" else O.dequantizeQ4_0(raw)
+    assert np.array_equal(dq.view(np.uint32), want)
+
+
+def test_golden_input_has_the_edge_blocks():
+    x = rd("ref_scheme_input.bin", np.float32)
+    assert np.all(x[100:132] == 0)                       # the all-zero block
+    assert np.all(x[4096:4104] == np.float32(1e-30))     # the tiny-scale block
+
+
+def test_mx_fp4_scheme_end_to_end():
+    """calibrateMX(x, 32, 2) + quantize + dequantize vs the OCP-MX golden
+    (test_scheme_conformance.nim:117-140)."""
+    x = rd("ref_mx_input.bin", np.float32)
+    want = rd("ref_mx_f4e2m1_dq.bin", np.uint32)
+    sc = O.calibrateMX(x, 32, 2)
+    codes = O.quantize(x, sc, 32, "f4")
+    lut = np.array([O.lib().lpo_f4e2m1_to_f32(c) for c in range(16)], np.float32)
+    dq = (lut[codes] * np.repeat(sc, 32)).astype(np.float32)   # dequantize: decode * scale
+    assert np.array_equal(dq.view(np.uint32), want)
+
+
+def test_mx_scales_are_exact_e8m0():
+    x = rd("ref_mx_input.bin", np.float32)
+    sc = O.calibrateMX(x, 32, 2)
+    for s in sc:
+        assert O.e8m0_to_f32(O.to_e8m0(float(s))) == s
+
+
+def test_e2m1_encode_matches_ml_dtypes():
+    z = np.load(os.path.join(G, "e2m1_encode.npz"))
+    ins, outs = z["ins"], z["outs"]
+    f = ins.view(np.float32)
+    L = O.lib()
+    got = np.array([L.lpo_to_f4e2m1(float(v)) for v in f], np.uint8)
+    assert np.array_equal(got, outs)
+
+
+def test_e2m1_decode_round_trips_every_code():
+    """test_mx_conformance.nim:24-28 (code 8 is -0 and encodes back to 8)."""
+    for c in range(16):
+        assert O.to_f4e2m1(O.lib().lpo_f4e2m1_to_f32(c)) == c
+
+
+def test_e8m0_encode_matches_ml_dtypes():
+    z = np.load(os.path.join(G, "e8m0_encode.npz"))
+    f = z["ins"].view(np.float32)
+    L = O.lib()
+    got = np.array([L.lpo_to_e8m0(float(v)) for v in f], np.uint8)
+    assert np.array_equal(got, z["outs"])
+
+
+def test_f16_encode_matches_numpy():
+    z = np.load(os.path.join(G, "f16_encode.npz"))
+    f = z["ins"].view(np.float32)
+    L = O.lib()
+    got = np.array([L.lpo_f32_to_f16(float(v)) for v in f], np.uint16)
+    want = z["outs"]
+    nan = np.isnan(f)
+    assert np.array_equal(got[~nan], want[~nan])
+    # NaN stays NaN (payload rules differ between ports; only NaN-ness matters)
+    assert np.all((got[nan] & 0x7C00) == 0x7C00) and np.all((got[nan] & 0x03FF) != 0)
+
+
+def test_f16_decode_exhaustive():
+    codes = np.arange(65536, dtype=np.uint16)
+    want = codes.view(np.float16).astype(np.float32).view(np.uint32)
+    L = O.lib()
+    got = np.array([L.lpo_f16_to_f32(int(c)) for c in codes], np.float32).view(np.uint32)
+    nan = np.isnan(codes.view(np.float16))
+    assert np.array_equal(got[~nan], want[~nan])
+
+
+def test_int4_pack_layout():
+    """test_intx_conformance.nim:32-36: low = 3, high = -2 -> 0xE3."""
+    assert O.packInt4(np.array([3, -2], np.int8))[0] == 0xE3
+    # odd tail keeps only the low nibble (test_intx_conformance.nim:49-52)
+    assert O.packInt4(np.array([5], np.int8))[0] & 0x0F == 5
+
+
+def test_i8_i4_encoders():
+    """test_intx_conformance.nim:8-30: rounding and clamps."""
+    one = np.ones(1, np.float32)
+    for v, q in [(2.6, 3), (-2.6, -3), (200.0, 127), (-200.0, -128), (2.5, 3), (-2.5, -3)]:
+        assert O.quantize(np.array([v], np.float32), one, 1, "i8")[0] == q
+    for v, q in [(100.0, 7), (-100.0, -8), (2.6, 3)]:
+        assert O.quantize(np.array([v], np.float32), one, 1, "i4")[0] == q
+
+
+def test_calibrate_symmetric_zero_group_and_ragged_tail():
+    """quant.nim:84-110: a zero group gets scale 1.0; the last group may be short."""
+    assert O.calibrateSymmetric(np.zeros(8, np.float32), 0, 127.0)[0] == 1.0
+    x = np.arange(100, dtype=np.float32) - 50
+    sc = O.calibrateSymmetric(x, 64, 127.0)
+    assert sc.size == 2
+    assert sc[0] == np.float32(50.0) / np.float32(127.0)
+    assert sc[1] == np.float32(49.0) / np.float32(127.0)
+
+
+def test_q8_0_split_matches_blocks():
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(4096).astype(np.float32)
+    blocks = O.quantizeQ8_0(x)
+    qs, d = O.quantizeQ8_0Split(x)
+    assert np.array_equal(blocks[:, 2:].reshape(-1).view(np.int8), qs)
+    dh = blocks[:, :2].copy().view(np.uint16).reshape(-1)
+    assert np.array_equal(dh.view(np.float16).astype(np.float32), d)
