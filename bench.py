@@ -1,0 +1,465 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused dequant-GEMV hot path (BASELINE.json `metric`).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (N = 1): BASELINE config 1 -- ggml Q4_0 fused dequant-GEMV
+with fp32 activations, 11008 x 4096 (Llama-7B MLP up), synthetic seeded
+N(0, 0.02) weights encoded on the GPU by the library's own Q4_0 encoder and
+N(0, 1) activations.  A step is one GEMV call.  `value` is algorithmic HBM
+bytes per step (weights + activations + output) / device time, with the
+weights resident; 16+ distinct weight copies (> 3x the 126 MB L2) rotate so no
+step reads another step's weights from L2.  The timed K steps run as CUDA
+graph replays bracketed by CUDA events on the launching stream.
+
+N > 1 (torchrun, one process per GPU): weak scaling of the LpPool form -- each
+rank owns 11008 contiguous rows of an (N*11008) x 4096 matrix, runs the same
+GEMV on them and all-gathers the output vector over NCCL every step, so every
+rank ends the step holding the whole y.
+
+`--impl reference` times the reference's algorithm on the host cores (the C
+restatement in oracle/, pooled over every core like LpPool) on the same
+workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "dequant-GEMV HBM GB/s (% of B200 peak) per format; Q8_0 GEMM int8 TOPS"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+M1, K1 = 11008, 4096   # config 1
+
+
+def cfg1_bytes(M=M1, K=K1) -> int:
+    """Algorithmic bytes of one config-1 call: Q4_0 blocks + fp32 x + fp32 y."""
+    return M * (K // 32) * 18 + K * 4 + M * 4
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the top kernel from a committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_id: str):
+        self.device_id = device_id
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.device_id], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().strip().splitlines() if r.strip()]
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ GPU workload
+class Cfg1Workload:
+    """Rotating copies of one rank's Q4_0 weight rows, x, y (device)."""
+
+    def __init__(self, torch, L, M, K, seed, ncopies=None):
+        self.torch, self.L, self.M, self.K = torch, L, M, K
+        self.bpr = K // 32
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        w = torch.randn(M * K, generator=g, device="cuda", dtype=torch.float32) * 0.02
+        blocks = torch.empty(M * self.bpr * 18, dtype=torch.uint8, device="cuda")
+        L.quantizeQ4_0Batch(w, blocks)
+        del w
+        wbytes = blocks.numel()
+        self.ncopies = ncopies or max(2, -(-3 * L2_BYTES // wbytes) + 1)
+        self.w = [blocks] + [blocks.clone() for _ in range(self.ncopies - 1)]
+        g.manual_seed(seed + 1_000_000)
+        self.x = torch.randn(K, generator=g, device="cuda", dtype=torch.float32)
+        self.y = torch.empty(M, dtype=torch.float32, device="cuda")
+
+    def step(self, i):
+        self.L.dequantGemvQ4_0(self.w[i % self.ncopies], self.bpr, self.x, self.y)
+
+
+def graph_time(torch, step, K, W, barrier, chunk=500):
+    """W eager warm-up steps, then exactly K steps timed as graph replays."""
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    G = min(chunk, K)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(G):
+                step(i)
+        graphs.append((g, K // G))
+        rem = K % G
+        if rem:
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=s):
+                for i in range(rem):
+                    step(i)
+            graphs.append((g2, 1))
+    torch.cuda.current_stream().wait_stream(s)
+    for g, _ in graphs:       # upload + one untimed pass
+        g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for g, reps in graphs:
+        for _ in range(reps):
+            g.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    return ms, graphs
+
+
+def device_uuid(torch):
+    try:
+        u = torch.cuda.get_device_properties(torch.cuda.current_device()).uuid
+        s = str(u)
+        return s if s.startswith("GPU-") else "GPU-" + s
+    except Exception:
+        return str(torch.cuda.current_device())
+
+
+# -------------------------------------------------------------- CPU side
+def cpu_baseline(seconds=8.0, M=M1, K=K1, threads=0):
+    """The reference's algorithm (oracle port, pooled over all host cores)
+    on config 1; returns (GB/s, cores, sample description)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal(M * K, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    x = rng.standard_normal(K, dtype=np.float32)
+    blocks = O.quantizeQ4_0(w).reshape(-1)
+    del w
+    pool = O.Pool(threads)
+    cores = pool.threadCount()
+    try:
+        O.dequantGemvQ4_0(blocks, K // 32, x, pool=pool)   # warm
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            O.dequantGemvQ4_0(blocks, K // 32, x, pool=pool)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= seconds:
+                break
+    finally:
+        pool.shutdown()
+    gbs = n * cfg1_bytes(M, K) / dt / 1e9
+    return gbs, cores, f"{n} full config-1 GEMVs ({M}x{K}) in {dt:.1f} s, LpPool-style row shards over {cores} threads"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal(M1 * K1, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    x = rng.standard_normal(K1, dtype=np.float32)
+    blocks = O.quantizeQ4_0(w).reshape(M1, -1)
+    del w
+    pool = O.Pool(0)
+    cores = pool.threadCount()
+    # size a step so the whole run stays within ~2 minutes
+    t0 = time.perf_counter()
+    O.dequantGemvQ4_0(blocks, K1 // 32, x, pool=pool)
+    t_full = time.perf_counter() - t0
+    budget = 90.0 / max(1, args.steps + args.warmup)
+    rows = int(min(M1, max(64 * cores, M1 * budget / max(t_full, 1e-6))))
+    rows = max(1, min(M1, rows))
+    sub = np.ascontiguousarray(blocks[:rows]).reshape(-1)
+    for _ in range(args.warmup):
+        O.dequantGemvQ4_0(sub, K1 // 32, x, pool=pool)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.dequantGemvQ4_0(sub, K1 // 32, x, pool=pool)
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    nbytes = cfg1_bytes(rows, K1)
+    gbs = args.steps * nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config1: ggml Q4_0 fused dequant-GEMV, fp32 activations, 11008x4096",
+                   "sample_rows": rows},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} of {M1} rows per step (C restatement of the scalar path, LpPool-style pool)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-formats", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    import nim_lowprec_b200 as L
+
+    wl = Cfg1Workload(torch, L, M1, K1, seed=1 + rank)
+    y_all = torch.empty(world * M1, dtype=torch.float32, device="cuda") if world > 1 else None
+
+    def step(i):
+        wl.step(i)
+        if dist is not None:
+            dist.all_gather_into_tensor(y_all, wl.y)
+
+    clk = ClockSampler(device_uuid(torch))
+    clk.start()
+    ms, graphs = graph_time(torch, step, args.steps, max(3, args.warmup), barrier)
+    clocks = clk.stop()
+    del graphs
+    t = torch.tensor([ms], device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    per_step_ms = ms / args.steps
+    total_bytes = world * args.steps * cfg1_bytes()
+    value = total_bytes / (ms / 1e3) / 1e9
+
+    # roofline of the dominant kernel (this rank's GEMV launches)
+    peak, peak_kind = load_peaks()
+    if world == 1:
+        kernel_ms = per_step_ms
+    else:  # time the GEMV alone for the roofline
+        kms, g2 = graph_time(torch, wl.step, min(args.steps, 20000), 3, barrier)
+        del g2
+        kernel_ms = kms / min(args.steps, 20000)
+    achieved = cfg1_bytes() / (kernel_ms / 1e3) / 1e9
+    traffic = load_traffic().get("gemv_q4_0_cfg1")
+
+    # e2e through the public API: x from pinned host memory in, y back out
+    xh = torch.empty(K1, dtype=torch.float32).pin_memory()
+    xh.copy_(torch.randn(K1))
+    yh = torch.empty(M1, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        wl.x.copy_(xh, non_blocking=True)
+        wl.step(i)
+        if dist is not None:
+            dist.all_gather_into_tensor(y_all, wl.y)
+        yh.copy_(wl.y, non_blocking=True)
+
+    e2e_steps = min(args.steps, 20000)
+    e_ms, g3 = graph_time(torch, e2e_step, e2e_steps, 3, barrier)
+    del g3
+    t = torch.tensor([e_ms], device="cuda")
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e_ms = float(t.item())
+    e2e_value = world * e2e_steps * cfg1_bytes() / (e_ms / 1e3) / 1e9
+
+    formats = None
+    if not args.no_formats and world == 1:
+        formats = per_format(torch, L, barrier)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline()
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": "config1: ggml Q4_0 fused dequant-GEMV, fp32 activations, 11008x4096 per GPU",
+            "rows_per_gpu": M1, "k": K1, "algorithmic_bytes_per_step_per_gpu": cfg1_bytes(),
+            "l2": f"{wl.ncopies} rotating weight copies ({wl.ncopies * M1 * K1 // 32 * 18 / 1e6:.0f} MB > 3x L2)",
+            "parallelism": "single GPU" if world == 1 else f"rows sharded over {world} GPUs + NCCL all-gather of y per step",
+            "timing": "CUDA-graph replays, CUDA events on the launching stream, max over ranks",
+        },
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_kind": f"{peak_kind} hbm_gbs"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K1 * 4,
+                "d2h_bytes_per_step": M1 * 4, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if formats:
+        line["formats"] = formats
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def per_format(torch, L, barrier, steps=5000):
+    """Secondary numbers for the other BASELINE configs (not the headline)."""
+    out = {}
+    peak, _ = load_peaks()
+    g = torch.Generator(device="cuda")
+
+    def rnd(n, seed, scale=1.0):
+        g.manual_seed(seed)
+        return torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * scale
+
+    # config 0: dequantGemvQ8 4096^2, weights and activations Q8_0 (split form)
+    M = K = 4096
+    w = rnd(M * K, 0, 0.02)
+    wq = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    wd = torch.empty(M * K // 32, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(w, wq, wd)
+    del w
+    x = rnd(K, 1_000_000)
+    xq = torch.empty(K, dtype=torch.int8, device="cuda")
+    xs = torch.empty(K // 32, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(x, xq, xs)
+    y = torch.empty(M, dtype=torch.float32, device="cuda")
+    nb = M * K + M * K // 32 * 4 + K + K // 32 * 4 + M * 4
+    R = -(-3 * L2_BYTES // (M * K + M * K // 8)) + 1
+    copies = [(wq, wd)] + [(wq.clone(), wd.clone()) for _ in range(R - 1)]
+    ms, gr = graph_time(torch, lambda i: L.dequantGemvQ8(*copies[i % R], 32, xq, xs, y), steps, 5, barrier)
+    del gr
+    v = nb / (ms / steps / 1e3) / 1e9
+    out["config0_q8xq8_4096"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3), "us": round(ms / steps * 1e3, 2)}
+    del copies
+
+    # config 2: MXFP4 14336x4096
+    M, K = 14336, 4096
+    w = rnd(M * K, 2, 0.02)
+    sc = torch.empty(M * K // 32, dtype=torch.float32, device="cuda")
+    L.calibrateMX(w, 32, 2, sc)
+    pk = torch.empty(M * K // 2, dtype=torch.uint8, device="cuda")
+    L.quantizeF4Packed(w, sc, 32, pk)
+    del w
+    x = rnd(K, 1_000_002)
+    y = torch.empty(M, dtype=torch.float32, device="cuda")
+    nb = M * K // 2 + M * K // 32 * 4 + K * 4 + M * 4
+    R = -(-3 * L2_BYTES // nb) + 1
+    copies = [(pk, sc)] + [(pk.clone(), sc.clone()) for _ in range(R - 1)]
+    ms, gr = graph_time(torch, lambda i: L.dequantGemvF4(copies[i % R][0], copies[i % R][1], 32, x, y), steps, 5, barrier)
+    del gr
+    v = nb / (ms / steps / 1e3) / 1e9
+    out["config2_mxfp4_14336x4096"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3), "us": round(ms / steps * 1e3, 2)}
+    del copies
+
+    # config 3: dequantGemmQ8 4096^2 x B
+    M = K = 4096
+    w = rnd(M * K, 3, 0.02)
+    wq = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    wd = torch.empty(M * K // 32, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(w, wq, wd)
+    del w
+    for B in (8, 64, 512):
+        x = rnd(K * B, 1_000_003)
+        xq = torch.empty(K * B, dtype=torch.int8, device="cuda")
+        xs = torch.empty(K * B // 32, dtype=torch.float32, device="cuda")
+        L.quantizeQ8_0Split(x, xq, xs)
+        y = torch.empty(M * B, dtype=torch.float32, device="cuda")
+        st = 200 if B == 512 else 1000
+        ms, gr = graph_time(torch, lambda i: L.dequantGemmQ8(wq, wd, 32, xq, xs, B, y), st, 3, barrier)
+        del gr
+        us = ms / st * 1e3
+        tops = 2 * M * K * B / (us / 1e6) / 1e12
+        out[f"config3_gemm_q8_B{B}"] = {"TOPS": round(tops, 2), "us": round(us, 2)}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

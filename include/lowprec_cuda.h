@@ -1,0 +1,234 @@
+/*
+ * lowprec_cuda.h -- C ABI of the B200 (sm_100a) implementation of
+ * nim-lowprec's fused dequant-GEMV/GEMM hot path (liblowprec_cuda.so).
+ *
+ * Each entry point replaces one Nim proc of the reference and keeps its
+ * argument order.  Nim's C backend passes an `openArray[T]` as a (T*, length)
+ * pair, so every array argument here is a pointer followed by its element
+ * count, and shapes are derived from those lengths exactly as the reference
+ * derives them (m = y.len, k = x.len, gpr = k div groupSize, ...).
+ *
+ * Two forms per kernel:
+ *   lp_*   DEVICE pointers + a CUDA stream; asynchronous, stream-ordered,
+ *          allocates nothing, reentrant across streams.
+ *   lph_*  HOST pointers, blocking: the literal drop-in for the Nim
+ *          signature.  Stages through a cached per-thread device workspace,
+ *          copies every input host->device, runs, copies the output back.
+ *
+ * Preconditions the reference asserts (e.g. simd/dequant.nim:768-771) return
+ * LP_ERR_SHAPE here instead of raising; nothing is launched in that case.
+ * Block formats are byte-compatible with the reference's packed objects:
+ *   BlockQ8_0 = { uint16 d (fp16 bits); int8 qs[32] }   34 bytes (ggml.nim:26-28)
+ *   BlockQ4_0 = { uint16 d (fp16 bits); uint8 qs[16] }  18 bytes (ggml.nim:30-32)
+ * so a `w_len`/`xq_len` of a block array counts BLOCKS, not bytes.
+ */
+#ifndef LOWPREC_CUDA_H
+#define LOWPREC_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status -- */
+#define LP_OK 0
+#define LP_ERR_SHAPE 1       /* a length precondition of the reference failed */
+#define LP_ERR_ARG 2         /* null pointer, negative length, bad option */
+#define LP_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define LP_ERR_NCCL 4        /* a collective failed */
+#define LP_ERR_TIMEOUT 5     /* a bounded device-side wait ran out */
+#define LP_ERR_UNSUPPORTED 6 /* shape outside what this build implements */
+#define LP_ERR_NO_DEVICE 7   /* no usable CUDA device */
+
+#define LP_QK 32
+#define LP_BLOCK_Q8_0_BYTES 34
+#define LP_BLOCK_Q4_0_BYTES 18
+
+typedef void *lp_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
+
+/* Library version, e.g. 100 for 0.1.0. */
+int lp_version(void);
+
+/* Message for a status code (static string). */
+const char *lp_status_string(int status);
+
+/* Synchronise the current device, then return (and clear) the first error a
+ * kernel of this library recorded on it (LP_OK if none).  Device-side
+ * failures never trap; they are reported here. */
+int lp_device_error(void);
+
+/* ======================= fp32-activation fused dequant-GEMVs ========== */
+
+/* dequantGemv: int8 weights M x K, scales M x (K/groupSize), fp32 x -> y.
+ * Replaces simd/dequant.nim:210-257 (proc dequantGemv*). */
+int lp_dequant_gemv(const int8_t *wq, int64_t wq_len, const float *scales, int64_t scales_len,
+                    int64_t group_size, const float *x, int64_t x_len, float *y, int64_t y_len,
+                    lp_stream_t stream);
+
+/* dequantGemvI4: packed two's-complement int4 (low nibble = even column).
+ * Replaces simd/dequant.nim:259-339 (proc dequantGemvI4*). */
+int lp_dequant_gemv_i4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                       int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                       float *y, int64_t y_len, lp_stream_t stream);
+
+/* dequantGemvF4: packed MXFP4 e2m1 codes with fp32 (E8M0-valued) scales.
+ * Replaces simd/dequant.nim:341-420 (proc dequantGemvF4*). */
+int lp_dequant_gemv_f4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                       int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                       float *y, int64_t y_len, lp_stream_t stream);
+
+/* dequantGemvQ8_0: ggml Q8_0 weight blocks, M x blocksPerRow.
+ * Replaces simd/dequant.nim:530-568 (proc dequantGemvQ8_0*). */
+int lp_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
+                         int64_t x_len, float *y, int64_t y_len, lp_stream_t stream);
+
+/* dequantGemvQ4_0: ggml Q4_0 weight blocks, M x blocksPerRow.
+ * Replaces simd/dequant.nim:570-622 (proc dequantGemvQ4_0*). */
+int lp_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
+                         int64_t x_len, float *y, int64_t y_len, lp_stream_t stream);
+
+/* ======================= int8-activation GEMVs (bit-exact) ============ */
+
+/* dequantGemvQ8: int8 weights and int8 activations, exact int32 group sums.
+ * Replaces simd/dequant.nim:753-878 (proc dequantGemvQ8*). */
+int lp_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                       int64_t w_scales_len, int64_t group_size, const int8_t *xq, int64_t xq_len,
+                       const float *x_scales, int64_t x_scales_len, float *y, int64_t y_len,
+                       lp_stream_t stream);
+
+/* dequantGemvI4Q8: packed int4 weights, int8 activations.
+ * Replaces simd/dequant.nim:968-1145 (proc dequantGemvI4Q8*). */
+int lp_dequant_gemv_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                         int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                         int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
+                         int64_t y_len, lp_stream_t stream);
+
+/* dequantGemvQ8_0Q8: Q8_0 weight blocks x Q8_0 activation blocks.
+ * Replaces simd/dequant.nim:1187-1286 (proc dequantGemvQ8_0Q8*). */
+int lp_dequant_gemv_q8_0q8(const void *w, int64_t w_len, int64_t blocks_per_row, const void *xq,
+                           int64_t xq_len, float *y, int64_t y_len, lp_stream_t stream);
+
+/* dequantGemvQ4_0Q8: Q4_0 weight blocks x Q8_0 activation blocks.
+ * Replaces simd/dequant.nim:1288-1365 (proc dequantGemvQ4_0Q8*). */
+int lp_dequant_gemv_q4_0q8(const void *w, int64_t w_len, int64_t blocks_per_row, const void *xq,
+                           int64_t xq_len, float *y, int64_t y_len, lp_stream_t stream);
+
+/* ======================= multi-column GEMM (bit-exact) ================= */
+
+/* dequantGemmQ8: xq is K x n column-major, x_scales n x gpr, y M x n
+ * row-major.  Replaces simd/dequant.nim:1382-1458 (proc dequantGemmQ8*). */
+int lp_dequant_gemm_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                       int64_t w_scales_len, int64_t group_size, const int8_t *xq, int64_t xq_len,
+                       const float *x_scales, int64_t x_scales_len, int64_t n, float *y,
+                       int64_t y_len, lp_stream_t stream);
+
+/* dequantGemmI4Q8: the same over packed int4 weights.
+ * Replaces simd/dequant.nim:1460-1583 (proc dequantGemmI4Q8*). */
+int lp_dequant_gemm_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                         int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                         int64_t xq_len, const float *x_scales, int64_t x_scales_len, int64_t n,
+                         float *y, int64_t y_len, lp_stream_t stream);
+
+/* ======================= encoders (bit-exact) ========================== */
+
+/* quantizeQ8_0Batch: fp32 -> Q8_0 blocks (d = amax/127 as fp16, ties-away
+ * round, clamp +-127).  Replaces simd/dequant.nim:1624-1641 (= quantizeQ8_0,
+ * ggml.nim:60-75). */
+int lp_quantize_q8_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len,
+                           lp_stream_t stream);
+
+/* quantizeQ4_0Batch: fp32 -> Q4_0 blocks (sign-keeping max, d = max/-8).
+ * Replaces simd/dequant.nim:1643-1715 (= quantizeQ4_0, ggml.nim:77-97). */
+int lp_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len,
+                           lp_stream_t stream);
+
+/* quantizeQ8_0 with the block split into the two arrays the group-scale
+ * int8 kernels take: qs (src_len int8) and d (src_len/32 floats, each the
+ * fp32 value of the block's fp16 scale).  Same arithmetic as ggml.nim:60-75;
+ * the split is the layout change dequantGemvQ8 needs (its xq / xScales). */
+int lp_quantize_q8_0_split(const float *src, int64_t src_len, int8_t *qs, int64_t qs_len,
+                           float *d, int64_t d_len, lp_stream_t stream);
+
+/* quantizeBatch: symmetric int8 encode q = toI8(x / scale) (divide, ties-away,
+ * clamp [-128,127]); group_size <= 0 means one per-tensor scale.
+ * Replaces simd/dequant.nim:1717-1750 (= quantize[I8], quant.nim:48-60). */
+int lp_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
+                      int64_t group_size, int8_t *dst, int64_t dst_len, lp_stream_t stream);
+
+/* calibrateSymmetric: scale = absmax/qmax per group (1.0 for a zero group,
+ * ragged last group, group_size <= 0 = per tensor).
+ * Replaces quant.nim:95-110 (proc calibrateSymmetric*). */
+int lp_calibrate_symmetric(const float *x, int64_t x_len, int64_t group_size, float qmax,
+                           float *scales, int64_t scales_len, lp_stream_t stream);
+
+/* calibrateMX: E8M0-valued fp32 scale 2^clamp(floor(log2 amax) - emax, +-127)
+ * per block, 1.0 for a zero block.  Replaces quant.nim:125-137. */
+int lp_calibrate_mx(const float *x, int64_t x_len, int64_t block_size, int32_t elem_emax,
+                    float *scales, int64_t scales_len, lp_stream_t stream);
+
+/* quantize[I4] + packInt4: q = toI4(x/scale + 0), two per byte, low nibble =
+ * even index.  Replaces quant.nim:48-60 with intx.nim:50-51 and :83-94.
+ * x_len must be even. */
+int lp_quantize_i4_packed(const float *x, int64_t x_len, const float *scales,
+                          int64_t scales_len, int64_t group_size, uint8_t *packed,
+                          int64_t packed_len, lp_stream_t stream);
+
+/* quantize[F4E2M1] + packF4: code = toF4E2M1(x/scale + 0), two per byte.
+ * Replaces quant.nim:48-60 with mxfloat.nim:52-66 and :138-149. */
+int lp_quantize_f4_packed(const float *x, int64_t x_len, const float *scales,
+                          int64_t scales_len, int64_t block_size, uint8_t *packed,
+                          int64_t packed_len, lp_stream_t stream);
+
+/* dequantizeQ8_0Batch / dequantizeQ4_0Batch: blocks -> fp32.
+ * Replace simd/dequant.nim:446-485 and :487-526 (= ggml.nim:36-56). */
+int lp_dequantize_q8_0_batch(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
+                             lp_stream_t stream);
+int lp_dequantize_q4_0_batch(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
+                             lp_stream_t stream);
+
+/* ======================= host-pointer drop-in forms ==================== */
+/* Same arguments and meaning as the lp_* forms above, HOST pointers, no
+ * stream; blocking. */
+int lph_dequant_gemv(const int8_t *wq, int64_t wq_len, const float *scales, int64_t scales_len,
+                     int64_t group_size, const float *x, int64_t x_len, float *y, int64_t y_len);
+int lph_dequant_gemv_i4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                        int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                        float *y, int64_t y_len);
+int lph_dequant_gemv_f4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                        int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                        float *y, int64_t y_len);
+int lph_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
+                          int64_t x_len, float *y, int64_t y_len);
+int lph_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
+                          int64_t x_len, float *y, int64_t y_len);
+int lph_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                        int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                        int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
+                        int64_t y_len);
+int lph_dequant_gemv_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                          int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                          int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
+                          int64_t y_len);
+int lph_dequant_gemv_q8_0q8(const void *w, int64_t w_len, int64_t blocks_per_row, const void *xq,
+                            int64_t xq_len, float *y, int64_t y_len);
+int lph_dequant_gemv_q4_0q8(const void *w, int64_t w_len, int64_t blocks_per_row, const void *xq,
+                            int64_t xq_len, float *y, int64_t y_len);
+int lph_dequant_gemm_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                        int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                        int64_t xq_len, const float *x_scales, int64_t x_scales_len, int64_t n,
+                        float *y, int64_t y_len);
+int lph_dequant_gemm_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                          int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                          int64_t xq_len, const float *x_scales, int64_t x_scales_len, int64_t n,
+                          float *y, int64_t y_len);
+int lph_quantize_q8_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len);
+int lph_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len);
+int lph_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
+                       int64_t group_size, int8_t *dst, int64_t dst_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOWPREC_CUDA_H */

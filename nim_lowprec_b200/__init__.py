@@ -1,0 +1,20 @@
+"""nim_lowprec_b200 -- B200 (sm_100a) implementation of nim-lowprec's fused
+dequant-GEMV/GEMM hot path behind the reference's own kernel API.
+
+The kernels live in liblowprec_cuda.so (built from csrc/ by
+``python -m nim_lowprec_b200.build``); this package binds its C ABI and
+mirrors the reference's Nim procs.  There is no CPU fallback: importing the
+API without the built library raises.
+"""
+from . import _native
+from .dequant import (  # noqa: F401
+    calibrateMX, calibrateSymmetric, dequantGemmI4Q8, dequantGemmQ8, dequantGemv,
+    dequantGemvF4, dequantGemvI4, dequantGemvI4Q8, dequantGemvQ4_0, dequantGemvQ4_0Q8,
+    dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantizeQ4_0Batch,
+    dequantizeQ8_0Batch, quantizeBatch, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0,
+    quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split)
+from .ggml import QK, BlockQ4_0, BlockQ8_0  # noqa: F401
+
+_native.lib()  # fail loudly at import if the CUDA library is missing
+
+__version__ = "0.1.0"

@@ -1,0 +1,129 @@
+"""ctypes binding of liblowprec_cuda.so (the C ABI in include/lowprec_cuda.h).
+
+Loading fails loudly: there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblowprec_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "lowprec_cuda.h")
+
+LP_OK = 0
+LP_ERR_SHAPE = 1
+LP_ERR_ARG = 2
+LP_ERR_CUDA = 3
+LP_ERR_NCCL = 4
+LP_ERR_TIMEOUT = 5
+LP_ERR_UNSUPPORTED = 6
+LP_ERR_NO_DEVICE = 7
+
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+_f32 = ctypes.c_float
+
+# argument kinds by C type, for the prototype table below
+_CT = {"p": _vp, "n": _i64, "f": _f32, "i": _i32}
+
+# name -> argument signature (p = pointer, n = int64, f = float, i = int32)
+SIGNATURES = {
+    "lp_dequant_gemv": "pnpnnpnpnp",
+    "lp_dequant_gemv_i4": "pnpnnpnpnp",
+    "lp_dequant_gemv_f4": "pnpnnpnpnp",
+    "lp_dequant_gemv_q8_0": "pnnpnpnp",
+    "lp_dequant_gemv_q4_0": "pnnpnpnp",
+    "lp_dequant_gemv_q8": "pnpnnpnpnpnp",
+    "lp_dequant_gemv_i4q8": "pnpnnpnpnpnp",
+    "lp_dequant_gemv_q8_0q8": "pnnpnpnp",
+    "lp_dequant_gemv_q4_0q8": "pnnpnpnp",
+    "lp_dequant_gemm_q8": "pnpnnpnpnnpnp",
+    "lp_dequant_gemm_i4q8": "pnpnnpnpnnpnp",
+    "lp_quantize_q8_0_batch": "pnpnp",
+    "lp_quantize_q4_0_batch": "pnpnp",
+    "lp_quantize_q8_0_split": "pnpnpnp",
+    "lp_quantize_batch": "pnpnnpnp",
+    "lp_calibrate_symmetric": "pnnfpnp",
+    "lp_calibrate_mx": "pnnipnp",
+    "lp_quantize_i4_packed": "pnpnnpnp",
+    "lp_quantize_f4_packed": "pnpnnpnp",
+    "lp_dequantize_q8_0_batch": "pnpnp",
+    "lp_dequantize_q4_0_batch": "pnpnp",
+    "lph_dequant_gemv": "pnpnnpnpn",
+    "lph_dequant_gemv_i4": "pnpnnpnpn",
+    "lph_dequant_gemv_f4": "pnpnnpnpn",
+    "lph_dequant_gemv_q8_0": "pnnpnpn",
+    "lph_dequant_gemv_q4_0": "pnnpnpn",
+    "lph_dequant_gemv_q8": "pnpnnpnpnpn",
+    "lph_dequant_gemv_i4q8": "pnpnnpnpnpn",
+    "lph_dequant_gemv_q8_0q8": "pnnpnpn",
+    "lph_dequant_gemv_q4_0q8": "pnnpnpn",
+    "lph_dequant_gemm_q8": "pnpnnpnpnnpn",
+    "lph_dequant_gemm_i4q8": "pnpnnpnpnnpn",
+    "lph_quantize_q8_0_batch": "pnpn",
+    "lph_quantize_q4_0_batch": "pnpn",
+    "lph_quantize_batch": "pnpnnpn",
+}
+
+
+def header_symbols(path: str = HEADER):
+    """Every function the public header declares (for export checks)."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(lph?_[a-z0-9_]+)\s*\(", text)))
+
+
+class NativeError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        super().__init__(f"{where}: {status_string(status)} (status {status})")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load liblowprec_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m nim_lowprec_b200.build` "
+                "(this package has no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, sig in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [_CT[c] for c in sig]
+        L.lp_version.restype = ctypes.c_int
+        L.lp_version.argtypes = []
+        L.lp_status_string.restype = ctypes.c_char_p
+        L.lp_status_string.argtypes = [ctypes.c_int]
+        L.lp_device_error.restype = ctypes.c_int
+        L.lp_device_error.argtypes = []
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return lib().lp_status_string(int(status)).decode()
+    except Exception:  # pragma: no cover
+        return f"status {status}"
+
+
+def check(status: int, where: str) -> None:
+    if status == LP_OK:
+        return
+    if status == LP_ERR_SHAPE:
+        # the reference asserts its shape preconditions (AssertionDefect)
+        raise AssertionError(f"{where}: {status_string(status)}")
+    raise NativeError(status, where)
+
+
+def device_error() -> int:
+    """Synchronise, then return and clear the first device-side error code."""
+    return int(lib().lp_device_error())

@@ -1,0 +1,561 @@
+// capi.cu -- the extern "C" boundary (include/lowprec_cuda.h).
+//
+// Shape rules follow the reference procs' entry asserts: m = y.len,
+// k = x.len, gpr = k div groupSize, and the listed length equalities
+// (e.g. simd/dequant.nim:221-226, 768-771, 1392-1400).  A failed rule
+// returns LP_ERR_SHAPE before anything is launched.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "gemv.cuh"
+#include "lp_internal.h"
+
+namespace lp {
+
+const DeviceInfo& device_info() {
+  static DeviceInfo info[kMaxDevices];
+  static std::once_flag once[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = dev % kMaxDevices;
+  std::call_once(once[slot], [&] {
+    DeviceInfo& d = info[slot];
+    d.ordinal = dev;
+    cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+  });
+  return info[slot];
+}
+
+}  // namespace lp
+
+using lp::GemvParams;
+
+namespace {
+
+#define LP_REQUIRE(cond)          \
+  do {                            \
+    if (!(cond)) return LP_ERR_SHAPE; \
+  } while (0)
+
+// Set by the host-staging forms: run an entry point's shape and argument
+// checks only, so a bad call fails before any device work or allocation.
+thread_local bool t_validate_only = false;
+
+#define LP_VALIDATED()                   \
+  do {                                   \
+    if (t_validate_only) return LP_OK;   \
+  } while (0)
+
+inline cudaStream_t S(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
+
+GemvParams base(const void* w, const float* ws, const void* x, const float* xs, float* y,
+                int64_t m, int64_t k, int64_t gs, int64_t gpr, int64_t row_bytes) {
+  GemvParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.w = static_cast<const uint8_t*>(w);
+  p.ws = ws;
+  p.x = x;
+  p.xs = xs;
+  p.y = y;
+  p.m = static_cast<int>(m);
+  p.k = static_cast<int>(k);
+  p.gs = static_cast<int>(gs);
+  p.gpr = static_cast<int>(gpr);
+  p.row_bytes = static_cast<int>(row_bytes);
+  return p;
+}
+
+constexpr int64_t kIntMax = 0x7fffffff;
+
+bool fits(int64_t m, int64_t k) { return m >= 0 && k >= 0 && m <= kIntMax && k <= kIntMax; }
+
+}  // namespace
+
+extern "C" {
+
+int lp_version(void) { return 100; }
+
+const char* lp_status_string(int s) {
+  switch (s) {
+    case LP_OK: return "ok";
+    case LP_ERR_SHAPE: return "shape precondition failed";
+    case LP_ERR_ARG: return "invalid argument";
+    case LP_ERR_CUDA: return "CUDA error";
+    case LP_ERR_NCCL: return "collective error";
+    case LP_ERR_TIMEOUT: return "device-side wait timed out";
+    case LP_ERR_UNSUPPORTED: return "shape not supported by this build";
+    case LP_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+int lp_device_error(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return LP_ERR_CUDA;
+  const unsigned int e = lp::take_error_gemv();
+  return static_cast<int>(e);
+}
+
+// ------------------------------------------------ fp32-activation GEMVs
+
+static int gemv_f32_group(int fmt, const void* w, int64_t w_len, const float* scales,
+                          int64_t scales_len, int64_t gs, const float* x, int64_t x_len, float* y,
+                          int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len, k = x_len;
+  LP_REQUIRE(gs > 0 && fits(m, k));
+  const int64_t gpr = k / gs;
+  const bool packed = fmt != 0;
+  const int64_t rb = packed ? k / 2 : k;
+  LP_REQUIRE(k % gs == 0);
+  if (packed) LP_REQUIRE(k % 2 == 0);
+  LP_REQUIRE(w_len == m * rb && scales_len == m * gpr);
+  if (m && (!w || !y || (k && (!x || !scales)))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  GemvParams p = base(w, scales, x, nullptr, y, m, k, gs, gpr, rb);
+  switch (fmt) {
+    case 0: return lp::launch_gemv<lp::FmtI8>(p, S(st));
+    case 1: return lp::launch_gemv<lp::FmtI4>(p, S(st));
+    default: return lp::launch_gemv<lp::FmtF4>(p, S(st));
+  }
+}
+
+int lp_dequant_gemv(const int8_t* wq, int64_t wq_len, const float* scales, int64_t scales_len,
+                    int64_t group_size, const float* x, int64_t x_len, float* y, int64_t y_len,
+                    lp_stream_t stream) {
+  return gemv_f32_group(0, wq, wq_len, scales, scales_len, group_size, x, x_len, y, y_len, stream);
+}
+int lp_dequant_gemv_i4(const uint8_t* wp, int64_t wp_len, const float* scales, int64_t scales_len,
+                       int64_t group_size, const float* x, int64_t x_len, float* y, int64_t y_len,
+                       lp_stream_t stream) {
+  return gemv_f32_group(1, wp, wp_len, scales, scales_len, group_size, x, x_len, y, y_len, stream);
+}
+int lp_dequant_gemv_f4(const uint8_t* wp, int64_t wp_len, const float* scales, int64_t scales_len,
+                       int64_t group_size, const float* x, int64_t x_len, float* y, int64_t y_len,
+                       lp_stream_t stream) {
+  return gemv_f32_group(2, wp, wp_len, scales, scales_len, group_size, x, x_len, y, y_len, stream);
+}
+
+static int gemv_f32_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, const float* x,
+                           int64_t x_len, float* y, int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len;
+  LP_REQUIRE(bpr >= 0 && fits(m, bpr * 32));
+  LP_REQUIRE(w_len == m * bpr && x_len == bpr * 32);
+  if (m && (!w || !y || (bpr && !x))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  const int64_t rb = bpr * (q4 ? 18 : 34);
+  GemvParams p = base(w, nullptr, x, nullptr, y, m, bpr * 32, 32, bpr, rb);
+  return q4 ? lp::launch_gemv<lp::FmtQ4_0>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0>(p, S(st));
+}
+
+int lp_dequant_gemv_q8_0(const void* w, int64_t w_len, int64_t bpr, const float* x, int64_t x_len,
+                         float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_f32_blocks(0, w, w_len, bpr, x, x_len, y, y_len, stream);
+}
+int lp_dequant_gemv_q4_0(const void* w, int64_t w_len, int64_t bpr, const float* x, int64_t x_len,
+                         float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_f32_blocks(1, w, w_len, bpr, x, x_len, y, y_len, stream);
+}
+
+// ------------------------------------------------ int8-activation GEMVs
+
+static int gemv_q8_group(int i4, const void* w, int64_t w_len, const float* ws, int64_t ws_len,
+                         int64_t gs, const int8_t* xq, int64_t xq_len, const float* xs,
+                         int64_t xs_len, float* y, int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len, k = xq_len;
+  LP_REQUIRE(gs > 0 && fits(m, k));
+  const int64_t gpr = k / gs;
+  const int64_t rb = i4 ? k / 2 : k;
+  LP_REQUIRE(k % gs == 0);
+  if (i4) LP_REQUIRE(k % 2 == 0);
+  LP_REQUIRE(w_len == m * rb && ws_len == m * gpr && xs_len == gpr);
+  if (m && (!w || !y || (k && (!xq || !ws || !xs)))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  GemvParams p = base(w, ws, xq, xs, y, m, k, gs, gpr, rb);
+  return i4 ? lp::launch_gemv<lp::FmtI4Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8>(p, S(st));
+}
+
+int lp_dequant_gemv_q8(const int8_t* wq, int64_t wq_len, const float* w_scales,
+                       int64_t w_scales_len, int64_t group_size, const int8_t* xq, int64_t xq_len,
+                       const float* x_scales, int64_t x_scales_len, float* y, int64_t y_len,
+                       lp_stream_t stream) {
+  return gemv_q8_group(0, wq, wq_len, w_scales, w_scales_len, group_size, xq, xq_len, x_scales,
+                       x_scales_len, y, y_len, stream);
+}
+int lp_dequant_gemv_i4q8(const uint8_t* wp, int64_t wp_len, const float* w_scales,
+                         int64_t w_scales_len, int64_t group_size, const int8_t* xq,
+                         int64_t xq_len, const float* x_scales, int64_t x_scales_len, float* y,
+                         int64_t y_len, lp_stream_t stream) {
+  return gemv_q8_group(1, wp, wp_len, w_scales, w_scales_len, group_size, xq, xq_len, x_scales,
+                       x_scales_len, y, y_len, stream);
+}
+
+static int gemv_q8_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, const void* xq,
+                          int64_t xq_len, float* y, int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len;
+  LP_REQUIRE(bpr >= 0 && fits(m, bpr * 32));
+  LP_REQUIRE(w_len == m * bpr && xq_len == bpr);
+  if (m && (!w || !y || (bpr && !xq))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  const int64_t rb = bpr * (q4 ? 18 : 34);
+  GemvParams p = base(w, nullptr, xq, nullptr, y, m, bpr * 32, 32, bpr, rb);
+  return q4 ? lp::launch_gemv<lp::FmtQ4_0Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0Q8>(p, S(st));
+}
+
+int lp_dequant_gemv_q8_0q8(const void* w, int64_t w_len, int64_t bpr, const void* xq,
+                           int64_t xq_len, float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_q8_blocks(0, w, w_len, bpr, xq, xq_len, y, y_len, stream);
+}
+int lp_dequant_gemv_q4_0q8(const void* w, int64_t w_len, int64_t bpr, const void* xq,
+                           int64_t xq_len, float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_q8_blocks(1, w, w_len, bpr, xq, xq_len, y, y_len, stream);
+}
+
+// ------------------------------------------------------------------ GEMM
+
+static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, int64_t ws_len,
+                       int64_t gs, const int8_t* xq, int64_t xq_len, const float* xs,
+                       int64_t xs_len, int64_t n, float* y, int64_t y_len, lp_stream_t st) {
+  LP_REQUIRE(n > 0 && gs > 0);
+  const int64_t m = y_len / n, k = xq_len / n;
+  LP_REQUIRE(fits(m, k) && fits(n, n));
+  const int64_t gpr = k / gs;
+  const int64_t rb = i4 ? k / 2 : k;
+  LP_REQUIRE(k % gs == 0);
+  if (i4) LP_REQUIRE(k % 2 == 0);
+  LP_REQUIRE(w_len == m * rb && ws_len == m * gpr && xq_len == n * k && xs_len == n * gpr &&
+             y_len == m * n);
+  if (m && (!w || !y || (k && (!xq || !ws || !xs)))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_gemm(static_cast<const uint8_t*>(w), i4, ws, gs, xq, xs, n, y, m, k, S(st));
+}
+
+int lp_dequant_gemm_q8(const int8_t* wq, int64_t wq_len, const float* w_scales,
+                       int64_t w_scales_len, int64_t group_size, const int8_t* xq, int64_t xq_len,
+                       const float* x_scales, int64_t x_scales_len, int64_t n, float* y,
+                       int64_t y_len, lp_stream_t stream) {
+  return gemm_common(0, wq, wq_len, w_scales, w_scales_len, group_size, xq, xq_len, x_scales,
+                     x_scales_len, n, y, y_len, stream);
+}
+int lp_dequant_gemm_i4q8(const uint8_t* wp, int64_t wp_len, const float* w_scales,
+                         int64_t w_scales_len, int64_t group_size, const int8_t* xq,
+                         int64_t xq_len, const float* x_scales, int64_t x_scales_len, int64_t n,
+                         float* y, int64_t y_len, lp_stream_t stream) {
+  return gemm_common(1, wp, wp_len, w_scales, w_scales_len, group_size, xq, xq_len, x_scales,
+                     x_scales_len, n, y, y_len, stream);
+}
+
+// -------------------------------------------------------------- encoders
+
+int lp_quantize_q8_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len,
+                           lp_stream_t stream) {
+  LP_REQUIRE(src_len >= 0 && src_len == blocks_len * 32);
+  if (src_len && (!src || !blocks)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_q8_0(src, src_len, static_cast<uint8_t*>(blocks), nullptr, nullptr,
+                                  S(stream));
+}
+
+int lp_quantize_q4_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len,
+                           lp_stream_t stream) {
+  LP_REQUIRE(src_len >= 0 && src_len == blocks_len * 32);
+  if (src_len && (!src || !blocks)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_q4_0(src, src_len, static_cast<uint8_t*>(blocks), S(stream));
+}
+
+int lp_quantize_q8_0_split(const float* src, int64_t src_len, int8_t* qs, int64_t qs_len,
+                           float* d, int64_t d_len, lp_stream_t stream) {
+  LP_REQUIRE(src_len >= 0 && src_len % 32 == 0 && qs_len == src_len && d_len == src_len / 32);
+  if (src_len && (!src || !qs || !d)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_q8_0(src, src_len, nullptr, qs, d, S(stream));
+}
+
+static int64_t num_groups(int64_t n, int64_t gs) { return gs > 0 ? (n + gs - 1) / gs : 1; }
+
+int lp_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
+                      int64_t group_size, int8_t* dst, int64_t dst_len, lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0 && x_len == dst_len);
+  LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, group_size) : 0));
+  if (x_len && (!x || !scales || !dst)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_batch(x, x_len, scales, group_size > 0 ? group_size : 0, dst,
+                                   S(stream));
+}
+
+int lp_calibrate_symmetric(const float* x, int64_t x_len, int64_t group_size, float qmax,
+                           float* scales, int64_t scales_len, lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0);
+  const int64_t gs = group_size > 0 ? group_size : std::max<int64_t>(x_len, 1);
+  LP_REQUIRE(scales_len == num_groups(x_len, gs) || (group_size <= 0 && scales_len == 1));
+  if (scales_len && (!scales || (x_len && !x))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_calibrate(x, x_len, gs, qmax, 0, 0, scales, scales_len, S(stream));
+}
+
+int lp_calibrate_mx(const float* x, int64_t x_len, int64_t block_size, int32_t elem_emax,
+                    float* scales, int64_t scales_len, lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0 && block_size > 0 && scales_len == num_groups(x_len, block_size));
+  if (scales_len && (!scales || (x_len && !x))) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_calibrate(x, x_len, block_size, 0.0f, elem_emax, 1, scales, scales_len,
+                              S(stream));
+}
+
+int lp_quantize_i4_packed(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
+                          int64_t group_size, uint8_t* packed, int64_t packed_len,
+                          lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0 && packed_len == (x_len + 1) / 2);
+  LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, group_size) : 0));
+  if (x_len && (!x || !scales || !packed)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_packed(x, x_len, scales, group_size > 0 ? group_size : 0, 0, packed,
+                                    S(stream));
+}
+
+int lp_quantize_f4_packed(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
+                          int64_t block_size, uint8_t* packed, int64_t packed_len,
+                          lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0 && packed_len == (x_len + 1) / 2);
+  LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, block_size) : 0));
+  if (x_len && (!x || !scales || !packed)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_packed(x, x_len, scales, block_size > 0 ? block_size : 0, 1, packed,
+                                    S(stream));
+}
+
+int lp_dequantize_q8_0_batch(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
+                             lp_stream_t stream) {
+  LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 32);
+  if (blocks_len && (!blocks || !dst)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_blocks(static_cast<const uint8_t*>(blocks), blocks_len, 0, dst,
+                                      S(stream));
+}
+
+int lp_dequantize_q4_0_batch(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
+                             lp_stream_t stream) {
+  LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 32);
+  if (blocks_len && (!blocks || !dst)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_blocks(static_cast<const uint8_t*>(blocks), blocks_len, 1, dst,
+                                      S(stream));
+}
+
+}  // extern "C"
+
+// ================================================== host-staging forms ==
+namespace {
+
+// One per calling thread: a device workspace grown on demand, reused across
+// calls, and a private stream.
+struct HostStage {
+  int device = -1;
+  void* buf = nullptr;
+  size_t cap = 0;
+  cudaStream_t stream = nullptr;
+  ~HostStage() {
+    if (buf) cudaFree(buf);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+thread_local HostStage t_stage;
+
+struct Seg {
+  const void* host;  // input to copy in (nullptr for outputs)
+  size_t bytes;
+  void* dev = nullptr;
+};
+
+// Lays the segments out in the workspace (256-byte aligned), copies inputs.
+int stage_in(std::vector<Seg*> segs) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return LP_ERR_NO_DEVICE;
+  HostStage& hs = t_stage;
+  if (hs.device != dev) {
+    if (hs.buf) cudaFree(hs.buf);
+    if (hs.stream) cudaStreamDestroy(hs.stream);
+    hs.buf = nullptr;
+    hs.cap = 0;
+    hs.stream = nullptr;
+    hs.device = dev;
+    if (cudaStreamCreateWithFlags(&hs.stream, cudaStreamNonBlocking) != cudaSuccess)
+      return LP_ERR_CUDA;
+  }
+  size_t total = 0;
+  for (Seg* s : segs) total += (s->bytes + 255) & ~size_t(255);
+  if (total > hs.cap) {
+    if (hs.buf) cudaFree(hs.buf);
+    hs.buf = nullptr;
+    const size_t want = std::max(total, hs.cap * 2);
+    if (cudaMalloc(&hs.buf, want) != cudaSuccess) {
+      hs.cap = 0;
+      return LP_ERR_CUDA;
+    }
+    hs.cap = want;
+  }
+  size_t off = 0;
+  for (Seg* s : segs) {
+    s->dev = static_cast<uint8_t*>(hs.buf) + off;
+    off += (s->bytes + 255) & ~size_t(255);
+    if (s->host && s->bytes &&
+        cudaMemcpyAsync(s->dev, s->host, s->bytes, cudaMemcpyHostToDevice, hs.stream) != cudaSuccess)
+      return LP_ERR_CUDA;
+  }
+  return LP_OK;
+}
+
+int stage_out(void* host, const Seg& s, int status) {
+  HostStage& hs = t_stage;
+  if (status == LP_OK && s.bytes &&
+      cudaMemcpyAsync(host, s.dev, s.bytes, cudaMemcpyDeviceToHost, hs.stream) != cudaSuccess)
+    status = LP_ERR_CUDA;
+  if (cudaStreamSynchronize(hs.stream) != cudaSuccess && status == LP_OK) status = LP_ERR_CUDA;
+  return status;
+}
+
+template <class T>
+size_t nb(int64_t len) {
+  return len > 0 ? static_cast<size_t>(len) * sizeof(T) : 0;
+}
+
+}  // namespace
+
+// Runs `call` with the validate-only switch set; returns its status.
+#define LPH_PRECHECK(call)                 \
+  do {                                     \
+    t_validate_only = true;                \
+    const int pre_ = (call);               \
+    t_validate_only = false;               \
+    if (pre_ != LP_OK) return pre_;        \
+  } while (0)
+
+extern "C" {
+
+#define LPH_GROUP_F32(NAME, DEVFN, WT)                                                           \
+  int NAME(const WT* w, int64_t w_len, const float* scales, int64_t scales_len, int64_t gs,      \
+           const float* x, int64_t x_len, float* y, int64_t y_len) {                             \
+    Seg sw{w, nb<WT>(w_len)}, ss{scales, nb<float>(scales_len)}, sx{x, nb<float>(x_len)},        \
+        sy{nullptr, nb<float>(y_len)};                                                            \
+    LPH_PRECHECK(DEVFN(w, w_len, scales, scales_len, gs, x, x_len, y, y_len, nullptr));          \
+    int st = stage_in({&sw, &ss, &sx, &sy});                                                     \
+    if (st != LP_OK) return st;                                                                   \
+    st = DEVFN(static_cast<const WT*>(sw.dev), w_len, static_cast<const float*>(ss.dev),         \
+               scales_len, gs, static_cast<const float*>(sx.dev), x_len,                         \
+               static_cast<float*>(sy.dev), y_len, t_stage.stream);                              \
+    return stage_out(y, sy, st);                                                                  \
+  }
+
+LPH_GROUP_F32(lph_dequant_gemv, lp_dequant_gemv, int8_t)
+LPH_GROUP_F32(lph_dequant_gemv_i4, lp_dequant_gemv_i4, uint8_t)
+LPH_GROUP_F32(lph_dequant_gemv_f4, lp_dequant_gemv_f4, uint8_t)
+
+#define LPH_BLOCKS_F32(NAME, DEVFN, BB)                                                          \
+  int NAME(const void* w, int64_t w_len, int64_t bpr, const float* x, int64_t x_len, float* y,   \
+           int64_t y_len) {                                                                      \
+    Seg sw{w, w_len > 0 ? static_cast<size_t>(w_len) * BB : 0}, sx{x, nb<float>(x_len)},         \
+        sy{nullptr, nb<float>(y_len)};                                                            \
+    LPH_PRECHECK(DEVFN(w, w_len, bpr, x, x_len, y, y_len, nullptr));                             \
+    int st = stage_in({&sw, &sx, &sy});                                                          \
+    if (st != LP_OK) return st;                                                                   \
+    st = DEVFN(sw.dev, w_len, bpr, static_cast<const float*>(sx.dev), x_len,                     \
+               static_cast<float*>(sy.dev), y_len, t_stage.stream);                              \
+    return stage_out(y, sy, st);                                                                  \
+  }
+
+LPH_BLOCKS_F32(lph_dequant_gemv_q8_0, lp_dequant_gemv_q8_0, 34)
+LPH_BLOCKS_F32(lph_dequant_gemv_q4_0, lp_dequant_gemv_q4_0, 18)
+
+#define LPH_GROUP_Q8(NAME, DEVFN, WT)                                                            \
+  int NAME(const WT* w, int64_t w_len, const float* ws, int64_t ws_len, int64_t gs,              \
+           const int8_t* xq, int64_t xq_len, const float* xs, int64_t xs_len, float* y,          \
+           int64_t y_len) {                                                                      \
+    Seg sw{w, nb<WT>(w_len)}, sws{ws, nb<float>(ws_len)}, sx{xq, nb<int8_t>(xq_len)},            \
+        sxs{xs, nb<float>(xs_len)}, sy{nullptr, nb<float>(y_len)};                                \
+    LPH_PRECHECK(DEVFN(w, w_len, ws, ws_len, gs, xq, xq_len, xs, xs_len, y, y_len, nullptr));    \
+    int st = stage_in({&sw, &sws, &sx, &sxs, &sy});                                              \
+    if (st != LP_OK) return st;                                                                   \
+    st = DEVFN(static_cast<const WT*>(sw.dev), w_len, static_cast<const float*>(sws.dev), ws_len, \
+               gs, static_cast<const int8_t*>(sx.dev), xq_len,                                   \
+               static_cast<const float*>(sxs.dev), xs_len, static_cast<float*>(sy.dev), y_len,   \
+               t_stage.stream);                                                                  \
+    return stage_out(y, sy, st);                                                                  \
+  }
+
+LPH_GROUP_Q8(lph_dequant_gemv_q8, lp_dequant_gemv_q8, int8_t)
+LPH_GROUP_Q8(lph_dequant_gemv_i4q8, lp_dequant_gemv_i4q8, uint8_t)
+
+#define LPH_BLOCKS_Q8(NAME, DEVFN, BB)                                                           \
+  int NAME(const void* w, int64_t w_len, int64_t bpr, const void* xq, int64_t xq_len, float* y,  \
+           int64_t y_len) {                                                                      \
+    Seg sw{w, w_len > 0 ? static_cast<size_t>(w_len) * BB : 0},                                  \
+        sx{xq, xq_len > 0 ? static_cast<size_t>(xq_len) * 34 : 0},                               \
+        sy{nullptr, nb<float>(y_len)};                                                            \
+    LPH_PRECHECK(DEVFN(w, w_len, bpr, xq, xq_len, y, y_len, nullptr));                           \
+    int st = stage_in({&sw, &sx, &sy});                                                          \
+    if (st != LP_OK) return st;                                                                   \
+    st = DEVFN(sw.dev, w_len, bpr, sx.dev, xq_len, static_cast<float*>(sy.dev), y_len,           \
+               t_stage.stream);                                                                  \
+    return stage_out(y, sy, st);                                                                  \
+  }
+
+LPH_BLOCKS_Q8(lph_dequant_gemv_q8_0q8, lp_dequant_gemv_q8_0q8, 34)
+LPH_BLOCKS_Q8(lph_dequant_gemv_q4_0q8, lp_dequant_gemv_q4_0q8, 18)
+
+#define LPH_GEMM(NAME, DEVFN, WT)                                                                \
+  int NAME(const WT* w, int64_t w_len, const float* ws, int64_t ws_len, int64_t gs,              \
+           const int8_t* xq, int64_t xq_len, const float* xs, int64_t xs_len, int64_t n,         \
+           float* y, int64_t y_len) {                                                            \
+    Seg sw{w, nb<WT>(w_len)}, sws{ws, nb<float>(ws_len)}, sx{xq, nb<int8_t>(xq_len)},            \
+        sxs{xs, nb<float>(xs_len)}, sy{nullptr, nb<float>(y_len)};                                \
+    LPH_PRECHECK(DEVFN(w, w_len, ws, ws_len, gs, xq, xq_len, xs, xs_len, n, y, y_len, nullptr)); \
+    int st = stage_in({&sw, &sws, &sx, &sxs, &sy});                                              \
+    if (st != LP_OK) return st;                                                                   \
+    st = DEVFN(static_cast<const WT*>(sw.dev), w_len, static_cast<const float*>(sws.dev), ws_len, \
+               gs, static_cast<const int8_t*>(sx.dev), xq_len,                                   \
+               static_cast<const float*>(sxs.dev), xs_len, n, static_cast<float*>(sy.dev),       \
+               y_len, t_stage.stream);                                                           \
+    return stage_out(y, sy, st);                                                                  \
+  }
+
+LPH_GEMM(lph_dequant_gemm_q8, lp_dequant_gemm_q8, int8_t)
+LPH_GEMM(lph_dequant_gemm_i4q8, lp_dequant_gemm_i4q8, uint8_t)
+
+int lph_quantize_q8_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len) {
+  Seg ss{src, nb<float>(src_len)}, sb{nullptr, blocks_len > 0 ? static_cast<size_t>(blocks_len) * 34 : 0};
+  LPH_PRECHECK(lp_quantize_q8_0_batch(src, src_len, blocks, blocks_len, nullptr));
+  int st = stage_in({&ss, &sb});
+  if (st != LP_OK) return st;
+  st = lp_quantize_q8_0_batch(static_cast<const float*>(ss.dev), src_len, sb.dev, blocks_len,
+                              t_stage.stream);
+  return stage_out(blocks, sb, st);
+}
+
+int lph_quantize_q4_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len) {
+  Seg ss{src, nb<float>(src_len)}, sb{nullptr, blocks_len > 0 ? static_cast<size_t>(blocks_len) * 18 : 0};
+  LPH_PRECHECK(lp_quantize_q4_0_batch(src, src_len, blocks, blocks_len, nullptr));
+  int st = stage_in({&ss, &sb});
+  if (st != LP_OK) return st;
+  st = lp_quantize_q4_0_batch(static_cast<const float*>(ss.dev), src_len, sb.dev, blocks_len,
+                              t_stage.stream);
+  return stage_out(blocks, sb, st);
+}
+
+int lph_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
+                       int64_t group_size, int8_t* dst, int64_t dst_len) {
+  Seg sx{x, nb<float>(x_len)}, ss{scales, nb<float>(scales_len)}, sd{nullptr, nb<int8_t>(dst_len)};
+  LPH_PRECHECK(lp_quantize_batch(x, x_len, scales, scales_len, group_size, dst, dst_len, nullptr));
+  int st = stage_in({&sx, &ss, &sd});
+  if (st != LP_OK) return st;
+  st = lp_quantize_batch(static_cast<const float*>(sx.dev), x_len,
+                         static_cast<const float*>(ss.dev), scales_len, group_size,
+                         static_cast<int8_t*>(sd.dev), dst_len, t_stage.stream);
+  return stage_out(dst, sd, st);
+}
+
+}  // extern "C"

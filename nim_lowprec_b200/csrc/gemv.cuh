@@ -1,0 +1,232 @@
+// gemv.cuh -- the fused dequant-GEMV skeleton for sm_100a.
+//
+// Every GEMV of nim-lowprec has the same shape: output row m is an ordered
+// fold over the row's groups (blocks) g of a per-group term,
+//     y[m] = fold_g term(m, g)
+// where term(m, g) needs only group g of row m plus the activations of group g:
+//   fp32 activations  term = (sequential fp32 sum over the group of w*x) * s
+//                     (simd/dequant.nim:253-256, 329-338, 410-419, 564-567,
+//                      616-621)
+//   int8 activations  term = (f32(exact int32 group dot) * ws) * xs
+//                     (applyScales, simd/dequant.nim:654-657)
+//   ggml int8 acts    term = f32(isum) * (wd * xd), folded into 4 lanes by
+//                     block index mod 4 (simd/dequant.nim:1275-1286)
+// and the fold is either serial from 0.0 or that 4-lane discipline.  Terms
+// parallelise freely; the fold must keep its order to stay bit-exact, so the
+// kernel splits the two:
+//
+//   warp 0   producer: streams tiles of RT consecutive weight rows (and their
+//            scale rows) HBM -> shared memory with 1-D bulk copies (TMA),
+//            `stages` deep, mbarrier-tracked.  Rows are contiguous in HBM, so
+//            a tile is one bulk copy.  Shapes whose rows are not 16-byte
+//            multiples take a plain-load staging path instead.
+//   warps 2+ consumers: compute every (row, group) term of a tile into a
+//            double-buffered term matrix in shared memory; two rows sharing a
+//            group run as one packed f32x2 chain on the fp32 paths.
+//   warp 1   folder: lane r folds row r of a finished tile in group order
+//            and writes y.  It overlaps the consumers' next tile.
+//
+// Each CTA owns a contiguous, balanced range of rows (persistent grid of
+// one CTA per SM), so its weight bytes are one contiguous HBM stream.
+#pragma once
+#include "lp_device.cuh"
+
+namespace lp {
+
+enum class Fold { Serial, Lanes4 };
+
+struct GemvParams {
+  const uint8_t* w;   // weight rows, row_bytes each
+  const float* ws;    // per-row group scales (M x gpr) or nullptr
+  const void* x;      // activations (format-specific)
+  const float* xs;    // activation group scales or nullptr
+  float* y;
+  int m, k, gs, gpr;  // gpr: groups (ggml: blocks) per row
+  int row_bytes;
+  int rt;             // rows per tile
+  int stages;
+  int bulk;           // 1: bulk-copy staging, 0: plain loads
+  int tstride;        // floats per term-matrix row
+  int x_bytes;        // shared bytes for the staged activations
+  int off_w, off_s, off_t, off_b;  // shared-memory offsets
+  int stage_w_bytes, stage_s_bytes;
+};
+
+constexpr int kMaxRt = 16;
+
+// ------------------------------------------------------------ x staging
+// Cooperative copy of `bytes` bytes global -> shared (byte loop; activations
+// are tiny next to the weights and are staged once per CTA).
+__device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, int bytes, int tid,
+                                           int nthr) {
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+    const int n16 = bytes >> 4;
+    for (int i = tid; i < n16; i += nthr)
+      reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    for (int i = (n16 << 4) + tid; i < bytes; i += nthr) dst[i] = src[i];
+  } else {
+    for (int i = tid; i < bytes; i += nthr) dst[i] = src[i];
+  }
+}
+
+// ----------------------------------------------------------- the kernel
+template <class Fmt, int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ volatile int s_abort;
+  uint8_t* xsm = smem;
+  uint8_t* stw = smem + p.off_w;
+  uint8_t* sts = smem + p.off_s;
+  float* terms = reinterpret_cast<float*>(smem + p.off_t);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_b);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + p.stages;
+  uint64_t* tfull = bars + 2 * p.stages;
+  uint64_t* tempty = tfull + 2;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row_begin = static_cast<int>((static_cast<int64_t>(p.m) * blockIdx.x) / gridDim.x);
+  const int row_end = static_cast<int>((static_cast<int64_t>(p.m) * (blockIdx.x + 1)) / gridDim.x);
+  const int nrows = row_end - row_begin;
+  const int ntiles = (nrows + p.rt - 1) / p.rt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], NCW);
+      mbar_init(&tempty[b], 1);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  Fmt::stage_x(xsm, p, threadIdx.x, blockDim.x);
+  __syncthreads();
+  if (ntiles == 0) return;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first();
+    int issued = 0;
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % p.stages;
+      if (t >= p.stages) {
+        if (!mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, &s_abort)) break;
+      }
+      if (s_abort) break;
+      const int r0 = row_begin + t * p.rt;
+      const int rows = min(p.rt, row_end - r0);
+      const uint32_t bw = static_cast<uint32_t>(rows) * p.row_bytes;
+      const uint32_t bs = Fmt::kScales ? static_cast<uint32_t>(rows) * p.gpr * 4u : 0u;
+      const uint8_t* gw = p.w + static_cast<int64_t>(r0) * p.row_bytes;
+      const float* gsc = Fmt::kScales ? p.ws + static_cast<int64_t>(r0) * p.gpr : nullptr;
+      uint8_t* dw = stw + s * p.stage_w_bytes;
+      uint8_t* ds = sts + s * p.stage_s_bytes;
+      if (p.bulk) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], bw + bs);
+          bulk_g2s(dw, gw, bw, &full[s], pol);
+          if (Fmt::kScales && bs) bulk_g2s(ds, gsc, bs, &full[s], pol);
+        }
+      } else {
+        for (uint32_t i = lane; i < bw; i += 32) dw[i] = gw[i];
+        if (Fmt::kScales)
+          for (uint32_t i = lane; i < bs / 4; i += 32) reinterpret_cast<float*>(ds)[i] = gsc[i];
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+      ++issued;
+    }
+    // Drain: never leave the CTA with a bulk copy still landing in shared.
+    if (p.bulk && lane == 0) {
+      for (int t = max(0, issued - p.stages); t < issued; ++t)
+        mbar_wait(&full[t % p.stages], (t / p.stages) & 1);
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- folder
+    for (int t = 0; t < ntiles; ++t) {
+      const int tb = t & 1;
+      if (!mbar_wait(&tfull[tb], (t >> 1) & 1, &s_abort)) break;
+      if (s_abort) break;
+      const int r0 = row_begin + t * p.rt;
+      const int rows = min(p.rt, row_end - r0);
+      if (lane < rows) {
+        const float* T = terms + (tb * p.rt + lane) * p.tstride;
+        const int g4 = p.gpr & ~3;
+        if (Fmt::kFold == Fold::Serial) {
+          float tot = 0.0f;
+          for (int g = 0; g < g4; g += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(T + g);
+            tot = fadd(tot, v.x);
+            tot = fadd(tot, v.y);
+            tot = fadd(tot, v.z);
+            tot = fadd(tot, v.w);
+          }
+          for (int g = g4; g < p.gpr; ++g) tot = fadd(tot, T[g]);
+          p.y[r0 + lane] = tot;
+        } else {
+          float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
+          for (int g = 0; g < g4; g += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(T + g);
+            l0 = fadd(l0, v.x);
+            l1 = fadd(l1, v.y);
+            l2 = fadd(l2, v.z);
+            l3 = fadd(l3, v.w);
+          }
+          for (int g = g4; g < p.gpr; ++g) {
+            const int l = g & 3;
+            if (l == 0) l0 = fadd(l0, T[g]);
+            else if (l == 1) l1 = fadd(l1, T[g]);
+            else l2 = fadd(l2, T[g]);
+          }
+          p.y[r0 + lane] = fadd(fadd(l0, l1), fadd(l2, l3));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[tb]);
+    }
+  } else {
+    // ------------------------------------------------------ consumers
+    const int ct = threadIdx.x - 64;
+    constexpr int NC = NCW * 32;
+    Fmt f;
+    f.init(p, xsm);
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % p.stages;
+      const int tb = t & 1;
+      bool ok = mbar_wait(&full[s], (t / p.stages) & 1, &s_abort);
+      if (ok && t >= 2) ok = mbar_wait(&tempty[tb], ((t >> 1) - 1) & 1, &s_abort);
+      if (!ok) break;
+      if (s_abort) break;
+      const int r0 = row_begin + t * p.rt;
+      const int rows = min(p.rt, row_end - r0);
+      const uint8_t* W = stw + s * p.stage_w_bytes;
+      const float* S = reinterpret_cast<const float*>(sts + s * p.stage_s_bytes);
+      float* T = terms + tb * p.rt * p.tstride;
+      const int npairs = (rows + 1) >> 1;
+      const int nunits = npairs * p.gpr;
+      for (int q = ct; q < nunits; q += NC) {
+        const int rp = q / p.gpr;
+        const int g = q - rp * p.gpr;
+        const int ra = 2 * rp;
+        const int rb = min(ra + 1, rows - 1);
+        float ta, tbv;
+        f.term2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                S + rb * p.gpr, g, ta, tbv);
+        T[ra * p.tstride + g] = ta;
+        if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = tbv;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        mbar_arrive(&tfull[tb]);
+      }
+    }
+  }
+}
+
+}  // namespace lp

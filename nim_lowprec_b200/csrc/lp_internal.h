@@ -1,0 +1,58 @@
+// lp_internal.h -- host-side plumbing shared by the library's .cu files.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "lowprec_cuda.h"
+
+namespace lp {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int ordinal = -1;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+
+// Properties of the current device (queried once per device, cached).
+const DeviceInfo& device_info();
+
+struct GemvParams;
+struct FmtI8;
+struct FmtI4;
+struct FmtF4;
+struct FmtQ8_0;
+struct FmtQ4_0;
+struct FmtQ8;
+struct FmtI4Q8;
+struct FmtQ8_0Q8;
+struct FmtQ4_0Q8;
+
+template <class Fmt>
+int launch_gemv(GemvParams p, cudaStream_t st);
+
+// encoders (quant.cu)
+int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* qs, float* d,
+                         cudaStream_t st);
+int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStream_t st);
+int launch_quantize_batch(const float* x, int64_t n, const float* scales, int64_t gs,
+                          int8_t* dst, cudaStream_t st);
+int launch_calibrate(const float* x, int64_t n, int64_t gs, float qmax, int mx_emax, int mx,
+                     float* scales, int64_t nscales, cudaStream_t st);
+int launch_quantize_packed(const float* x, int64_t n, const float* scales, int64_t gs, int f4,
+                           uint8_t* packed, cudaStream_t st);
+int launch_dequantize_blocks(const uint8_t* blocks, int64_t nblocks, int q4, float* dst,
+                             cudaStream_t st);
+
+// GEMM (gemm.cu)
+int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
+                const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
+
+// error words of the translation units whose kernels wait (read + clear)
+unsigned int take_error_gemv();
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LP_OK : LP_ERR_CUDA; }
+
+}  // namespace lp

@@ -1,0 +1,285 @@
+// quant.cu -- the encoders of the hot path, bit-exact against the reference:
+//   quantizeQ8_0 / quantizeQ8_0Batch   one warp per 32-element block: warp
+//                                      abs-max (order-free), d = amax/127,
+//                                      q = clamp(round(x * (1/d)), +-127)
+//   quantizeQ4_0                        sign-keeping max, first index wins
+//   quantizeBatch                       q = toI8(x / scale)
+//   calibrateSymmetric / calibrateMX    per-group abs-max -> scale
+//   quantize[I4]+packInt4, quantize[F4E2M1]+packF4   weight preparation
+//   dequantizeQ8_0 / Q4_0               blocks -> fp32
+// Division, reciprocal and the fp16 conversion are the IEEE round-to-nearest
+// operations (__fdiv_rn, __float2half_rn); roundf rounds half away from zero
+// like Nim's round (simd/dequant.nim:1589-1591).  These kernels stream
+// activation-sized data (or run once at weight load), so they are simple
+// coalesced grid-stride kernels.
+#include <algorithm>
+
+#include "lp_device.cuh"
+#include "lp_internal.h"
+
+namespace lp {
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(int64_t work, int per_block) {
+  const DeviceInfo& di = device_info();
+  const int64_t need = (work + per_block - 1) / per_block;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, di.sm_count * 16)));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ggml.nim:60-75.  Writes packed blocks and/or the split (qs, f32(f16(d))).
+__global__ void k_quantize_q8_0(const float* __restrict__ src, int64_t nblocks,
+                                uint8_t* __restrict__ blocks, int8_t* __restrict__ qs,
+                                float* __restrict__ dsplit) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t b = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       b < nblocks; b += warps) {
+    const float v = src[b * 32 + lane];
+    const float amax = warp_max(fabsf(v));  // NaN never wins, as with the strict > scan
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    float r = roundf(__fmul_rn(v, id));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    const int8_t q = static_cast<int8_t>(static_cast<int>(r));
+    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+    if (blocks) {
+      uint8_t* blk = blocks + b * 34;
+      blk[2 + lane] = static_cast<uint8_t>(q);
+      if (lane == 0) {
+        blk[0] = static_cast<uint8_t>(dh & 0xFF);
+        blk[1] = static_cast<uint8_t>(dh >> 8);
+      }
+    }
+    if (qs) qs[b * 32 + lane] = q;
+    if (dsplit && lane == 0) dsplit[b] = h2f(dh);
+  }
+}
+
+// ggml.nim:77-97: vmax = the first element of largest magnitude (strict >
+// scan from 0), d = vmax / -8, q = clamp(int(round(x*id)) + 8, 0, 15).
+__global__ void k_quantize_q4_0(const float* __restrict__ src, int64_t nblocks,
+                                uint8_t* __restrict__ blocks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t b = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       b < nblocks; b += warps) {
+    const float v = src[b * 32 + lane];
+    const float a = fabsf(v);
+    // key: magnitude bits (NaN excluded), ties to the lowest index
+    const uint64_t mag = (a == a) ? __float_as_uint(a) : 0u;
+    uint64_t key = (mag << 32) | static_cast<uint32_t>(31 - lane);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other > key ? other : key;
+    }
+    const int win = 31 - static_cast<int>(key & 31u);
+    const float vw = __shfl_sync(0xffffffffu, v, win);
+    const float vmax = (key >> 32) != 0 ? vw : 0.0f;
+    const float d = __fdiv_rn(vmax, -8.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int q = static_cast<int>(roundf(__fmul_rn(v, id))) + 8;
+    q = min(max(q, 0), 15);
+    const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
+    uint8_t* blk = blocks + b * 18;
+    if (lane < 16) blk[2 + lane] = static_cast<uint8_t>(q | (qhi << 4));
+    if (lane == 0) {
+      const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+      blk[0] = static_cast<uint8_t>(dh & 0xFF);
+      blk[1] = static_cast<uint8_t>(dh >> 8);
+    }
+  }
+}
+
+// quant.nim:48-60 (quantizeBatch, simd/dequant.nim:1717-1750):
+// toI8(x / scale): round half away, clamp [-128, 127].
+__global__ void k_quantize_batch(const float* __restrict__ x, int64_t n,
+                                 const float* __restrict__ scales, int64_t gs,
+                                 int8_t* __restrict__ dst) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float s = scales[gs > 0 ? i / gs : 0];
+    float r = roundf(__fadd_rn(__fdiv_rn(x[i], s), 0.0f));
+    r = fminf(fmaxf(r, -128.0f), 127.0f);
+    dst[i] = static_cast<int8_t>(static_cast<int>(r));
+  }
+}
+
+// floor(log2(a)) the way frexp reports it (a > 0 finite); glibc's frexp
+// gives exponent 0 for an infinity, which the reference then uses as is.
+__device__ __forceinline__ int floor_log2(float a) {
+  const uint32_t u = __float_as_uint(a);
+  if (u >= 0x7F800000u) return -1;              // +inf: frexp exp 0 -> 0 - 1
+  if (u >= 0x00800000u) return static_cast<int>(u >> 23) - 127;
+  return (31 - __clz(static_cast<int>(u))) - 149;  // subnormal
+}
+
+__device__ __forceinline__ float pow2i(int k) {  // exact 2^k, k in [-127, 127]
+  return k >= -126 ? __uint_as_float(static_cast<uint32_t>(k + 127) << 23)
+                   : __uint_as_float(0x00400000u);
+}
+
+// calibrateSymmetric (quant.nim:84-110) and calibrateMX (quant.nim:112-137):
+// one CTA per group.
+__global__ void k_calibrate(const float* __restrict__ x, int64_t n, int64_t gs, float qmax,
+                            int emax, int mx, float* __restrict__ scales, int64_t nscales) {
+  __shared__ float red[kThreads / 32];
+  for (int64_t g = blockIdx.x; g < nscales; g += gridDim.x) {
+    const int64_t lo = g * gs;
+    const int64_t hi = min(lo + gs, n);
+    float m = 0.0f;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+      v = warp_max(v);
+      if (threadIdx.x == 0) {
+        float s;
+        if (mx) {
+          if (v == 0.0f) {
+            s = 1.0f;
+          } else {
+            int k = floor_log2(v) - emax;
+            k = max(-127, min(127, k));
+            s = pow2i(k);
+          }
+        } else {
+          s = v == 0.0f ? 1.0f : __fdiv_rn(v, qmax);
+        }
+        scales[g] = s;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// toF4E2M1 (mxfloat.nim:52-66, nearestCode tinyfloat.nim:24-46).
+__device__ __forceinline__ uint32_t to_e2m1(float f) {
+  const uint32_t sign = (__float_as_uint(f) >> 31) ? 8u : 0u;
+  const float a = fabsf(f);
+  if (a != a) return 0u;
+  if (a >= 6.0f) return sign | 7u;
+  const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  int lo = 0, hi = 7;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (mag[mid] >= a) hi = mid;
+    else lo = mid + 1;
+  }
+  int code = 0;
+  if (hi != 0) {
+    const int clo = hi - 1;
+    const float midv = (mag[clo] + mag[hi]) * 0.5f;  // exact on this grid
+    if (a < midv) code = clo;
+    else if (a > midv) code = hi;
+    else code = (clo & 1) == 0 ? clo : hi;
+  }
+  return code == 0 ? sign : (sign | static_cast<uint32_t>(code));
+}
+
+// quantize[T] (quant.nim:48-60, value = x/scale + 0.0) + pack two per byte,
+// low nibble = even index (intx.nim:83-94, mxfloat.nim:138-149).
+__global__ void k_quantize_packed(const float* __restrict__ x, int64_t n,
+                                  const float* __restrict__ scales, int64_t gs, int f4,
+                                  uint8_t* __restrict__ packed) {
+  const int64_t nbytes = (n + 1) / 2;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < nbytes;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint32_t nib[2] = {0u, 0u};
+    for (int h = 0; h < 2; ++h) {
+      const int64_t i = 2 * j + h;
+      if (i >= n) break;
+      const float s = scales[gs > 0 ? i / gs : 0];
+      const float v = __fadd_rn(__fdiv_rn(x[i], s), 0.0f);
+      if (f4) {
+        nib[h] = to_e2m1(v);
+      } else {
+        float r = roundf(v);
+        r = fminf(fmaxf(r, -8.0f), 7.0f);
+        nib[h] = static_cast<uint32_t>(static_cast<int>(r)) & 15u;
+      }
+    }
+    packed[j] = static_cast<uint8_t>(nib[0] | (nib[1] << 4));
+  }
+}
+
+// dequantizeQ8_0 / dequantizeQ4_0 (ggml.nim:36-56): value = d * q.
+__global__ void k_dequantize_blocks(const uint8_t* __restrict__ blocks, int64_t nblocks, int q4,
+                                    float* __restrict__ dst) {
+  const int64_t n = nblocks * 32;
+  const int bs = q4 ? 18 : 34;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (i >> 5) * bs;
+    const int e = static_cast<int>(i & 31);
+    const float d = h2f(static_cast<uint32_t>(blk[0]) | (static_cast<uint32_t>(blk[1]) << 8));
+    int q;
+    if (q4) {
+      const uint32_t b = blk[2 + (e & 15)];
+      q = static_cast<int>(e < 16 ? (b & 15u) : (b >> 4)) - 8;
+    } else {
+      q = static_cast<int8_t>(blk[2 + e]);
+    }
+    dst[i] = __fmul_rn(d, i2f_rn(q));
+  }
+}
+
+}  // namespace
+
+int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* qs, float* d,
+                         cudaStream_t st) {
+  const int64_t nb = n / 32;
+  if (nb == 0) return LP_OK;
+  k_quantize_q8_0<<<grid_for(nb * 32, kThreads), kThreads, 0, st>>>(src, nb, blocks, qs, d);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStream_t st) {
+  const int64_t nb = n / 32;
+  if (nb == 0) return LP_OK;
+  k_quantize_q4_0<<<grid_for(nb * 32, kThreads), kThreads, 0, st>>>(src, nb, blocks);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_quantize_batch(const float* x, int64_t n, const float* scales, int64_t gs,
+                          int8_t* dst, cudaStream_t st) {
+  if (n == 0) return LP_OK;
+  k_quantize_batch<<<grid_for(n, kThreads), kThreads, 0, st>>>(x, n, scales, gs, dst);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_calibrate(const float* x, int64_t n, int64_t gs, float qmax, int mx_emax, int mx,
+                     float* scales, int64_t nscales, cudaStream_t st) {
+  if (nscales == 0) return LP_OK;
+  const int grid = static_cast<int>(std::min<int64_t>(nscales, device_info().sm_count * 8));
+  k_calibrate<<<grid, kThreads, 0, st>>>(x, n, gs, qmax, mx_emax, mx, scales, nscales);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_quantize_packed(const float* x, int64_t n, const float* scales, int64_t gs, int f4,
+                           uint8_t* packed, cudaStream_t st) {
+  if (n == 0) return LP_OK;
+  k_quantize_packed<<<grid_for((n + 1) / 2, kThreads), kThreads, 0, st>>>(x, n, scales, gs, f4,
+                                                                           packed);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_dequantize_blocks(const uint8_t* blocks, int64_t nblocks, int q4, float* dst,
+                             cudaStream_t st) {
+  if (nblocks == 0) return LP_OK;
+  k_dequantize_blocks<<<grid_for(nblocks * 32, kThreads), kThreads, 0, st>>>(blocks, nblocks, q4,
+                                                                             dst);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace lp

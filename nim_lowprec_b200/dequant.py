@@ -1,0 +1,293 @@
+"""The reference's kernel API, proc for proc, over the CUDA library.
+
+Names, argument order and meaning follow nim-lowprec's ``simd/dequant`` and
+``ggml``/``quant`` procs (cited per function).  As in the reference, shapes
+come from array lengths and the output ``y`` (``var openArray[float32]``) is
+written in place.  A failed shape precondition raises ``AssertionError`` (the
+reference's ``assert``).
+
+Arrays may be
+  * torch CUDA tensors: the device path (``lp_*``), stream-ordered on
+    ``torch.cuda.current_stream()``;
+  * numpy arrays: the host drop-in path (``lph_*``), blocking, with every
+    input copied to the device and ``y`` copied back.
+Mixing the two in one call is an error.  Everything must be C-contiguous.
+ggml block arrays are numpy structured arrays of ``BlockQ8_0``/``BlockQ4_0``
+or uint8 arrays/tensors whose total size is a multiple of the block size.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import _native as N
+from .ggml import Q4_0_BYTES, Q8_0_BYTES
+
+try:  # torch is optional for the host path
+    import torch
+except Exception:  # pragma: no cover
+    torch = None
+
+
+def _is_tensor(a) -> bool:
+    return torch is not None and isinstance(a, torch.Tensor)
+
+
+def _mode(*arrs) -> str:
+    dev = [a for a in arrs if a is not None]
+    kinds = {("dev" if _is_tensor(a) else "host") for a in dev}
+    if len(kinds) != 1:
+        raise TypeError("pass all-torch-CUDA or all-numpy arrays, not a mix")
+    kind = kinds.pop()
+    if kind == "dev":
+        for a in dev:
+            if not a.is_cuda:
+                raise TypeError("torch tensors must live on a CUDA device")
+            if not a.is_contiguous():
+                raise ValueError("tensors must be contiguous")
+    else:
+        for a in dev:
+            if not isinstance(a, np.ndarray):
+                raise TypeError(f"expected numpy array, got {type(a).__name__}")
+            if not a.flags["C_CONTIGUOUS"]:
+                raise ValueError("arrays must be C-contiguous")
+    return kind
+
+
+_TORCH_DT = {}
+if torch is not None:
+    _TORCH_DT = {torch.int8: np.int8, torch.uint8: np.uint8, torch.float32: np.float32}
+
+
+def _check_dtype(a, want, name):
+    if a is None:
+        return
+    got = _TORCH_DT.get(a.dtype) if _is_tensor(a) else a.dtype
+    if got is None or np.dtype(got) != np.dtype(want):
+        raise TypeError(f"{name}: expected {np.dtype(want)}, got {a.dtype}")
+
+
+def _numel(a) -> int:
+    return 0 if a is None else (a.numel() if _is_tensor(a) else a.size)
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    return a.data_ptr() if _is_tensor(a) else a.ctypes.data
+
+
+def _blocks(a, bb: int) -> int:
+    """Block count of a ggml block array (structured or raw bytes)."""
+    if isinstance(a, np.ndarray) and a.dtype.fields is not None:
+        if a.dtype.itemsize != bb:
+            raise TypeError(f"block dtype itemsize {a.dtype.itemsize} != {bb}")
+        return a.size
+    _check_dtype(a, np.uint8, "blocks")
+    n = _numel(a)
+    if n % bb:
+        raise AssertionError(f"block array of {n} bytes is not a multiple of {bb}")
+    return n // bb
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _call(mode, name, *args):
+    L = N.lib()
+    if mode == "dev":
+        st = getattr(L, "lp_" + name)(*args, _stream())
+    else:
+        st = getattr(L, "lph_" + name)(*args)
+    N.check(st, name)
+
+
+# ====================================== fp32-activation fused GEMVs ======
+
+def _gemv_group(name, w, scales, groupSize, x, y, wdt):
+    mode = _mode(w, scales, x, y)
+    _check_dtype(w, wdt, "w"); _check_dtype(scales, np.float32, "scales")
+    _check_dtype(x, np.float32, "x"); _check_dtype(y, np.float32, "y")
+    _call(mode, name, _ptr(w), _numel(w), _ptr(scales), _numel(scales), int(groupSize),
+          _ptr(x), _numel(x), _ptr(y), _numel(y))
+
+
+def dequantGemv(wq, scales, groupSize, x, y):
+    """simd/dequant.nim:210-257: int8 weights, fp32 activations."""
+    _gemv_group("dequant_gemv", wq, scales, groupSize, x, y, np.int8)
+
+
+def dequantGemvI4(wpacked, scales, groupSize, x, y):
+    """simd/dequant.nim:259-339: packed int4 weights (low nibble = even column)."""
+    _gemv_group("dequant_gemv_i4", wpacked, scales, groupSize, x, y, np.uint8)
+
+
+def dequantGemvF4(wpacked, scales, groupSize, x, y):
+    """simd/dequant.nim:341-420: packed MXFP4 (e2m1) weights, fp32 E8M0 scales."""
+    _gemv_group("dequant_gemv_f4", wpacked, scales, groupSize, x, y, np.uint8)
+
+
+def _gemv_blocks(name, w, bb, blocksPerRow, x, y, xq_blocks=False):
+    mode = _mode(w, x, y)
+    nw = _blocks(w, bb)
+    if xq_blocks:
+        nx = _blocks(x, Q8_0_BYTES)
+    else:
+        _check_dtype(x, np.float32, "x")
+        nx = _numel(x)
+    _check_dtype(y, np.float32, "y")
+    _call(mode, name, _ptr(w), nw, int(blocksPerRow), _ptr(x), nx, _ptr(y), _numel(y))
+
+
+def dequantGemvQ8_0(w, blocksPerRow, x, y):
+    """simd/dequant.nim:530-568: ggml Q8_0 weights, fp32 activations."""
+    _gemv_blocks("dequant_gemv_q8_0", w, Q8_0_BYTES, blocksPerRow, x, y)
+
+
+def dequantGemvQ4_0(w, blocksPerRow, x, y):
+    """simd/dequant.nim:570-622: ggml Q4_0 weights, fp32 activations."""
+    _gemv_blocks("dequant_gemv_q4_0", w, Q4_0_BYTES, blocksPerRow, x, y)
+
+
+# ====================================== int8-activation GEMVs ===========
+
+def _gemv_q8(name, w, wScales, groupSize, xq, xScales, y, wdt):
+    mode = _mode(w, wScales, xq, xScales, y)
+    _check_dtype(w, wdt, "w"); _check_dtype(wScales, np.float32, "wScales")
+    _check_dtype(xq, np.int8, "xq"); _check_dtype(xScales, np.float32, "xScales")
+    _check_dtype(y, np.float32, "y")
+    _call(mode, name, _ptr(w), _numel(w), _ptr(wScales), _numel(wScales), int(groupSize),
+          _ptr(xq), _numel(xq), _ptr(xScales), _numel(xScales), _ptr(y), _numel(y))
+
+
+def dequantGemvQ8(wq, wScales, groupSize, xq, xScales, y):
+    """simd/dequant.nim:753-878: int8 x int8, exact int32 group sums."""
+    _gemv_q8("dequant_gemv_q8", wq, wScales, groupSize, xq, xScales, y, np.int8)
+
+
+def dequantGemvI4Q8(wpacked, wScales, groupSize, xq, xScales, y):
+    """simd/dequant.nim:968-1145: packed int4 x int8."""
+    _gemv_q8("dequant_gemv_i4q8", wpacked, wScales, groupSize, xq, xScales, y, np.uint8)
+
+
+def dequantGemvQ8_0Q8(w, blocksPerRow, xq, y):
+    """simd/dequant.nim:1187-1286: Q8_0 weights x Q8_0 activation blocks."""
+    _gemv_blocks("dequant_gemv_q8_0q8", w, Q8_0_BYTES, blocksPerRow, xq, y, xq_blocks=True)
+
+
+def dequantGemvQ4_0Q8(w, blocksPerRow, xq, y):
+    """simd/dequant.nim:1288-1365: Q4_0 weights x Q8_0 activation blocks."""
+    _gemv_blocks("dequant_gemv_q4_0q8", w, Q4_0_BYTES, blocksPerRow, xq, y, xq_blocks=True)
+
+
+# ====================================== multi-column GEMM ===============
+
+def _gemm(name, w, wScales, groupSize, xq, xScales, n, y, wdt):
+    mode = _mode(w, wScales, xq, xScales, y)
+    _check_dtype(w, wdt, "w"); _check_dtype(wScales, np.float32, "wScales")
+    _check_dtype(xq, np.int8, "xq"); _check_dtype(xScales, np.float32, "xScales")
+    _check_dtype(y, np.float32, "y")
+    _call(mode, name, _ptr(w), _numel(w), _ptr(wScales), _numel(wScales), int(groupSize),
+          _ptr(xq), _numel(xq), _ptr(xScales), _numel(xScales), int(n), _ptr(y), _numel(y))
+
+
+def dequantGemmQ8(wq, wScales, groupSize, xq, xScales, n, y):
+    """simd/dequant.nim:1382-1458: xq K x n column-major, y M x n row-major."""
+    _gemm("dequant_gemm_q8", wq, wScales, groupSize, xq, xScales, n, y, np.int8)
+
+
+def dequantGemmI4Q8(wpacked, wScales, groupSize, xq, xScales, n, y):
+    """simd/dequant.nim:1460-1583."""
+    _gemm("dequant_gemm_i4q8", wpacked, wScales, groupSize, xq, xScales, n, y, np.uint8)
+
+
+# ====================================== encoders ========================
+
+def quantizeQ8_0Batch(src, blocks):
+    """simd/dequant.nim:1624-1641 (= quantizeQ8_0, ggml.nim:60-75)."""
+    mode = _mode(src, blocks)
+    _check_dtype(src, np.float32, "src")
+    _call(mode, "quantize_q8_0_batch", _ptr(src), _numel(src), _ptr(blocks),
+          _blocks(blocks, Q8_0_BYTES))
+
+
+def quantizeQ4_0Batch(src, blocks):
+    """simd/dequant.nim:1643-1715 (= quantizeQ4_0, ggml.nim:77-97)."""
+    mode = _mode(src, blocks)
+    _check_dtype(src, np.float32, "src")
+    _call(mode, "quantize_q4_0_batch", _ptr(src), _numel(src), _ptr(blocks),
+          _blocks(blocks, Q4_0_BYTES))
+
+
+quantizeQ8_0 = quantizeQ8_0Batch
+quantizeQ4_0 = quantizeQ4_0Batch
+
+
+def quantizeBatch(x, scales, groupSize, dst):
+    """simd/dequant.nim:1717-1750: dst = toI8(x / scale); groupSize <= 0 is
+    per-tensor (QParams.scheme = qPerTensor)."""
+    mode = _mode(x, scales, dst)
+    _check_dtype(x, np.float32, "x"); _check_dtype(scales, np.float32, "scales")
+    _check_dtype(dst, np.int8, "dst")
+    _call(mode, "quantize_batch", _ptr(x), _numel(x), _ptr(scales), _numel(scales),
+          int(groupSize), _ptr(dst), _numel(dst))
+
+
+def _dev_only(name, *arrs):
+    if _mode(*arrs) != "dev":
+        raise TypeError(f"{name} takes torch CUDA tensors")
+
+
+def quantizeQ8_0Split(src, qs, d):
+    """quantizeQ8_0 (ggml.nim:60-75) with the block fields split into the
+    (xq, xScales) arrays of dequantGemvQ8: d = f32(f16(amax/127))."""
+    _dev_only("quantizeQ8_0Split", src, qs, d)
+    N.check(N.lib().lp_quantize_q8_0_split(_ptr(src), _numel(src), _ptr(qs), _numel(qs),
+                                           _ptr(d), _numel(d), _stream()), "quantize_q8_0_split")
+
+
+def calibrateSymmetric(x, groupSize, qmax, scales):
+    """quant.nim:95-110, writing the scales into `scales` (device)."""
+    _dev_only("calibrateSymmetric", x, scales)
+    N.check(N.lib().lp_calibrate_symmetric(_ptr(x), _numel(x), int(groupSize), float(qmax),
+                                           _ptr(scales), _numel(scales), _stream()),
+            "calibrate_symmetric")
+
+
+def calibrateMX(x, blockSize, elemEmax, scales):
+    """quant.nim:125-137, writing the E8M0-valued fp32 scales (device)."""
+    _dev_only("calibrateMX", x, scales)
+    N.check(N.lib().lp_calibrate_mx(_ptr(x), _numel(x), int(blockSize), int(elemEmax),
+                                    _ptr(scales), _numel(scales), _stream()), "calibrate_mx")
+
+
+def quantizeI4Packed(x, scales, groupSize, packed):
+    """quantize[I4] (quant.nim:48-60) + packInt4 (intx.nim:83-94), device."""
+    _dev_only("quantizeI4Packed", x, scales, packed)
+    N.check(N.lib().lp_quantize_i4_packed(_ptr(x), _numel(x), _ptr(scales), _numel(scales),
+                                          int(groupSize), _ptr(packed), _numel(packed),
+                                          _stream()), "quantize_i4_packed")
+
+
+def quantizeF4Packed(x, scales, blockSize, packed):
+    """quantize[F4E2M1] (quant.nim:48-60) + packF4 (mxfloat.nim:138-149), device."""
+    _dev_only("quantizeF4Packed", x, scales, packed)
+    N.check(N.lib().lp_quantize_f4_packed(_ptr(x), _numel(x), _ptr(scales), _numel(scales),
+                                          int(blockSize), _ptr(packed), _numel(packed),
+                                          _stream()), "quantize_f4_packed")
+
+
+def dequantizeQ8_0Batch(blocks, dst):
+    """simd/dequant.nim:446-485 (= dequantizeQ8_0, ggml.nim:36-45), device."""
+    _dev_only("dequantizeQ8_0Batch", blocks, dst)
+    N.check(N.lib().lp_dequantize_q8_0_batch(_ptr(blocks), _blocks(blocks, Q8_0_BYTES),
+                                             _ptr(dst), _numel(dst), _stream()),
+            "dequantize_q8_0_batch")
+
+
+def dequantizeQ4_0Batch(blocks, dst):
+    """simd/dequant.nim:487-526 (= dequantizeQ4_0, ggml.nim:46-56), device."""
+    _dev_only("dequantizeQ4_0Batch", blocks, dst)
+    N.check(N.lib().lp_dequantize_q4_0_batch(_ptr(blocks), _blocks(blocks, Q4_0_BYTES),
+                                             _ptr(dst), _numel(dst), _stream()),
+            "dequantize_q4_0_batch")

@@ -1,0 +1,92 @@
+"""CPU checks of the C ABI: the library loads without a GPU, exports every
+symbol the public header declares, and rejects bad shapes with LP_ERR_SHAPE
+before touching the device (the reference's entry asserts)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from nim_lowprec_b200 import _native as N
+
+
+def test_library_exports_every_header_symbol():
+    L = N.lib()
+    syms = N.header_symbols()
+    assert len(syms) >= 38
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert missing == []
+
+
+def test_every_header_symbol_has_a_prototype():
+    syms = set(N.header_symbols())
+    bound = set(N.SIGNATURES) | {"lp_version", "lp_status_string", "lp_device_error"}
+    assert syms <= bound
+
+
+def test_version_and_status_strings():
+    L = N.lib()
+    assert L.lp_version() == 100
+    assert N.status_string(N.LP_ERR_SHAPE) == "shape precondition failed"
+    assert N.status_string(N.LP_ERR_TIMEOUT) == "device-side wait timed out"
+
+
+NULL = None
+
+
+@pytest.mark.parametrize("args", [
+    # wq_len != m*k
+    (NULL, 10, NULL, 2, 32, NULL, 64, NULL, 2, NULL, 1, NULL),
+    # k not a multiple of groupSize
+    (NULL, 40, NULL, 2, 32, NULL, 40, NULL, 2, NULL, 1, NULL),
+    # groupSize 0 (the reference divides by it)
+    (NULL, 64, NULL, 2, 0, NULL, 64, NULL, 2, NULL, 1, NULL),
+    # xScales.len != gpr
+    (NULL, 64, NULL, 2, 32, NULL, 64, NULL, 3, NULL, 1, NULL),
+])
+def test_gemv_q8_shape_rules(args):
+    assert N.lib().lp_dequant_gemv_q8(*args) == N.LP_ERR_SHAPE
+
+
+def test_i4_requires_even_k_and_packed_length():
+    L = N.lib()
+    # k = 3 odd, gs 3
+    assert L.lp_dequant_gemv_i4q8(NULL, 1, NULL, 1, 3, NULL, 3, NULL, 1, NULL, 1, NULL) == N.LP_ERR_SHAPE
+    # packed length must be m*k/2
+    assert L.lp_dequant_gemv_i4q8(NULL, 64, NULL, 2, 32, NULL, 64, NULL, 2, NULL, 1, NULL) == N.LP_ERR_SHAPE
+
+
+def test_ggml_shape_rules():
+    L = N.lib()
+    # x.len must be blocksPerRow * 32
+    assert L.lp_dequant_gemv_q4_0(NULL, 4, 4, NULL, 100, NULL, 1, NULL) == N.LP_ERR_SHAPE
+    # w.len must be m * blocksPerRow
+    assert L.lp_dequant_gemv_q8_0q8(NULL, 5, 4, NULL, 4, NULL, 1, NULL) == N.LP_ERR_SHAPE
+    # quantize: src.len == blocks.len * 32
+    assert L.lp_quantize_q8_0_batch(NULL, 33, NULL, 1, NULL) == N.LP_ERR_SHAPE
+
+
+def test_gemm_shape_rules():
+    L = N.lib()
+    # n = 0 (the reference divides by n)
+    assert L.lp_dequant_gemm_q8(NULL, 0, NULL, 0, 32, NULL, 0, NULL, 0, 0, NULL, 0, NULL) == N.LP_ERR_SHAPE
+    # y.len not m*n
+    assert L.lp_dequant_gemm_q8(NULL, 64, NULL, 2, 32, NULL, 128, NULL, 4, 2, NULL, 3, NULL) == N.LP_ERR_SHAPE
+
+
+def test_null_pointer_with_valid_shape_is_an_argument_error():
+    L = N.lib()
+    assert L.lp_dequant_gemv_q8(NULL, 64, NULL, 2, 32, NULL, 64, NULL, 2, NULL, 1, NULL) == N.LP_ERR_ARG
+
+
+def test_python_api_maps_shape_errors_to_assertion():
+    import nim_lowprec_b200 as L
+    with pytest.raises(AssertionError):
+        L.dequantGemvQ8(np.zeros(10, np.int8), np.zeros(2, np.float32), 32,
+                        np.zeros(64, np.int8), np.zeros(2, np.float32), np.zeros(1, np.float32))
+
+
+def test_python_api_rejects_wrong_dtypes_and_mixed_arrays():
+    import nim_lowprec_b200 as L
+    with pytest.raises(TypeError):
+        L.dequantGemvQ8(np.zeros(64, np.int16), np.zeros(2, np.float32), 32,
+                        np.zeros(64, np.int8), np.zeros(2, np.float32), np.zeros(1, np.float32))

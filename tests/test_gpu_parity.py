@@ -1,0 +1,447 @@
+"""CUDA kernels vs the CPU oracle, through the C ABI (device and host forms).
+
+Bit-exact for every path (integer, encoder and fp32-activation GEMVs alike:
+the fp32 kernels reproduce the reference's scalar summation order), on
+  * the reference tests' own inputs (test_sdot.nim, test_parallel.nim,
+    test_quant_simd.nim, test_scheme_conformance.nim goldens),
+  * edge shapes (M = 1, odd M, block tails bpr = 3 mod 4, group tails),
+  * the BASELINE configurations at full size (configs 0-2 and the GEMM).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import refcases as C
+from gpu_util import F, acts, bits_equal, mismatch_report, to_dev, to_host, weights
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+import nim_lowprec_b200 as L  # noqa: E402
+from nim_lowprec_b200 import _native as N  # noqa: E402
+
+G = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def dev_y(m):
+    return torch.full((m,), float("nan"), dtype=torch.float32, device="cuda")
+
+
+def assert_bits(got, want):
+    assert bits_equal(got, want), mismatch_report(got, want)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert N.device_error() == 0
+
+
+# ------------------------------------------------------------ encoders --
+
+def test_quantize_q8_0_matches_gguf_golden():
+    x = np.fromfile(os.path.join(G, "ref_scheme_input.bin"), np.float32)
+    want = np.fromfile(os.path.join(G, "ref_ggml_q8_0_bytes.bin"), np.uint8)
+    (xd,) = to_dev(x)
+    blocks = torch.empty(x.size // 32 * 34, dtype=torch.uint8, device="cuda")
+    L.quantizeQ8_0Batch(xd, blocks)
+    assert np.array_equal(to_host(blocks), want)
+
+
+def test_quantize_q4_0_matches_gguf_golden():
+    x = np.fromfile(os.path.join(G, "ref_scheme_input.bin"), np.float32)
+    want = np.fromfile(os.path.join(G, "ref_ggml_q4_0_bytes.bin"), np.uint8)
+    (xd,) = to_dev(x)
+    blocks = torch.empty(x.size // 32 * 18, dtype=torch.uint8, device="cuda")
+    L.quantizeQ4_0Batch(xd, blocks)
+    assert np.array_equal(to_host(blocks), want)
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0"])
+def test_dequantize_blocks_match_gguf_golden(fmt):
+    raw = np.fromfile(os.path.join(G, f"ref_ggml_{fmt}_bytes.bin"), np.uint8)
+    want = np.fromfile(os.path.join(G, f"ref_ggml_{fmt}_dq.bin"), np.uint32)
+    (rd,) = to_dev(raw)
+    out = torch.empty(want.size, dtype=torch.float32, device="cuda")
+    (L.dequantizeQ8_0Batch if fmt == "q8_0" else L.dequantizeQ4_0Batch)(rd, out)
+    assert np.array_equal(to_host(out).view(np.uint32), want)
+
+
+def test_quantize_q8_0_random_and_edges_vs_oracle():
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(32 * 4099) * 3).astype(F)
+    x[32 * 5:32 * 6] = 0.0                # all-zero block: d = 0 path
+    x[32 * 7:32 * 8] = np.float32(1e-30)  # tiny block, d underflows fp16
+    x[32 * 9 + 3] = np.float32(-7.0)      # ties and sign
+    (xd,) = to_dev(x)
+    blocks = torch.empty(x.size // 32 * 34, dtype=torch.uint8, device="cuda")
+    L.quantizeQ8_0Batch(xd, blocks)
+    assert np.array_equal(to_host(blocks), O.quantizeQ8_0(x).reshape(-1))
+    qs = torch.empty(x.size, dtype=torch.int8, device="cuda")
+    d = torch.empty(x.size // 32, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(xd, qs, d)
+    oq, od = O.quantizeQ8_0Split(x)
+    assert np.array_equal(to_host(qs), oq) and bits_equal(to_host(d), od)
+
+
+def test_quantize_q4_0_sign_keeping_max_ties():
+    x = np.zeros(32 * 3, F)
+    x[3], x[10] = -2.0, 2.0      # equal magnitude: the first (negative) wins
+    x[32 + 1], x[32 + 5] = 1.5, -1.5
+    x[64:96] = np.linspace(-1, 1, 32, dtype=F)
+    (xd,) = to_dev(x)
+    blocks = torch.empty(3 * 18, dtype=torch.uint8, device="cuda")
+    L.quantizeQ4_0Batch(xd, blocks)
+    assert np.array_equal(to_host(blocks), O.quantizeQ4_0(x).reshape(-1))
+
+
+@pytest.mark.parametrize("n,gs", [(4096, 128), (4099, 64), (1000, 0), (4096, 32)])
+def test_quantize_batch_and_calibrate_vs_oracle(n, gs):
+    """test_quant_simd.nim:330-355 shapes (per-group, ragged, per-tensor)."""
+    u = 55555
+    x = np.empty(n, F)
+    for i in range(n):
+        u = (u * 1664525 + 1013904223) & 0xFFFFFFFF
+        x[i] = (F(u >> 8) / F(1 << 24) - F(0.5)) * F(30.0)
+    sc_o = O.calibrateSymmetric(x, gs, 127.0)
+    (xd,) = to_dev(x)
+    sc = torch.empty(sc_o.size, dtype=torch.float32, device="cuda")
+    L.calibrateSymmetric(xd, gs, 127.0, sc)
+    assert bits_equal(to_host(sc), sc_o)
+    q = torch.empty(n, dtype=torch.int8, device="cuda")
+    L.quantizeBatch(xd, sc, gs, q)
+    assert np.array_equal(to_host(q), O.quantizeBatch(x, sc_o, gs))
+    # host drop-in form of the same entry point
+    qh = np.empty(n, np.int8)
+    L.quantizeBatch(x, sc_o, gs, qh)
+    assert np.array_equal(qh, O.quantizeBatch(x, sc_o, gs))
+
+
+def test_calibrate_mx_and_f4_pack_vs_golden_input():
+    x = np.fromfile(os.path.join(G, "ref_mx_input.bin"), np.float32)
+    sc_o = O.calibrateMX(x, 32, 2)
+    (xd,) = to_dev(x)
+    sc = torch.empty(sc_o.size, dtype=torch.float32, device="cuda")
+    L.calibrateMX(xd, 32, 2, sc)
+    assert bits_equal(to_host(sc), sc_o)
+    pk = torch.empty(x.size // 2, dtype=torch.uint8, device="cuda")
+    L.quantizeF4Packed(xd, sc, 32, pk)
+    assert np.array_equal(to_host(pk), O.packF4(O.quantize(x, sc_o, 32, "f4")))
+
+
+def test_i4_weight_prep_vs_oracle():
+    w = weights(11, 4096 * 8)
+    sc_o = O.calibrateSymmetric(w, 32, 7.0)
+    (wd,) = to_dev(w)
+    sc = torch.empty(sc_o.size, dtype=torch.float32, device="cuda")
+    L.calibrateSymmetric(wd, 32, 7.0, sc)
+    assert bits_equal(to_host(sc), sc_o)
+    pk = torch.empty(w.size // 2, dtype=torch.uint8, device="cuda")
+    L.quantizeI4Packed(wd, sc, 32, pk)
+    assert np.array_equal(to_host(pk), O.packInt4(O.quantize(w, sc_o, 32, "i4")))
+
+
+# ------------------------------------------- int8-activation GEMVs ------
+
+@pytest.mark.parametrize("M,K,gs", C.SDOT_INT8_SHAPES)
+def test_gemv_q8_sdot_cases(M, K, gs):
+    wq, ws, xq, xs = C.sdot_int8_case(M, K, gs)
+    want = O.dequantGemvQ8(wq, ws, gs, xq, xs)
+    d = to_dev(wq, ws, xq, xs)
+    y = dev_y(M)
+    L.dequantGemvQ8(*d[:2], gs, *d[2:], y)
+    assert_bits(to_host(y), want)
+    yh = np.empty(M, F)
+    L.dequantGemvQ8(wq, ws, gs, xq, xs, yh)   # host drop-in
+    assert_bits(yh, want)
+
+
+@pytest.mark.parametrize("M,K,gs", C.SDOT_INT4_SHAPES)
+def test_gemv_i4q8_sdot_cases(M, K, gs):
+    vals, ws, xq, xs = C.sdot_int4_case(M, K, gs)
+    wp = C.pack_i4_values(vals)
+    want = O.dequantGemvI4Q8(wp, ws, gs, xq, xs)
+    d = to_dev(wp, ws, xq, xs)
+    y = dev_y(M)
+    L.dequantGemvI4Q8(*d[:2], gs, *d[2:], y)
+    assert_bits(to_host(y), want)
+
+
+@pytest.mark.parametrize("M,bpr", C.GGML_SHAPES)
+def test_gemv_ggml_q8_sdot_cases(M, bpr):
+    w8, w4, x = C.ggml_q8_w_blocks(M, bpr), C.ggml_q4_w_blocks(M, bpr), C.ggml_x_blocks(bpr)
+    for fn, ofn, w in ((L.dequantGemvQ8_0Q8, O.dequantGemvQ8_0Q8, w8),
+                       (L.dequantGemvQ4_0Q8, O.dequantGemvQ4_0Q8, w4)):
+        want = ofn(w, bpr, x)
+        wd, xd = to_dev(w.reshape(-1), x.reshape(-1))
+        y = dev_y(M)
+        fn(wd, bpr, xd, y)
+        assert_bits(to_host(y), want)
+        yh = np.empty(M, F)
+        fn(w, bpr, x, yh)
+        assert_bits(yh, want)
+
+
+@pytest.mark.parametrize("M", [1, 7, 300, 4096])
+@pytest.mark.parametrize("K", [4096, 11008])
+def test_gemv_q8_i4q8_q8_0_split_random(M, K):
+    """Config 0 / config 4 arithmetic: weights and activations Q8_0-encoded
+    (split form), gs 32."""
+    w = weights(100 + M, M * K)
+    x = acts(100 + M, K)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)
+    d = to_dev(wq, wd, xq, xd)
+    y = dev_y(M)
+    L.dequantGemvQ8(*d[:2], 32, *d[2:], y)
+    assert_bits(to_host(y), O.dequantGemvQ8(wq, wd, 32, xq, xd))
+    # int4 weights (config 4 weight prep: symmetric qmax 7)
+    s4 = O.calibrateSymmetric(w, 32, 7.0)
+    wp = O.packInt4(O.quantize(w, s4, 32, "i4"))
+    d4 = to_dev(wp, s4)
+    L.dequantGemvI4Q8(d4[0], d4[1], 32, d[2], d[3], y)
+    assert_bits(to_host(y), O.dequantGemvI4Q8(wp, s4, 32, xq, xd))
+
+
+# ------------------------------------------- fp32-activation GEMVs ------
+
+def _fp32_cases():
+    return [(1, 64), (7, 96), (5, 384), (37, 4096), (300, 512), (1024, 4096)]
+
+
+@pytest.mark.parametrize("M,K", _fp32_cases())
+def test_fp32_gemvs_bit_exact_vs_scalar_order(M, K):
+    w = weights(7 + M, M * K)
+    x = acts(7 + M, K)
+    y = dev_y(M)
+    (xd,) = to_dev(x)
+    # int8 per-group
+    s8 = O.calibrateSymmetric(w, 32, 127.0)
+    q8 = O.quantize(w, s8, 32, "i8")
+    a, b = to_dev(q8, s8)
+    L.dequantGemv(a, b, 32, xd, y)
+    assert_bits(to_host(y), O.dequantGemv(q8, s8, 32, x))
+    # int4 packed
+    s4 = O.calibrateSymmetric(w, 32, 7.0)
+    p4 = O.packInt4(O.quantize(w, s4, 32, "i4"))
+    a, b = to_dev(p4, s4)
+    L.dequantGemvI4(a, b, 32, xd, y)
+    assert_bits(to_host(y), O.dequantGemvI4(p4, s4, 32, x))
+    # MXFP4
+    sm = O.calibrateMX(w, 32, 2)
+    pf = O.packF4(O.quantize(w, sm, 32, "f4"))
+    a, b = to_dev(pf, sm)
+    L.dequantGemvF4(a, b, 32, xd, y)
+    assert_bits(to_host(y), O.dequantGemvF4(pf, sm, 32, x))
+    # ggml blocks
+    bpr = K // 32
+    for enc, fn, ofn in ((O.quantizeQ8_0, L.dequantGemvQ8_0, O.dequantGemvQ8_0),
+                         (O.quantizeQ4_0, L.dequantGemvQ4_0, O.dequantGemvQ4_0)):
+        blk = enc(w).reshape(-1)
+        (bd,) = to_dev(blk)
+        fn(bd, bpr, xd, y)
+        assert_bits(to_host(y), ofn(blk, bpr, x))
+
+
+@pytest.mark.parametrize("gs", [20, 40, 48, 64, 96, 128])
+def test_fp32_gemvs_generic_group_sizes(gs):
+    """Group tails that are not 32 (test_quant_simd.nim uses 40 and 48)."""
+    M, K = 23, gs * 6
+    w = weights(gs, M * K)
+    x = acts(gs, K)
+    (xd,) = to_dev(x)
+    y = dev_y(M)
+    s8 = O.calibrateSymmetric(w, gs, 127.0)
+    q8 = O.quantize(w, s8, gs, "i8")
+    a, b = to_dev(q8, s8)
+    L.dequantGemv(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemv(q8, s8, gs, x))
+    s4 = O.calibrateSymmetric(w, gs, 7.0)
+    p4 = O.packInt4(O.quantize(w, s4, gs, "i4"))
+    a, b = to_dev(p4, s4)
+    L.dequantGemvI4(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemvI4(p4, s4, gs, x))
+    sm = O.calibrateMX(w, gs, 2)
+    pf = O.packF4(O.quantize(w, sm, gs, "f4"))
+    a, b = to_dev(pf, sm)
+    L.dequantGemvF4(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemvF4(pf, sm, gs, x))
+    xs = O.calibrateSymmetric(x, gs, 127.0)
+    xq = O.quantizeBatch(x, xs, gs)
+    a, b, c, d = to_dev(q8, s8, xq, xs)
+    L.dequantGemvQ8(a, b, gs, c, d, y)
+    assert_bits(to_host(y), O.dequantGemvQ8(q8, s8, gs, xq, xs))
+
+
+@pytest.mark.parametrize("M", C.PAR_ROWS)
+def test_parallel_test_inputs(M):
+    """The inputs of test_parallel.nim through every fp32 kernel."""
+    x = C.par_x()
+    (xd,) = to_dev(x)
+    y = dev_y(M)
+    gs = C.PAR_GS
+    wq, sc = C.par_int8(M)
+    a, b = to_dev(wq, sc)
+    L.dequantGemv(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemv(wq, sc, gs, x))
+    w4, sc4 = C.par_int4(M)
+    a, b = to_dev(w4, sc4)
+    L.dequantGemvI4(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemvI4(w4, sc4, gs, x))
+    wf, scf = C.par_f4(M)
+    a, b = to_dev(wf, scf)
+    L.dequantGemvF4(a, b, gs, xd, y)
+    assert_bits(to_host(y), O.dequantGemvF4(wf, scf, gs, x))
+    for blocks_fn, fn, ofn in ((C.par_q8_0, L.dequantGemvQ8_0, O.dequantGemvQ8_0),
+                               (C.par_q4_0, L.dequantGemvQ4_0, O.dequantGemvQ4_0)):
+        blk, bpr = blocks_fn(M)
+        (bd,) = to_dev(blk.reshape(-1))
+        fn(bd, bpr, xd, y)
+        assert_bits(to_host(y), ofn(blk, bpr, x))
+
+
+# ----------------------------------------------------------------- GEMM --
+
+@pytest.mark.parametrize("M,K,gs,n", C.GEMM_I8_SHAPES)
+def test_gemm_q8_sdot_cases(M, K, gs, n):
+    wq, ws, xq, xs = C.gemm_int8_case(M, K, gs, n)
+    want = O.dequantGemmQ8(wq, ws, gs, xq, xs, n)
+    d = to_dev(wq, ws, xq, xs)
+    y = dev_y(M * n)
+    L.dequantGemmQ8(*d[:2], gs, *d[2:], n, y)
+    assert_bits(to_host(y), want)
+
+
+@pytest.mark.parametrize("M,K,gs,n", C.GEMM_I4_SHAPES)
+def test_gemm_i4q8_sdot_cases(M, K, gs, n):
+    wp, ws, xq, xs = C.gemm_int4_case(M, K, gs, n)
+    want = O.dequantGemmI4Q8(wp, ws, gs, xq, xs, n)
+    d = to_dev(wp, ws, xq, xs)
+    y = dev_y(M * n)
+    L.dequantGemmI4Q8(*d[:2], gs, *d[2:], n, y)
+    assert_bits(to_host(y), want)
+
+
+@pytest.mark.parametrize("n", [8, 64])
+def test_gemm_config3_full(n):
+    """Config 3: Q8_0 weight 4096x4096 times n Q8_0-quantized columns."""
+    M = K = 4096
+    w = weights(3, M * K)
+    x = acts(3, K * n)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)   # column c = x[c*K:(c+1)*K]
+    pool = O.Pool(0)
+    try:
+        want = O.dequantGemmQ8(wq, wd, 32, xq, xd, n, pool=pool)
+    finally:
+        pool.shutdown()
+    d = to_dev(wq, wd, xq, xd)
+    y = dev_y(M * n)
+    L.dequantGemmQ8(*d[:2], 32, *d[2:], n, y)
+    assert_bits(to_host(y), want)
+
+
+def test_gemm_column_equals_gemv_on_device():
+    """test_sdot.nim:243-282 on the device: every GEMM column is the GEMV."""
+    M, K, n = 129, 512, 5
+    w = weights(9, M * K)
+    x = acts(9, K * n)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)
+    d = to_dev(wq, wd, xq, xd)
+    y = dev_y(M * n)
+    L.dequantGemmQ8(*d[:2], 32, *d[2:], n, y)
+    Y = to_host(y).reshape(M, n)
+    for c in range(n):
+        yc = dev_y(M)
+        L.dequantGemvQ8(d[0], d[1], 32, d[2][c * K:(c + 1) * K], d[3][c * 16:(c + 1) * 16], yc)
+        assert_bits(Y[:, c], to_host(yc))
+
+
+# ------------------------------------------ configs at full size -------
+
+def test_config0_full_q8_gemv():
+    M = K = 4096
+    w = weights(0, M * K)
+    x = acts(0, K)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)
+    d = to_dev(wq, wd, x)
+    # activations quantized on the GPU, as a caller does
+    xq_d = torch.empty(K, dtype=torch.int8, device="cuda")
+    xd_d = torch.empty(K // 32, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(d[2], xq_d, xd_d)
+    assert np.array_equal(to_host(xq_d), xq)
+    y = dev_y(M)
+    L.dequantGemvQ8(d[0], d[1], 32, xq_d, xd_d, y)
+    assert_bits(to_host(y), O.dequantGemvQ8(wq, wd, 32, xq, xd))
+
+
+def test_config1_full_q4_0_gemv():
+    M, K = 11008, 4096
+    w = weights(1, M * K)
+    x = acts(1, K)
+    blk = O.quantizeQ4_0(w).reshape(-1)
+    wd_, xd_ = to_dev(w, x)
+    bd = torch.empty(blk.size, dtype=torch.uint8, device="cuda")
+    L.quantizeQ4_0Batch(wd_, bd)                 # GPU weight prep == oracle
+    assert np.array_equal(to_host(bd), blk)
+    y = dev_y(M)
+    L.dequantGemvQ4_0(bd, K // 32, xd_, y)
+    assert_bits(to_host(y), O.dequantGemvQ4_0(blk, K // 32, x))
+
+
+def test_config2_full_mxfp4_gemv():
+    M, K = 14336, 4096
+    w = weights(2, M * K)
+    x = acts(2, K)
+    sm = O.calibrateMX(w, 32, 2)
+    pf = O.packF4(O.quantize(w, sm, 32, "f4"))
+    a, b, xd = to_dev(pf, sm, x)
+    y = dev_y(M)
+    L.dequantGemvF4(a, b, 32, xd, y)
+    assert_bits(to_host(y), O.dequantGemvF4(pf, sm, 32, x))
+
+
+# ------------------------------------------------------- errors, edges --
+
+def test_shape_errors_raise_like_reference_asserts():
+    wq, ws, xq, xs = to_dev(np.zeros(64, np.int8), np.zeros(2, F), np.zeros(32, np.int8),
+                            np.zeros(1, F))
+    with pytest.raises(AssertionError):
+        L.dequantGemvQ8(wq, ws, 32, xq, xs, dev_y(3))       # wq.len != m*k
+    with pytest.raises(AssertionError):
+        L.dequantGemvQ8(wq, ws, 0, xq, xs, dev_y(2))        # groupSize 0
+    with pytest.raises(AssertionError):
+        L.dequantGemvQ8(wq, ws, 32, xq, torch.zeros(2, device="cuda"), dev_y(2))
+
+
+def test_empty_shapes():
+    # m = 0: nothing to do; k = 0: every row is the empty fold 0.0
+    e8 = torch.empty(0, dtype=torch.int8, device="cuda")
+    ef = torch.empty(0, dtype=torch.float32, device="cuda")
+    L.dequantGemvQ8(e8, ef, 32, e8, ef, ef)
+    y = dev_y(4)
+    L.dequantGemv(e8, ef, 32, ef, y)
+    assert np.array_equal(to_host(y), np.zeros(4, F))
+
+
+def test_unaligned_device_pointers_take_plain_staging():
+    """A weight view starting 1 byte into an allocation cannot use bulk
+    copies; the plain-load staging must give the same bits."""
+    M, K = 65, 512
+    w = weights(5, M * K)
+    x = acts(5, K)
+    s8 = O.calibrateSymmetric(w, 32, 127.0)
+    q8 = O.quantize(w, s8, 32, "i8")
+    big = torch.zeros(q8.size + 1, dtype=torch.int8, device="cuda")
+    big[1:] = torch.from_numpy(q8).cuda()
+    sd, xd = to_dev(s8, x)
+    y = dev_y(M)
+    L.dequantGemv(big[1:], sd, 32, xd, y)
+    assert_bits(to_host(y), O.dequantGemv(q8, s8, 32, x))
