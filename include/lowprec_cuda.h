@@ -53,6 +53,9 @@ int lp_version(void);
 /* Message for a status code (static string). */
 const char *lp_status_string(int status);
 
+/* Text of the last CUDA error this thread's calls hit ("" if none). */
+const char *lp_last_error_detail(void);
+
 /* Synchronise the current device, then return (and clear) the first error a
  * kernel of this library recorded on it (LP_OK if none).  Device-side
  * failures never trap; they are reported here. */

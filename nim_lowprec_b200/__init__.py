@@ -2,7 +2,7 @@
 dequant-GEMV/GEMM hot path behind the reference's own kernel API.
 
 The kernels live in liblowprec_cuda.so (built from csrc/ by
-``python -m nim_lowprec_b200.build``); this package binds its C ABI and
+``python nim_lowprec_b200/build.py``); this package binds its C ABI and
 mirrors the reference's Nim procs.  There is no CPU fallback: importing the
 API without the built library raises.
 """

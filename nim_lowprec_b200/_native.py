@@ -78,7 +78,13 @@ def header_symbols(path: str = HEADER):
 
 class NativeError(RuntimeError):
     def __init__(self, status: int, where: str):
-        super().__init__(f"{where}: {status_string(status)} (status {status})")
+        detail = ""
+        if status == LP_ERR_CUDA:
+            try:
+                detail = " [" + lib().lp_last_error_detail().decode() + "]"
+            except Exception:  # pragma: no cover
+                pass
+        super().__init__(f"{where}: {status_string(status)} (status {status}){detail}")
         self.status = status
 
 
@@ -91,7 +97,7 @@ def lib():
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise ImportError(
-                f"{LIB_PATH} is missing: build it with `python -m nim_lowprec_b200.build` "
+                f"{LIB_PATH} is missing: build it with `python nim_lowprec_b200/build.py` "
                 "(this package has no CPU fallback)")
         L = ctypes.CDLL(LIB_PATH)
         for name, sig in SIGNATURES.items():
@@ -102,6 +108,8 @@ def lib():
         L.lp_version.argtypes = []
         L.lp_status_string.restype = ctypes.c_char_p
         L.lp_status_string.argtypes = [ctypes.c_int]
+        L.lp_last_error_detail.restype = ctypes.c_char_p
+        L.lp_last_error_detail.argtypes = []
         L.lp_device_error.restype = ctypes.c_int
         L.lp_device_error.argtypes = []
         _lib = L

@@ -1,6 +1,8 @@
 """Build liblowprec_cuda.so in-tree with nvcc for sm_100a.
 
-    python -m nim_lowprec_b200.build [--force]
+    python nim_lowprec_b200/build.py [--force] [-v]
+
+(Run it by path: importing the package itself loads the built library.)
 
 Every .cu under csrc/ is compiled for `sm_100a` only (the library uses
 tcgen05/TMA-era PTX: bulk copies, mbarrier waits, f32x2 arithmetic) and

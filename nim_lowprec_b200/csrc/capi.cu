@@ -5,6 +5,7 @@
 // (e.g. simd/dequant.nim:221-226, 768-771, 1392-1400).  A failed rule
 // returns LP_ERR_SHAPE before anything is launched.
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -29,6 +30,16 @@ const DeviceInfo& device_info() {
     cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
   });
   return info[slot];
+}
+
+namespace {
+thread_local char t_detail[256] = "";
+}
+
+const char* t_detail_ptr() { return t_detail; }
+
+void note_cuda_error(cudaError_t e) {
+  snprintf(t_detail, sizeof(t_detail), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
 }  // namespace lp
@@ -93,6 +104,8 @@ const char* lp_status_string(int s) {
     default: return "unknown status";
   }
 }
+
+const char* lp_last_error_detail(void) { return lp::t_detail_ptr(); }
 
 int lp_device_error(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LP_ERR_CUDA;
@@ -384,8 +397,8 @@ int stage_in(std::vector<Seg*> segs) {
     hs.cap = 0;
     hs.stream = nullptr;
     hs.device = dev;
-    if (cudaStreamCreateWithFlags(&hs.stream, cudaStreamNonBlocking) != cudaSuccess)
-      return LP_ERR_CUDA;
+    const cudaError_t e = cudaStreamCreateWithFlags(&hs.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return lp::cuda_status(e);
   }
   size_t total = 0;
   for (Seg* s : segs) total += (s->bytes + 255) & ~size_t(255);

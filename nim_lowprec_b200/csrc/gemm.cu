@@ -162,8 +162,10 @@ int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, co
   static bool attr_set[kMaxDevices] = {};
   const DeviceInfo& di = device_info();
   if (!attr_set[di.ordinal % kMaxDevices]) {
-    cudaFuncSetAttribute(k_gemm_dp4a, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         di.max_smem_optin);
+    cudaFuncAttributes fa;
+    int lim = di.max_smem_optin;
+    if (cudaFuncGetAttributes(&fa, k_gemm_dp4a) == cudaSuccess) lim -= static_cast<int>(fa.sharedSizeBytes);
+    cudaFuncSetAttribute(k_gemm_dp4a, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     attr_set[di.ordinal % kMaxDevices] = true;
   }
   if (a.k == 0) {

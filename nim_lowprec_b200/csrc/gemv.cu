@@ -56,6 +56,20 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   if (p.gpr == 0)  // no groups: every row is the empty fold, 0.0
     return cuda_status(cudaMemsetAsync(p.y, 0, static_cast<size_t>(p.m) * sizeof(float), st));
   const DeviceInfo& di = device_info();
+  auto kern = gemv_kernel<Fmt, kNcw>;
+  // Dynamic shared memory may use the opt-in maximum minus the kernel's
+  // static shared memory; set once per device.
+  static int dyn_max[kMaxDevices];
+  static std::once_flag once[kMaxDevices];
+  const int slot = di.ordinal % kMaxDevices;
+  std::call_once(once[slot], [&] {
+    cudaFuncAttributes fa;
+    int lim = di.max_smem_optin;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) lim -= static_cast<int>(fa.sharedSizeBytes);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim) != cudaSuccess)
+      lim = 48 * 1024 - 256;
+    dyn_max[slot] = lim;
+  });
   const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
   p.rt = std::max(1, std::min({kRtCap, kStageTarget / std::max(row_total, 1), p.m}));
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
@@ -64,7 +78,7 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.tstride = round_up(std::max(p.gpr, 1), 32) + 4;
   const int terms_bytes = 2 * p.rt * p.tstride * 4;
   const int fixed = round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
-  const int budget = di.max_smem_optin - 1024;
+  const int budget = dyn_max[slot];
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
   p.stages = std::min(kMaxStages, (budget - fixed) / std::max(per_stage, 1));
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations or rows too large for shared
@@ -77,14 +91,9 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
   p.off_b = round_up(p.off_t + terms_bytes, 16);
   const int smem = p.off_b + 8 * (2 * p.stages + 4);
-  auto kern = gemv_kernel<Fmt, kNcw>;
-  static std::once_flag once[kMaxDevices];
-  std::call_once(once[di.ordinal % kMaxDevices], [&] {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, di.max_smem_optin);
-  });
   const int grid = std::min(p.m, di.sm_count);
   kern<<<grid, 32 * (kNcw + 2), smem, st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? LP_OK : LP_ERR_CUDA;
+  return cuda_status(cudaGetLastError());
 }
 
 template int launch_gemv<FmtI8>(GemvParams, cudaStream_t);

@@ -53,6 +53,13 @@ int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, co
 // error words of the translation units whose kernels wait (read + clear)
 unsigned int take_error_gemv();
 
-inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? LP_OK : LP_ERR_CUDA; }
+// Records the CUDA error text for lp_last_error_detail() and maps to a status.
+void note_cuda_error(cudaError_t e);
+const char* t_detail_ptr();
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return LP_OK;
+  note_cuda_error(e);
+  return LP_ERR_CUDA;
+}
 
 }  // namespace lp

@@ -1,0 +1,145 @@
+## nim_lowprec_cuda -- drop-in replacements for nim-lowprec's fused
+## dequant-GEMV/GEMM procs, running on a B200 through liblowprec_cuda.so.
+##
+## Same proc names, argument order and meaning as the reference's
+## `simd/dequant` and `ggml` modules (src/nim_lowprec/simd/dequant.nim,
+## ggml.nim); an `openArray[T]` crosses the C ABI as (pointer, length), which is
+## exactly how the C ABI in include/lowprec_cuda.h takes it.  These forms take
+## HOST arrays and block (the `lph_*` entry points): inputs are copied to the
+## device, the kernel runs, `y` is copied back.  A failed shape precondition
+## raises AssertionDefect, like the reference's `assert`.
+##
+## Status: written against the C ABI, not compiled here (no Nim toolchain in
+## this build environment).  Usage mirrors the reference:
+##
+##   import nim_lowprec/[intx, ggml]
+##   import nim_lowprec_cuda
+##   dequantGemvQ8(wq, wScales, 32, xq, xScales, y)
+##
+## Types come from the reference modules (I8, BlockQ8_0, BlockQ4_0), which
+## are layout-compatible with the C ABI (34 / 18-byte blocks).
+
+import nim_lowprec/[intx, ggml]
+
+const lpLib* {.strdefine.} = "liblowprec_cuda.so"
+
+type LowprecCudaError* = object of CatchableError
+
+proc lph_dequant_gemv(wq: pointer, wqLen: int64, scales: pointer, scalesLen: int64,
+    groupSize: int64, x: pointer, xLen: int64, y: pointer, yLen: int64): cint {.
+    importc, dynlib: lpLib.}
+proc lph_dequant_gemv_i4(w: pointer, wLen: int64, scales: pointer, scalesLen: int64,
+    groupSize: int64, x: pointer, xLen: int64, y: pointer, yLen: int64): cint {.
+    importc, dynlib: lpLib.}
+proc lph_dequant_gemv_f4(w: pointer, wLen: int64, scales: pointer, scalesLen: int64,
+    groupSize: int64, x: pointer, xLen: int64, y: pointer, yLen: int64): cint {.
+    importc, dynlib: lpLib.}
+proc lph_dequant_gemv_q8_0(w: pointer, wLen: int64, bpr: int64, x: pointer, xLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequant_gemv_q4_0(w: pointer, wLen: int64, bpr: int64, x: pointer, xLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequant_gemv_q8(wq: pointer, wqLen: int64, ws: pointer, wsLen: int64, gs: int64,
+    xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, y: pointer, yLen: int64): cint {.
+    importc, dynlib: lpLib.}
+proc lph_dequant_gemv_i4q8(w: pointer, wLen: int64, ws: pointer, wsLen: int64, gs: int64,
+    xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, y: pointer, yLen: int64): cint {.
+    importc, dynlib: lpLib.}
+proc lph_dequant_gemv_q8_0q8(w: pointer, wLen: int64, bpr: int64, xq: pointer, xqLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequant_gemv_q4_0q8(w: pointer, wLen: int64, bpr: int64, xq: pointer, xqLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequant_gemm_q8(wq: pointer, wqLen: int64, ws: pointer, wsLen: int64, gs: int64,
+    xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, n: int64, y: pointer,
+    yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequant_gemm_i4q8(w: pointer, wLen: int64, ws: pointer, wsLen: int64, gs: int64,
+    xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, n: int64, y: pointer,
+    yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_quantize_q8_0_batch(src: pointer, srcLen: int64, blocks: pointer,
+    blocksLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_quantize_q4_0_batch(src: pointer, srcLen: int64, blocks: pointer,
+    blocksLen: int64): cint {.importc, dynlib: lpLib.}
+proc lp_status_string(status: cint): cstring {.importc, dynlib: lpLib.}
+
+template base[T](a: openArray[T]): pointer =
+  (if a.len > 0: cast[pointer](unsafeAddr a[0]) else: nil)
+
+proc check(status: cint, where: string) =
+  if status == 0: return
+  if status == 1:  # LP_ERR_SHAPE: the reference's entry asserts
+    raise newException(AssertionDefect, where & ": " & $lp_status_string(status))
+  raise newException(LowprecCudaError, where & ": " & $lp_status_string(status))
+
+# ---- fp32-activation fused GEMVs (simd/dequant.nim:210-622) ----
+
+proc dequantGemv*(wq: openArray[I8], scales: openArray[float32], groupSize: int,
+    x: openArray[float32], y: var openArray[float32]) =
+  check(lph_dequant_gemv(base(wq), wq.len, base(scales), scales.len, groupSize,
+      base(x), x.len, base(y), y.len), "dequantGemv")
+
+proc dequantGemvI4*(wpacked: openArray[byte], scales: openArray[float32], groupSize: int,
+    x: openArray[float32], y: var openArray[float32]) =
+  check(lph_dequant_gemv_i4(base(wpacked), wpacked.len, base(scales), scales.len,
+      groupSize, base(x), x.len, base(y), y.len), "dequantGemvI4")
+
+proc dequantGemvF4*(wpacked: openArray[byte], scales: openArray[float32], groupSize: int,
+    x: openArray[float32], y: var openArray[float32]) =
+  check(lph_dequant_gemv_f4(base(wpacked), wpacked.len, base(scales), scales.len,
+      groupSize, base(x), x.len, base(y), y.len), "dequantGemvF4")
+
+proc dequantGemvQ8_0*(w: openArray[BlockQ8_0], blocksPerRow: int, x: openArray[float32],
+    y: var openArray[float32]) =
+  check(lph_dequant_gemv_q8_0(base(w), w.len, blocksPerRow, base(x), x.len, base(y),
+      y.len), "dequantGemvQ8_0")
+
+proc dequantGemvQ4_0*(w: openArray[BlockQ4_0], blocksPerRow: int, x: openArray[float32],
+    y: var openArray[float32]) =
+  check(lph_dequant_gemv_q4_0(base(w), w.len, blocksPerRow, base(x), x.len, base(y),
+      y.len), "dequantGemvQ4_0")
+
+# ---- int8-activation GEMVs (simd/dequant.nim:753-1365) ----
+
+proc dequantGemvQ8*(wq: openArray[I8], wScales: openArray[float32], groupSize: int,
+    xq: openArray[I8], xScales: openArray[float32], y: var openArray[float32]) =
+  check(lph_dequant_gemv_q8(base(wq), wq.len, base(wScales), wScales.len, groupSize,
+      base(xq), xq.len, base(xScales), xScales.len, base(y), y.len), "dequantGemvQ8")
+
+proc dequantGemvI4Q8*(wpacked: openArray[byte], wScales: openArray[float32],
+    groupSize: int, xq: openArray[I8], xScales: openArray[float32],
+    y: var openArray[float32]) =
+  check(lph_dequant_gemv_i4q8(base(wpacked), wpacked.len, base(wScales), wScales.len,
+      groupSize, base(xq), xq.len, base(xScales), xScales.len, base(y), y.len),
+      "dequantGemvI4Q8")
+
+proc dequantGemvQ8_0Q8*(w: openArray[BlockQ8_0], blocksPerRow: int,
+    xq: openArray[BlockQ8_0], y: var openArray[float32]) =
+  check(lph_dequant_gemv_q8_0q8(base(w), w.len, blocksPerRow, base(xq), xq.len, base(y),
+      y.len), "dequantGemvQ8_0Q8")
+
+proc dequantGemvQ4_0Q8*(w: openArray[BlockQ4_0], blocksPerRow: int,
+    xq: openArray[BlockQ8_0], y: var openArray[float32]) =
+  check(lph_dequant_gemv_q4_0q8(base(w), w.len, blocksPerRow, base(xq), xq.len, base(y),
+      y.len), "dequantGemvQ4_0Q8")
+
+# ---- multi-column GEMM (simd/dequant.nim:1382-1583) ----
+
+proc dequantGemmQ8*(wq: openArray[I8], wScales: openArray[float32], groupSize: int,
+    xq: openArray[I8], xScales: openArray[float32], n: int, y: var openArray[float32]) =
+  check(lph_dequant_gemm_q8(base(wq), wq.len, base(wScales), wScales.len, groupSize,
+      base(xq), xq.len, base(xScales), xScales.len, n, base(y), y.len), "dequantGemmQ8")
+
+proc dequantGemmI4Q8*(wpacked: openArray[byte], wScales: openArray[float32],
+    groupSize: int, xq: openArray[I8], xScales: openArray[float32], n: int,
+    y: var openArray[float32]) =
+  check(lph_dequant_gemm_i4q8(base(wpacked), wpacked.len, base(wScales), wScales.len,
+      groupSize, base(xq), xq.len, base(xScales), xScales.len, n, base(y), y.len),
+      "dequantGemmI4Q8")
+
+# ---- encoders (simd/dequant.nim:1624-1715) ----
+
+proc quantizeQ8_0Batch*(src: openArray[float32], blocks: var openArray[BlockQ8_0]) =
+  check(lph_quantize_q8_0_batch(base(src), src.len, base(blocks), blocks.len),
+      "quantizeQ8_0Batch")
+
+proc quantizeQ4_0Batch*(src: openArray[float32], blocks: var openArray[BlockQ4_0]) =
+  check(lph_quantize_q4_0_batch(base(src), src.len, base(blocks), blocks.len),
+      "quantizeQ4_0Batch")

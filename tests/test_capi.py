@@ -19,7 +19,8 @@ def test_library_exports_every_header_symbol():
 
 def test_every_header_symbol_has_a_prototype():
     syms = set(N.header_symbols())
-    bound = set(N.SIGNATURES) | {"lp_version", "lp_status_string", "lp_device_error"}
+    bound = set(N.SIGNATURES) | {"lp_version", "lp_status_string", "lp_device_error",
+                                  "lp_last_error_detail"}
     assert syms <= bound
 
 
