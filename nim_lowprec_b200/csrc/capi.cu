@@ -83,6 +83,9 @@ GemvParams base(const void* w, const float* ws, const void* x, const float* xs, 
 
 constexpr int64_t kIntMax = 0x7fffffff;
 
+// A pointer may be null only when its array is empty.
+inline bool bad(const void* p, int64_t len) { return len > 0 && p == nullptr; }
+
 bool fits(int64_t m, int64_t k) { return m >= 0 && k >= 0 && m <= kIntMax && k <= kIntMax; }
 
 }  // namespace
@@ -126,7 +129,7 @@ static int gemv_f32_group(int fmt, const void* w, int64_t w_len, const float* sc
   LP_REQUIRE(k % gs == 0);
   if (packed) LP_REQUIRE(k % 2 == 0);
   LP_REQUIRE(w_len == m * rb && scales_len == m * gpr);
-  if (m && (!w || !y || (k && (!x || !scales)))) return LP_ERR_ARG;
+  if (bad(w, w_len) || bad(scales, scales_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   GemvParams p = base(w, scales, x, nullptr, y, m, k, gs, gpr, rb);
   switch (fmt) {
@@ -157,7 +160,7 @@ static int gemv_f32_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, co
   const int64_t m = y_len;
   LP_REQUIRE(bpr >= 0 && fits(m, bpr * 32));
   LP_REQUIRE(w_len == m * bpr && x_len == bpr * 32);
-  if (m && (!w || !y || (bpr && !x))) return LP_ERR_ARG;
+  if (bad(w, w_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   const int64_t rb = bpr * (q4 ? 18 : 34);
   GemvParams p = base(w, nullptr, x, nullptr, y, m, bpr * 32, 32, bpr, rb);
@@ -185,7 +188,8 @@ static int gemv_q8_group(int i4, const void* w, int64_t w_len, const float* ws, 
   LP_REQUIRE(k % gs == 0);
   if (i4) LP_REQUIRE(k % 2 == 0);
   LP_REQUIRE(w_len == m * rb && ws_len == m * gpr && xs_len == gpr);
-  if (m && (!w || !y || (k && (!xq || !ws || !xs)))) return LP_ERR_ARG;
+  if (bad(w, w_len) || bad(ws, ws_len) || bad(xq, xq_len) || bad(xs, xs_len) || bad(y, y_len))
+    return LP_ERR_ARG;
   LP_VALIDATED();
   GemvParams p = base(w, ws, xq, xs, y, m, k, gs, gpr, rb);
   return i4 ? lp::launch_gemv<lp::FmtI4Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8>(p, S(st));
@@ -211,7 +215,7 @@ static int gemv_q8_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, con
   const int64_t m = y_len;
   LP_REQUIRE(bpr >= 0 && fits(m, bpr * 32));
   LP_REQUIRE(w_len == m * bpr && xq_len == bpr);
-  if (m && (!w || !y || (bpr && !xq))) return LP_ERR_ARG;
+  if (bad(w, w_len) || bad(xq, xq_len) || bad(y, y_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   const int64_t rb = bpr * (q4 ? 18 : 34);
   GemvParams p = base(w, nullptr, xq, nullptr, y, m, bpr * 32, 32, bpr, rb);
@@ -241,7 +245,8 @@ static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, in
   if (i4) LP_REQUIRE(k % 2 == 0);
   LP_REQUIRE(w_len == m * rb && ws_len == m * gpr && xq_len == n * k && xs_len == n * gpr &&
              y_len == m * n);
-  if (m && (!w || !y || (k && (!xq || !ws || !xs)))) return LP_ERR_ARG;
+  if (bad(w, w_len) || bad(ws, ws_len) || bad(xq, xq_len) || bad(xs, xs_len) || bad(y, y_len))
+    return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_gemm(static_cast<const uint8_t*>(w), i4, ws, gs, xq, xs, n, y, m, k, S(st));
 }
@@ -266,7 +271,7 @@ int lp_dequant_gemm_i4q8(const uint8_t* wp, int64_t wp_len, const float* w_scale
 int lp_quantize_q8_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len,
                            lp_stream_t stream) {
   LP_REQUIRE(src_len >= 0 && src_len == blocks_len * 32);
-  if (src_len && (!src || !blocks)) return LP_ERR_ARG;
+  if (bad(src, src_len) || bad(blocks, blocks_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_q8_0(src, src_len, static_cast<uint8_t*>(blocks), nullptr, nullptr,
                                   S(stream));
@@ -275,7 +280,7 @@ int lp_quantize_q8_0_batch(const float* src, int64_t src_len, void* blocks, int6
 int lp_quantize_q4_0_batch(const float* src, int64_t src_len, void* blocks, int64_t blocks_len,
                            lp_stream_t stream) {
   LP_REQUIRE(src_len >= 0 && src_len == blocks_len * 32);
-  if (src_len && (!src || !blocks)) return LP_ERR_ARG;
+  if (bad(src, src_len) || bad(blocks, blocks_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_q4_0(src, src_len, static_cast<uint8_t*>(blocks), S(stream));
 }
@@ -283,7 +288,7 @@ int lp_quantize_q4_0_batch(const float* src, int64_t src_len, void* blocks, int6
 int lp_quantize_q8_0_split(const float* src, int64_t src_len, int8_t* qs, int64_t qs_len,
                            float* d, int64_t d_len, lp_stream_t stream) {
   LP_REQUIRE(src_len >= 0 && src_len % 32 == 0 && qs_len == src_len && d_len == src_len / 32);
-  if (src_len && (!src || !qs || !d)) return LP_ERR_ARG;
+  if (bad(src, src_len) || bad(qs, qs_len) || bad(d, d_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_q8_0(src, src_len, nullptr, qs, d, S(stream));
 }
@@ -294,7 +299,7 @@ int lp_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_
                       int64_t group_size, int8_t* dst, int64_t dst_len, lp_stream_t stream) {
   LP_REQUIRE(x_len >= 0 && x_len == dst_len);
   LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, group_size) : 0));
-  if (x_len && (!x || !scales || !dst)) return LP_ERR_ARG;
+  if (bad(x, x_len) || bad(scales, scales_len) || bad(dst, dst_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_batch(x, x_len, scales, group_size > 0 ? group_size : 0, dst,
                                    S(stream));
@@ -305,7 +310,7 @@ int lp_calibrate_symmetric(const float* x, int64_t x_len, int64_t group_size, fl
   LP_REQUIRE(x_len >= 0);
   const int64_t gs = group_size > 0 ? group_size : std::max<int64_t>(x_len, 1);
   LP_REQUIRE(scales_len == num_groups(x_len, gs) || (group_size <= 0 && scales_len == 1));
-  if (scales_len && (!scales || (x_len && !x))) return LP_ERR_ARG;
+  if (bad(x, x_len) || bad(scales, scales_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_calibrate(x, x_len, gs, qmax, 0, 0, scales, scales_len, S(stream));
 }
@@ -313,7 +318,7 @@ int lp_calibrate_symmetric(const float* x, int64_t x_len, int64_t group_size, fl
 int lp_calibrate_mx(const float* x, int64_t x_len, int64_t block_size, int32_t elem_emax,
                     float* scales, int64_t scales_len, lp_stream_t stream) {
   LP_REQUIRE(x_len >= 0 && block_size > 0 && scales_len == num_groups(x_len, block_size));
-  if (scales_len && (!scales || (x_len && !x))) return LP_ERR_ARG;
+  if (bad(x, x_len) || bad(scales, scales_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_calibrate(x, x_len, block_size, 0.0f, elem_emax, 1, scales, scales_len,
                               S(stream));
@@ -324,7 +329,7 @@ int lp_quantize_i4_packed(const float* x, int64_t x_len, const float* scales, in
                           lp_stream_t stream) {
   LP_REQUIRE(x_len >= 0 && packed_len == (x_len + 1) / 2);
   LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, group_size) : 0));
-  if (x_len && (!x || !scales || !packed)) return LP_ERR_ARG;
+  if (bad(x, x_len) || bad(scales, scales_len) || bad(packed, packed_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_packed(x, x_len, scales, group_size > 0 ? group_size : 0, 0, packed,
                                     S(stream));
@@ -335,7 +340,7 @@ int lp_quantize_f4_packed(const float* x, int64_t x_len, const float* scales, in
                           lp_stream_t stream) {
   LP_REQUIRE(x_len >= 0 && packed_len == (x_len + 1) / 2);
   LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, block_size) : 0));
-  if (x_len && (!x || !scales || !packed)) return LP_ERR_ARG;
+  if (bad(x, x_len) || bad(scales, scales_len) || bad(packed, packed_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_quantize_packed(x, x_len, scales, block_size > 0 ? block_size : 0, 1, packed,
                                     S(stream));
@@ -344,7 +349,7 @@ int lp_quantize_f4_packed(const float* x, int64_t x_len, const float* scales, in
 int lp_dequantize_q8_0_batch(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
                              lp_stream_t stream) {
   LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 32);
-  if (blocks_len && (!blocks || !dst)) return LP_ERR_ARG;
+  if (bad(blocks, blocks_len) || bad(dst, dst_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_dequantize_blocks(static_cast<const uint8_t*>(blocks), blocks_len, 0, dst,
                                       S(stream));
@@ -353,7 +358,7 @@ int lp_dequantize_q8_0_batch(const void* blocks, int64_t blocks_len, float* dst,
 int lp_dequantize_q4_0_batch(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
                              lp_stream_t stream) {
   LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 32);
-  if (blocks_len && (!blocks || !dst)) return LP_ERR_ARG;
+  if (bad(blocks, blocks_len) || bad(dst, dst_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   return lp::launch_dequantize_blocks(static_cast<const uint8_t*>(blocks), blocks_len, 1, dst,
                                       S(stream));

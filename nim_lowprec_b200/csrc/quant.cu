@@ -88,14 +88,16 @@ __global__ void k_quantize_q4_0(const float* __restrict__ src, int64_t nblocks,
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q = static_cast<int>(roundf(__fmul_rn(v, id))) + 8;
     q = min(max(q, 0), 15);
+    // byte i (i < 16) = q[i] | q[i+16] << 4; the 18-byte block is written as
+    // nine 2-byte-aligned halfwords: d, then qs byte pairs.
     const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
-    uint8_t* blk = blocks + b * 18;
-    if (lane < 16) blk[2 + lane] = static_cast<uint8_t>(q | (qhi << 4));
-    if (lane == 0) {
-      const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-      blk[0] = static_cast<uint8_t>(dh & 0xFF);
-      blk[1] = static_cast<uint8_t>(dh >> 8);
-    }
+    const uint32_t byte = static_cast<uint32_t>(q | (qhi << 4)) & 0xFFu;
+    const uint32_t lo = __shfl_sync(0xffffffffu, byte, (2 * lane - 2) & 31);
+    const uint32_t hi = __shfl_sync(0xffffffffu, byte, (2 * lane - 1) & 31);
+    const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+    unsigned short* blk = reinterpret_cast<unsigned short*>(blocks + b * 18);
+    if (lane == 0) blk[0] = dh;
+    else if (lane < 9) blk[lane] = static_cast<unsigned short>(lo | (hi << 8));
   }
 }
 
