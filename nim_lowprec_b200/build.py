@@ -26,7 +26,11 @@ OBJDIR = os.path.join(HERE, "_build")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+# -fmad=false: ptxas may otherwise contract a multiply feeding an add into one
+# FMA even across the explicit mul.rn/add.rn f32x2 pairs of the bit-exact
+# paths (measured on sm_100a); this is the device-side twin of the
+# reference's -ffp-contract=off (simd/dequant.nim:36).
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I", CSRC, "-I", INCLUDE]
 
 
