@@ -78,6 +78,7 @@ GemvParams base(const void* w, const float* ws, const void* x, const float* xs, 
   p.gs = static_cast<int>(gs);
   p.gpr = static_cast<int>(gpr);
   p.row_bytes = static_cast<int>(row_bytes);
+  p.neg_zero = -0.0f;
   return p;
 }
 

@@ -50,6 +50,7 @@ struct GemvParams {
   int x_bytes;        // shared bytes for the staged activations
   int off_w, off_s, off_t, off_b;  // shared-memory offsets
   int stage_w_bytes, stage_s_bytes;
+  float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
 };
 
 constexpr int kMaxRt = 16;

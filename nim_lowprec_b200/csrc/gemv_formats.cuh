@@ -111,13 +111,14 @@ struct FmtI8 : StageXF32 {
       const uint32_t B[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
       const uint64_t bias = pk(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
       uint64_t acc = pk(0.0f, 0.0f);
+      const uint64_t nz = pk(p.neg_zero, p.neg_zero);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint32_t ua = A[j] ^ 0x80808080u, ub = B[j] ^ 0x80808080u;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
           const uint64_t wv = add2(magic_pair(ua, ub, b), bias);
-          acc = add2(acc, mul2(wv, xp.x2[4 * j + b]));
+          acc = add2(acc, mul2_rn(wv, xp.x2[4 * j + b], nz));
         }
       }
       float pa_, pb_;
@@ -157,6 +158,7 @@ struct FmtI4 : StageXF32 {
       const uint32_t B[4] = {bq.x, bq.y, bq.z, bq.w};
       const uint64_t bias = pk(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
       uint64_t acc = pk(0.0f, 0.0f);
+      const uint64_t nz = pk(p.neg_zero, p.neg_zero);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         // n ^ 8 = value + 8 for a two's-complement nibble n
@@ -168,9 +170,9 @@ struct FmtI4 : StageXF32 {
         for (int b = 0; b < 4; ++b) {
           const int c = 8 * j + 2 * b;  // even column: low nibble of byte 4j+b
           const uint64_t we = add2(magic_pair(loA, loB, b), bias);
-          acc = add2(acc, mul2(we, xp.x2[c]));
+          acc = add2(acc, mul2_rn(we, xp.x2[c], nz));
           const uint64_t wo = add2(magic_pair(hiA, hiB, b), bias);
-          acc = add2(acc, mul2(wo, xp.x2[c + 1]));
+          acc = add2(acc, mul2_rn(wo, xp.x2[c + 1], nz));
         }
       }
       float pa_, pb_;
@@ -222,6 +224,7 @@ struct FmtF4 : StageXF32 {
       const uint32_t B[4] = {bq.x, bq.y, bq.z, bq.w};
       const uint64_t bias = pk(-8388620.0f, -8388620.0f);  // -(2^23 + 12)
       uint64_t acc = pk(0.0f, 0.0f);
+      const uint64_t nz = pk(p.neg_zero, p.neg_zero);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
 #pragma unroll
@@ -231,7 +234,7 @@ struct FmtF4 : StageXF32 {
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const uint64_t wv = add2(magic_pair(ua, ub, b), bias);
-            acc = add2(acc, mul2(wv, xp.x2[8 * j + 4 * h + b]));
+            acc = add2(acc, mul2_rn(wv, xp.x2[8 * j + 4 * h + b], nz));
           }
         }
       }
@@ -270,13 +273,14 @@ struct FmtQ8_0 : StageXF32 {
     load_q8_0(wB + g * 34, dB, B);
     const uint64_t bias = pk(-8388736.0f, -8388736.0f);
     uint64_t acc = pk(0.0f, 0.0f);
+      const uint64_t nz = pk(p.neg_zero, p.neg_zero);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t ua = A[j] ^ 0x80808080u, ub = B[j] ^ 0x80808080u;
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const uint64_t wv = add2(magic_pair(ua, ub, b), bias);
-        acc = add2(acc, mul2(wv, xp.x2[4 * j + b]));
+        acc = add2(acc, mul2_rn(wv, xp.x2[4 * j + b], nz));
       }
     }
     float pa_, pb_;
@@ -303,6 +307,7 @@ struct FmtQ4_0 : StageXF32 {
     load_q4_0(wB + g * 18, dB, B);
     const uint64_t bias = pk(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
     uint64_t acc = pk(0.0f, 0.0f);
+      const uint64_t nz = pk(p.neg_zero, p.neg_zero);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t loA = A[j] & 0x0F0F0F0Fu, hiA = (A[j] >> 4) & 0x0F0F0F0Fu;
@@ -311,9 +316,9 @@ struct FmtQ4_0 : StageXF32 {
       for (int b = 0; b < 4; ++b) {
         const int i = 4 * j + b;
         const uint64_t wl = add2(magic_pair(loA, loB, b), bias);
-        acc = add2(acc, mul2(wl, xp.x2[i]));
+        acc = add2(acc, mul2_rn(wl, xp.x2[i], nz));
         const uint64_t wh = add2(magic_pair(hiA, hiB, b), bias);
-        acc = add2(acc, mul2(wh, xp.x2[i + 16]));
+        acc = add2(acc, mul2_rn(wh, xp.x2[i + 16], nz));
       }
     }
     float pa_, pb_;

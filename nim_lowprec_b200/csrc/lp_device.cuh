@@ -121,6 +121,17 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+// Rounded packed product a*b computed as fma(a, b, z) with z = -0.0 supplied
+// at run time (a kernel parameter).  fma(a, b, -0) is exactly round(a*b),
+// signed zeros included, and because the compiler cannot see that z is zero
+// it cannot merge this product with the add that consumes it -- it does
+// merge mul.rn.f32x2 into a following add.rn.f32x2 (measured on sm_100a),
+// which would turn the reference's two roundings into one.
+__device__ __forceinline__ uint64_t mul2_rn(uint64_t a, uint64_t b, uint64_t z) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(z));
+  return d;
+}
 __device__ __forceinline__ float fmul(float a, float b) {
   float d;
   asm("mul.rn.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
