@@ -78,7 +78,11 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.tstride = round_up(std::max(p.gpr, 1), 32) + 4;
   const int terms_bytes = 2 * p.rt * p.tstride * 4;
   const int fixed = round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
-  const int budget = dyn_max[slot];
+  // Two CTAs per SM when they fit (twice the consumer warps to hide the
+  // fp32 chains' latency), else one.
+  const int two_cta = (dyn_max[slot] - 1024) / 2 - 1024;
+  int budget = dyn_max[slot];
+  if (fixed + 2 * (p.stage_w_bytes + p.stage_s_bytes) <= two_cta) budget = two_cta;
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
   p.stages = std::min(kMaxStages, (budget - fixed) / std::max(per_stage, 1));
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations or rows too large for shared
@@ -91,9 +95,22 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
   p.off_b = round_up(p.off_t + terms_bytes, 16);
   const int smem = p.off_b + 8 * (2 * p.stages + 4);
-  const int grid = std::min(p.m, di.sm_count);
-  kern<<<grid, 32 * (kNcw + 2), smem, st>>>(p);
-  return cuda_status(cudaGetLastError());
+  const int ctas_per_sm = budget < dyn_max[slot] ? 2 : 1;
+  const int grid = std::min(p.m, di.sm_count * ctas_per_sm);
+  // Programmatic dependent launch: this grid may start while the previous
+  // kernel in the stream drains; it prefetches its weights at once and waits
+  // for that kernel (griddepcontrol.wait) before it reads x or writes y.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(32 * (kNcw + 2));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p));
 }
 
 template int launch_gemv<FmtI8>(GemvParams, cudaStream_t);

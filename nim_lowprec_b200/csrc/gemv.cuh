@@ -72,7 +72,7 @@ __device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, int
 
 // ----------------------------------------------------------- the kernel
 template <class Fmt, int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ volatile int s_abort;
   uint8_t* xsm = smem;
@@ -104,15 +104,18 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     s_abort = 0;
     mbar_fence_init();
   }
-  Fmt::stage_x(xsm, p, threadIdx.x, blockDim.x);
   __syncthreads();
   if (ntiles == 0) return;
 
   if (warp == 0) {
     // ------------------------------------------------------ producer
+    // Weights never come from the kernel this launch may overlap with (see
+    // launch_gemv), so the stream starts before the grid dependency is
+    // resolved; the activations wait for it in the consumer warps.
     const uint64_t pol = l2_evict_first();
     int issued = 0;
     for (int t = 0; t < ntiles; ++t) {
+      if (t == p.stages) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
       const int s = t % p.stages;
       if (t >= p.stages) {
         if (!mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, &s_abort)) break;
@@ -142,6 +145,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
       }
       ++issued;
     }
+    if (issued <= p.stages) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Drain: never leave the CTA with a bulk copy still landing in shared.
     if (p.bulk && lane == 0) {
       for (int t = max(0, issued - p.stages); t < issued; ++t)
@@ -194,8 +198,17 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     // ------------------------------------------------------ consumers
     const int ct = threadIdx.x - 64;
     constexpr int NC = NCW * 32;
+    // The activations (and y, written by the folder after these warps
+    // signal) may belong to the previous kernel in the stream.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    Fmt::stage_x(xsm, p, ct, NC);
+    asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
     Fmt f;
     f.init(p, xsm);
+    // Unit q = rp * gpr + g walks q = ct, ct + NC, ...; step it without a
+    // division per unit.
+    const int drp = NC / p.gpr, dg = NC - drp * p.gpr;
+    const int rp0 = ct / p.gpr, g0 = ct - rp0 * p.gpr;
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % p.stages;
       const int tb = t & 1;
@@ -209,10 +222,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
       const float* S = reinterpret_cast<const float*>(sts + s * p.stage_s_bytes);
       float* T = terms + tb * p.rt * p.tstride;
       const int npairs = (rows + 1) >> 1;
-      const int nunits = npairs * p.gpr;
-      for (int q = ct; q < nunits; q += NC) {
-        const int rp = q / p.gpr;
-        const int g = q - rp * p.gpr;
+      int g = g0;
+      for (int rp = rp0; rp < npairs;) {
         const int ra = 2 * rp;
         const int rb = min(ra + 1, rows - 1);
         float ta, tbv;
@@ -220,6 +231,12 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
                 S + rb * p.gpr, g, ta, tbv);
         T[ra * p.tstride + g] = ta;
         if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = tbv;
+        g += dg;
+        rp += drp;
+        if (g >= p.gpr) {
+          g -= p.gpr;
+          ++rp;
+        }
       }
       __syncwarp();
       if (lane == 0) {
