@@ -70,6 +70,72 @@ __device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, int
   }
 }
 
+// ------------------------------------------------------------- folds
+// Row folds in group order.  Terms come in 32 at a time, the next batch
+// loaded while the current one is added, so the add chain (the only true
+// dependency) never waits on shared-memory latency.
+__device__ __forceinline__ void load32(const float* T, int g, int g4, float4 (&v)[8]) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    v[k] = (g + 4 * k < g4) ? *reinterpret_cast<const float4*>(T + g + 4 * k)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// total = ((0 + t0) + t1) + ... (simd/dequant.nim:877 and kin)
+__device__ __forceinline__ float fold_serial(const float* T, int gpr) {
+  const int g4 = gpr & ~3;
+  float tot = 0.0f;
+  float4 a[8], b[8];
+  load32(T, 0, g4, a);
+  for (int g = 0; g < g4; g += 32) {
+    load32(T, g + 32, g4, b);
+    const int n4 = min(8, (g4 - g) >> 2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < n4) {
+        tot = fadd(tot, a[k].x);
+        tot = fadd(tot, a[k].y);
+        tot = fadd(tot, a[k].z);
+        tot = fadd(tot, a[k].w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = b[k];
+  }
+  for (int g = g4; g < gpr; ++g) tot = fadd(tot, T[g]);
+  return tot;
+}
+
+// lane[b & 3] += t_b, then (l0 + l1) + (l2 + l3) (simd/dequant.nim:1275-1286)
+__device__ __forceinline__ float fold_lanes4(const float* T, int gpr) {
+  const int g4 = gpr & ~3;
+  float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
+  float4 a[8], b[8];
+  load32(T, 0, g4, a);
+  for (int g = 0; g < g4; g += 32) {
+    load32(T, g + 32, g4, b);
+    const int n4 = min(8, (g4 - g) >> 2);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < n4) {
+        l0 = fadd(l0, a[k].x);
+        l1 = fadd(l1, a[k].y);
+        l2 = fadd(l2, a[k].z);
+        l3 = fadd(l3, a[k].w);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = b[k];
+  }
+  for (int g = g4; g < gpr; ++g) {
+    const int l = g & 3;
+    if (l == 0) l0 = fadd(l0, T[g]);
+    else if (l == 1) l1 = fadd(l1, T[g]);
+    else l2 = fadd(l2, T[g]);
+  }
+  return fadd(fadd(l0, l1), fadd(l2, l3));
+}
+
 // ----------------------------------------------------------- the kernel
 template <class Fmt, int NCW>
 __global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParams p) {
@@ -161,35 +227,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParam
       const int rows = min(p.rt, row_end - r0);
       if (lane < rows) {
         const float* T = terms + (tb * p.rt + lane) * p.tstride;
-        const int g4 = p.gpr & ~3;
-        if (Fmt::kFold == Fold::Serial) {
-          float tot = 0.0f;
-          for (int g = 0; g < g4; g += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(T + g);
-            tot = fadd(tot, v.x);
-            tot = fadd(tot, v.y);
-            tot = fadd(tot, v.z);
-            tot = fadd(tot, v.w);
-          }
-          for (int g = g4; g < p.gpr; ++g) tot = fadd(tot, T[g]);
-          p.y[r0 + lane] = tot;
-        } else {
-          float l0 = 0.0f, l1 = 0.0f, l2 = 0.0f, l3 = 0.0f;
-          for (int g = 0; g < g4; g += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(T + g);
-            l0 = fadd(l0, v.x);
-            l1 = fadd(l1, v.y);
-            l2 = fadd(l2, v.z);
-            l3 = fadd(l3, v.w);
-          }
-          for (int g = g4; g < p.gpr; ++g) {
-            const int l = g & 3;
-            if (l == 0) l0 = fadd(l0, T[g]);
-            else if (l == 1) l1 = fadd(l1, T[g]);
-            else l2 = fadd(l2, T[g]);
-          }
-          p.y[r0 + lane] = fadd(fadd(l0, l1), fadd(l2, l3));
-        }
+        const float out = Fmt::kFold == Fold::Serial ? fold_serial(T, p.gpr) : fold_lanes4(T, p.gpr);
+        p.y[r0 + lane] = out;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[tb]);
