@@ -20,10 +20,11 @@ unsigned int take_error_gemv() {
 
 namespace {
 
-constexpr int kNcw = 8;                 // consumer warps per CTA
-constexpr int kStageTarget = 32 * 1024; // bytes of weights+scales per stage
+constexpr int kNcw = 8;          // consumer warps per CTA (256 threads)
 constexpr int kMaxStages = 8;
-constexpr int kRtCap = 8;
+// Per-CTA shared-memory target: small enough that the next kernel's CTA fits
+// on the same SM under programmatic dependent launch.
+constexpr int kSmemTarget = 110 * 1024;
 
 template <class Fmt>
 int x_stage_bytes(const GemvParams& p);
@@ -58,7 +59,8 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   const DeviceInfo& di = device_info();
   auto kern = gemv_kernel<Fmt, kNcw>;
   // Dynamic shared memory may use the opt-in maximum minus the kernel's
-  // static shared memory; set once per device.
+  // static shared memory; set once per device.  Rows per CTA beyond
+  // kMaxRowsPerPass are processed in several passes.
   static int dyn_max[kMaxDevices];
   static std::once_flag once[kMaxDevices];
   const int slot = di.ordinal % kMaxDevices;
@@ -70,33 +72,40 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
       lim = 48 * 1024 - 256;
     dyn_max[slot] = lim;
   });
-  const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
-  p.rt = std::max(1, std::min({kRtCap, kStageTarget / std::max(row_total, 1), p.m}));
+  constexpr int NC = kNcw * 32;
+  const int gbytes = p.row_bytes / p.gpr + (Fmt::kScales ? 4 : 0);  // per group, rounded down
+  // Chunk width: a stage is SR x G groups with SR * G = 2 * NC, i.e. one
+  // row pair per consumer thread; narrower when a row has fewer groups.
+  p.G = std::min(gbytes <= 24 ? 64 : 32, round_up(p.gpr, 4));
+  p.SR = std::min(32, 2 * NC / p.G);    // rows per stage (one producer lane each)
+  const int rows_per_cta = (p.m + std::min(p.m, di.sm_count) - 1) / std::min(p.m, di.sm_count);
+  p.RP = std::min(kMaxRowsPerPass, rows_per_cta);
+  p.tstride = p.G + 4;
+  const int64_t slice = static_cast<int64_t>(p.G) * p.row_bytes / p.gpr;
+  p.slice_pitch = round_up(static_cast<int>(slice), 16);
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
-  p.stage_w_bytes = round_up(p.rt * p.row_bytes, 16);
-  p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 16) : 0;
-  p.tstride = round_up(std::max(p.gpr, 1), 32) + 4;
-  const int terms_bytes = 2 * p.rt * p.tstride * 4;
+  p.stage_w_bytes = p.SR * p.slice_pitch;
+  p.stage_s_bytes = Fmt::kScales ? p.SR * p.G * 4 : 0;
+  const int terms_bytes = 2 * p.RP * p.tstride * 4;
   const int fixed = round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
-  // Two CTAs per SM when they fit (twice the consumer warps to hide the
-  // fp32 chains' latency), else one.
-  const int two_cta = (dyn_max[slot] - 1024) / 2 - 1024;
-  int budget = dyn_max[slot];
-  if (fixed + 2 * (p.stage_w_bytes + p.stage_s_bytes) <= two_cta) budget = two_cta;
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  p.stages = std::min(kMaxStages, (budget - fixed) / std::max(per_stage, 1));
-  if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations or rows too large for shared
+  int budget = std::min(dyn_max[slot], kSmemTarget);
+  if (fixed + 3 * per_stage > budget) budget = dyn_max[slot];
+  p.stages = std::min(kMaxStages, (budget - fixed) / per_stage);
+  if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
+  // Bulk copies need 16-byte aligned row slices of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
   const uintptr_t sa = reinterpret_cast<uintptr_t>(p.ws);
-  p.bulk = (p.row_bytes % 16 == 0) && (wa % 16 == 0) &&
+  p.bulk = (p.row_bytes % 16 == 0) && (slice % 16 == 0) && (wa % 16 == 0) &&
+           ((static_cast<int64_t>(p.row_bytes) - (static_cast<int64_t>((p.gpr - 1) / p.G) * p.G) *
+                                                     p.row_bytes / p.gpr) % 16 == 0) &&
            (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
   p.off_w = round_up(p.x_bytes, 128);
   p.off_s = p.off_w + p.stages * p.stage_w_bytes;
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
   p.off_b = round_up(p.off_t + terms_bytes, 16);
   const int smem = p.off_b + 8 * (2 * p.stages + 4);
-  const int ctas_per_sm = budget < dyn_max[slot] ? 2 : 1;
-  const int grid = std::min(p.m, di.sm_count * ctas_per_sm);
+  const int grid = std::min(p.m, di.sm_count);
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream drains; it prefetches its weights at once and waits
   // for that kernel (griddepcontrol.wait) before it reads x or writes y.
