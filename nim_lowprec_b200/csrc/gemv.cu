@@ -20,11 +20,8 @@ unsigned int take_error_gemv() {
 
 namespace {
 
-constexpr int kNcw = 8;          // consumer warps per CTA (256 threads)
-constexpr int kMaxStages = 8;
-// Per-CTA shared-memory target: small enough that the next kernel's CTA fits
-// on the same SM under programmatic dependent launch.
-constexpr int kSmemTarget = 110 * 1024;
+constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
+constexpr int kMaxStages = 12;
 
 template <class Fmt>
 int x_stage_bytes(const GemvParams& p);
@@ -89,8 +86,9 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   const int terms_bytes = 2 * p.RP * p.tstride * 4;
   const int fixed = round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  int budget = std::min(dyn_max[slot], kSmemTarget);
-  if (fixed + 3 * per_stage > budget) budget = dyn_max[slot];
+  // All the shared memory goes to stages: the weight stream needs about a
+  // microsecond of HBM bandwidth per SM in flight.
+  const int budget = dyn_max[slot];
   p.stages = std::min(kMaxStages, (budget - fixed) / per_stage);
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
   // Bulk copies need 16-byte aligned row slices of weights and scales.

@@ -15,7 +15,7 @@
 // parallelise freely; the fold must keep its order to stay bit-exact.
 //
 // Work layout.  Each CTA owns a contiguous, balanced range of rows (one CTA
-// per SM).  K is cut into chunks of G groups; a stage is SR rows x one chunk,
+// per SM, sixteen consumer warps).  K is cut into chunks of G groups; a stage is SR rows x one chunk,
 // where SR * G / 2 equals the consumer thread count, so every consumer
 // thread computes exactly one row pair of one group per stage.  Stages run
 // chunk-major over the CTA's rows (all rows of chunk 0, then chunk 1, ...),
