@@ -46,6 +46,36 @@ int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return ((p.k + 15) & ~15) + 
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// A 2-D row-major tensor map: `inner` elements per row, `rows` rows, row
+// pitch `pitch` bytes, box `bi` x `br`.  Encoding is a host-side computation.
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+               int64_t inner, int64_t rows, int64_t pitch, int bi, int br) {
+  if (bi <= 0 || bi > 256 || br <= 0 || br > 256 || (static_cast<int64_t>(bi) * esize) % 16) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(bi), static_cast<cuuint32_t>(br)};
+  const cuuint32_t estr[2] = {1, 1};
+  // Resolved through the runtime, so the library has no link-time
+  // dependency on the driver library (it loads on machines without a GPU).
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<EncodeFn>(fn);
+  }();
+  if (!encode) return false;
+  return encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 template <class Fmt>
@@ -79,7 +109,9 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.RP = std::min(kMaxRowsPerPass, rows_per_cta);
   p.tstride = p.G + 4;
   const int64_t slice = static_cast<int64_t>(p.G) * p.row_bytes / p.gpr;
-  p.slice_pitch = round_up(static_cast<int>(slice), 16);
+  // Shared row pitch: 128-byte multiple, so every TMA destination (a whole
+  // stage or one row of it) is 128-byte aligned; the boxes are this wide.
+  p.slice_pitch = round_up(static_cast<int>(slice), 128);
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
   p.stage_w_bytes = p.SR * p.slice_pitch;
   p.stage_s_bytes = Fmt::kScales ? p.SR * p.G * 4 : 0;
@@ -94,10 +126,21 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   // Bulk copies need 16-byte aligned row slices of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
   const uintptr_t sa = reinterpret_cast<uintptr_t>(p.ws);
-  p.bulk = (p.row_bytes % 16 == 0) && (slice % 16 == 0) && (wa % 16 == 0) &&
-           ((static_cast<int64_t>(p.row_bytes) - (static_cast<int64_t>((p.gpr - 1) / p.G) * p.G) *
-                                                     p.row_bytes / p.gpr) % 16 == 0) &&
-           (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
+  p.bulk = (p.row_bytes % 16 == 0) && (slice % 16 == 0) && (p.slice_pitch / 8 <= 256) &&
+           (wa % 16 == 0) && (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
+  if (p.bulk) {
+    const bool ok =
+        encode_2d(&p.tw_full, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, p.w, p.row_bytes / 8, p.m,
+                  p.row_bytes, p.slice_pitch / 8, p.SR) &&
+        encode_2d(&p.tw_row, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, p.w, p.row_bytes / 8, p.m,
+                  p.row_bytes, p.slice_pitch / 8, 1) &&
+        (!Fmt::kScales ||
+         (encode_2d(&p.ts_full, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
+                    p.G, p.SR) &&
+          encode_2d(&p.ts_row, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
+                    p.G, 1)));
+    if (!ok) p.bulk = 0;
+  }
   p.off_w = round_up(p.x_bytes, 128);
   p.off_s = p.off_w + p.stages * p.stage_w_bytes;
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;

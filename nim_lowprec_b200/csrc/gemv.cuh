@@ -21,9 +21,12 @@
 // chunk-major over the CTA's rows (all rows of chunk 0, then chunk 1, ...),
 // so each row's terms arrive in group order, one chunk at a time.
 //
-//   warp 0   producer: per stage one 1-D bulk copy (TMA) per row slice of
-//            weights and of scales, HBM -> shared, `stages` deep, tracked by
-//            mbarriers.  Shapes whose slices are not 16-byte aligned take a
+//   warp 0   producer: per stage one 2-D tiled TMA load of the weight box
+//            (SR rows x one chunk) and one of the scale box, HBM -> shared,
+//            `stages` deep, tracked by mbarriers (a CTA's last rows come in
+//            single-row boxes so no other CTA's rows are fetched).  Few large
+//            copies keep enough bytes in flight per SM; one small copy per
+//            row does not.  Shapes whose rows are not 16-byte aligned take a
 //            plain-load staging path.  It starts before the activations are
 //            staged and, under programmatic dependent launch, before the
 //            previous kernel in the stream has finished.
@@ -42,7 +45,11 @@ namespace lp {
 
 enum class Fold { Serial, Lanes4 };
 
-struct GemvParams {
+struct alignas(64) GemvParams {
+  // 2-D tensor maps over the weight rows (uint64 elements, row_bytes / 8 per
+  // row) and the scale rows (fp32, gpr per row): box *_full covers a whole
+  // stage (SR rows x one chunk), box *_row a single row of it.
+  CUtensorMap tw_full, tw_row, ts_full, ts_row;
   const uint8_t* w;   // weight rows, row_bytes each
   const float* ws;    // per-row group scales (M x gpr) or nullptr
   const void* x;      // activations (format-specific)
@@ -54,7 +61,7 @@ struct GemvParams {
   int SR;             // rows per stage (<= 32)
   int RP;             // rows per pass (term-matrix height), <= kMaxRowsPerPass
   int stages;
-  int bulk;           // 1: bulk-copy staging, 0: plain loads
+  int bulk;           // 1: tensor-map (TMA) staging, 0: plain loads
   int tstride;        // floats per term-matrix row
   int x_bytes;        // shared bytes for the staged activations
   int off_w, off_s, off_t, off_b;  // shared-memory offsets
@@ -164,7 +171,8 @@ __device__ __forceinline__ void fold_chunk(const float* T, int ts, int nrows_lan
 
 // ----------------------------------------------------------- the kernel
 template <class Fmt, int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(32 * (NCW + 2), 1)
+    gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ volatile int s_abort;
   uint8_t* xsm = smem;
@@ -206,6 +214,10 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     // launch_gemv), so the stream starts before the grid dependency is
     // resolved; the activations wait for it in the consumer warps.
     const uint64_t pol = l2_evict_first();
+    if (p.bulk && lane == 0) {
+      tma_prefetch_desc(&p.tw_full);
+      tma_prefetch_desc(&p.tw_row);
+    }
     int t = 0;
     for (; !sc.done(); sc.next(p), ++t) {
       const int s = t % p.stages;
@@ -224,15 +236,28 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
       const uint8_t* gw = p.w + static_cast<int64_t>(r0) * p.row_bytes + gb0;
       const float* gsc = Fmt::kScales ? p.ws + static_cast<int64_t>(r0) * p.gpr + g0 : nullptr;
       if (p.bulk) {
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], rows * (slice + sslice));
-        __syncwarp();
-        if (lane < rows) {
-          bulk_g2s(dw + lane * p.slice_pitch, gw + static_cast<int64_t>(lane) * p.row_bytes, slice,
-                   &full[s], pol);
-          if (Fmt::kScales)
-            bulk_g2s(ds + lane * p.G, gsc + static_cast<int64_t>(lane) * p.gpr, sslice, &full[s],
-                     pol);
+        // Boxes are a full chunk wide (columns past the row end read as 0)
+        // and count full-width bytes.
+        const int c0 = static_cast<int>(gb0 >> 3);
+        if (rows == p.SR) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[s], p.SR * (p.slice_pitch + (Fmt::kScales ? p.G * 4 : 0)));
+            tma_load_2d(dw, &p.tw_full, c0, r0, &full[s], pol);
+            if (Fmt::kScales) tma_load_2d(ds, &p.ts_full, g0, r0, &full[s], pol);
+          }
+        } else {
+          if (lane == 0)
+            mbar_arrive_expect_tx(&full[s], rows * (p.slice_pitch + (Fmt::kScales ? p.G * 4 : 0)));
+          __syncwarp();
+          if (lane < rows) {
+            tma_load_2d(dw + lane * p.slice_pitch, &p.tw_row, c0, r0 + lane, &full[s], pol);
+            if (Fmt::kScales) tma_load_2d(ds + lane * p.G, &p.ts_row, g0, r0 + lane, &full[s], pol);
+          }
         }
+        (void)slice;
+        (void)sslice;
+        (void)gw;
+        (void)gsc;
       } else {
         for (int r = 0; r < rows; ++r) {
           for (uint32_t i = lane; i < slice; i += 32)

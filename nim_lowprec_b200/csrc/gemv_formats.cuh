@@ -63,6 +63,15 @@ __device__ __forceinline__ int nib_at(const uint8_t* row, int kk) {
   return static_cast<int>((kk & 1) ? (b >> 4) : (b & 15u));
 }
 
+// Staged fp32 activations use a swizzled layout: the 16-byte unit i (0..7) of
+// 32-float block b lives at unit 8 b + (i ^ (b & 7)).  Consumer lanes load
+// whole blocks of consecutive b, so without it the eight lanes of each
+// shared-memory wavefront would all hit one bank group.
+__device__ __forceinline__ int xsw(int kk) {
+  const int b = kk >> 5;
+  return (((b << 3) | (((kk >> 2) & 7) ^ (b & 7))) << 2) | (kk & 3);
+}
+
 // The fp32 activations of one group of 32, each duplicated into an f32x2.
 struct XPairs {
   int g = -1;
@@ -70,10 +79,10 @@ struct XPairs {
   __device__ __forceinline__ void load(const float* x, int grp) {
     if (grp == g) return;
     g = grp;
-    const float4* v = reinterpret_cast<const float4*>(x + grp * 32);
+    const float4* v = reinterpret_cast<const float4*>(x) + (grp << 3);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 f = v[i];
+      const float4 f = v[i ^ (grp & 7)];
       x2[4 * i + 0] = pk(f.x, f.x);
       x2[4 * i + 1] = pk(f.y, f.y);
       x2[4 * i + 2] = pk(f.z, f.z);
@@ -82,10 +91,21 @@ struct XPairs {
   }
 };
 
-// fp32 activation staging shared by the fp32 formats.
+// fp32 activation staging shared by the fp32 formats (swizzled, see xsw).
 struct StageXF32 {
   static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
-    copy_bytes(xsm, static_cast<const uint8_t*>(p.x), p.k * 4, tid, nthr);
+    const float* src = static_cast<const float*>(p.x);
+    float* dst = reinterpret_cast<float*>(xsm);
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (p.k & 3) == 0) {
+      const int n4 = p.k >> 2;
+      for (int q = tid; q < n4; q += nthr) {
+        const int b = q >> 3;
+        reinterpret_cast<float4*>(dst)[(b << 3) | ((q & 7) ^ (b & 7))] =
+            __ldg(reinterpret_cast<const float4*>(src) + q);
+      }
+    } else {
+      for (int i = tid; i < p.k; i += nthr) dst[xsw(i)] = src[i];
+    }
   }
 };
 
@@ -134,7 +154,7 @@ struct FmtI8 : StageXF32 {
                                   const float* s, int g) {
     float partial = 0.0f;
     for (int kk = g * p.gs; kk < (g + 1) * p.gs; ++kk)
-      partial = fadd(partial, fmul(i2f_rn(static_cast<int8_t>(w[kk])), x[kk]));
+      partial = fadd(partial, fmul(i2f_rn(static_cast<int8_t>(w[kk])), x[xsw(kk)]));
     return fmul(partial, s[g]);
   }
 };
@@ -189,7 +209,7 @@ struct FmtI4 : StageXF32 {
     float partial = 0.0f;
     for (int kk = g * p.gs; kk < (g + 1) * p.gs; ++kk) {
       const int n = nib_at(w, kk);
-      partial = fadd(partial, fmul(i2f_rn(n >= 8 ? n - 16 : n), x[kk]));
+      partial = fadd(partial, fmul(i2f_rn(n >= 8 ? n - 16 : n), x[xsw(kk)]));
     }
     return fmul(partial, s[g]);
   }
@@ -253,7 +273,7 @@ struct FmtF4 : StageXF32 {
     const float sc = fmul(s[g], 0.5f);
     float partial = 0.0f;
     for (int kk = g * p.gs; kk < (g + 1) * p.gs; ++kk)
-      partial = fadd(partial, fmul(i2f_rn(lut[nib_at(w, kk)]), x[kk]));
+      partial = fadd(partial, fmul(i2f_rn(lut[nib_at(w, kk)]), x[xsw(kk)]));
     return fmul(partial, sc);
   }
 };
