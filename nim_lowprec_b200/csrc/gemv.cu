@@ -114,9 +114,10 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.slice_pitch = round_up(static_cast<int>(slice), 128);
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
   p.stage_w_bytes = p.SR * p.slice_pitch;
-  p.stage_s_bytes = Fmt::kScales ? p.SR * p.G * 4 : 0;
+  p.spitch = round_up(p.G * 4, 128) / 4;  // scale rows: 128-byte pitch, as wide a box
+  p.stage_s_bytes = Fmt::kScales ? p.SR * p.spitch * 4 : 0;
   const int terms_bytes = 2 * p.RP * p.tstride * 4;
-  const int fixed = round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
+  const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
   // All the shared memory goes to stages: the weight stream needs about a
   // microsecond of HBM bandwidth per SM in flight.
@@ -136,16 +137,16 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
                   p.row_bytes, p.slice_pitch / 8, 1) &&
         (!Fmt::kScales ||
          (encode_2d(&p.ts_full, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
-                    p.G, p.SR) &&
+                    p.spitch, p.SR) &&
           encode_2d(&p.ts_row, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
-                    p.G, 1)));
+                    p.spitch, 1)));
     if (!ok) p.bulk = 0;
   }
   p.off_w = round_up(p.x_bytes, 128);
   p.off_s = p.off_w + p.stages * p.stage_w_bytes;
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
   p.off_b = round_up(p.off_t + terms_bytes, 16);
-  const int smem = p.off_b + 8 * (2 * p.stages + 4);
+  const int smem = 128 + p.off_b + 8 * (2 * p.stages + 4);  // + base alignment slack
   const int grid = std::min(p.m, di.sm_count);
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream drains; it prefetches its weights at once and waits

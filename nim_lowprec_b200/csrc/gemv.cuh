@@ -65,7 +65,8 @@ struct alignas(64) GemvParams {
   int tstride;        // floats per term-matrix row
   int x_bytes;        // shared bytes for the staged activations
   int off_w, off_s, off_t, off_b;  // shared-memory offsets
-  int slice_pitch;    // shared bytes per weight row slice (G groups, 16-aligned)
+  int slice_pitch;    // shared bytes per weight row slice (G groups, 128-byte multiple)
+  int spitch;         // shared floats per scale row slice (spitch * 4: 128-byte multiple)
   int stage_w_bytes, stage_s_bytes;
   float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
 };
@@ -173,8 +174,12 @@ __device__ __forceinline__ void fold_chunk(const float* T, int ts, int nrows_lan
 template <class Fmt, int NCW>
 __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ volatile int s_abort;
+  // Every TMA destination below is 128-byte aligned relative to this base;
+  // align the base itself rather than rely on the declaration (the launch
+  // reserves the 128 bytes this may skip).
+  uint8_t* smem = smem_raw + ((128u - (saddr(smem_raw) & 127u)) & 127u);
   uint8_t* xsm = smem;
   uint8_t* stw = smem + p.off_w;
   uint8_t* sts = smem + p.off_s;
@@ -241,17 +246,17 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         const int c0 = static_cast<int>(gb0 >> 3);
         if (rows == p.SR) {
           if (lane == 0) {
-            mbar_arrive_expect_tx(&full[s], p.SR * (p.slice_pitch + (Fmt::kScales ? p.G * 4 : 0)));
+            mbar_arrive_expect_tx(&full[s], p.SR * (p.slice_pitch + (Fmt::kScales ? p.spitch * 4 : 0)));
             tma_load_2d(dw, &p.tw_full, c0, r0, &full[s], pol);
             if (Fmt::kScales) tma_load_2d(ds, &p.ts_full, g0, r0, &full[s], pol);
           }
         } else {
           if (lane == 0)
-            mbar_arrive_expect_tx(&full[s], rows * (p.slice_pitch + (Fmt::kScales ? p.G * 4 : 0)));
+            mbar_arrive_expect_tx(&full[s], rows * (p.slice_pitch + (Fmt::kScales ? p.spitch * 4 : 0)));
           __syncwarp();
           if (lane < rows) {
             tma_load_2d(dw + lane * p.slice_pitch, &p.tw_row, c0, r0 + lane, &full[s], pol);
-            if (Fmt::kScales) tma_load_2d(ds + lane * p.G, &p.ts_row, g0, r0 + lane, &full[s], pol);
+            if (Fmt::kScales) tma_load_2d(ds + lane * p.spitch, &p.ts_row, g0, r0 + lane, &full[s], pol);
           }
         }
         (void)slice;
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
           for (uint32_t i = lane; i < slice; i += 32)
             dw[r * p.slice_pitch + i] = gw[static_cast<int64_t>(r) * p.row_bytes + i];
           if (Fmt::kScales)
-            for (int i = lane; i < gc; i += 32) ds[r * p.G + i] = gsc[static_cast<int64_t>(r) * p.gpr + i];
+            for (int i = lane; i < gc; i += 32) ds[r * p.spitch + i] = gsc[static_cast<int64_t>(r) * p.gpr + i];
         }
         __threadfence_block();
         __syncwarp();
@@ -343,7 +348,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         const float* S = reinterpret_cast<const float*>(sts + s * p.stage_s_bytes);
         float ta, tbv;
         f.term2(p, xsm, W + ra * p.slice_pitch - wb, W + rb * p.slice_pitch - wb,
-                S + ra * p.G - g0, S + rb * p.G - g0, g0 + gl, ta, tbv);
+                S + ra * p.spitch - g0, S + rb * p.spitch - g0, g0 + gl, ta, tbv);
         float* T = terms + (tb * p.RP + sc.sb * p.SR + ra) * p.tstride + gl;
         T[0] = ta;
         if (ra + 1 < rows) T[p.tstride] = tbv;
