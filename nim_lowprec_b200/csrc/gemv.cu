@@ -46,36 +46,6 @@ int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return ((p.k + 15) & ~15) + 
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-// A 2-D row-major tensor map: `inner` elements per row, `rows` rows, row
-// pitch `pitch` bytes, box `bi` x `br`.  Encoding is a host-side computation.
-bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
-               int64_t inner, int64_t rows, int64_t pitch, int bi, int br) {
-  if (bi <= 0 || bi > 256 || br <= 0 || br > 256 || (static_cast<int64_t>(bi) * esize) % 16) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(bi), static_cast<cuuint32_t>(br)};
-  const cuuint32_t estr[2] = {1, 1};
-  // Resolved through the runtime, so the library has no link-time
-  // dependency on the driver library (it loads on machines without a GPU).
-  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-  static EncodeFn encode = [] {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-            cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      fn = nullptr;
-    return reinterpret_cast<EncodeFn>(fn);
-  }();
-  if (!encode) return false;
-  return encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 template <class Fmt>
@@ -100,57 +70,40 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     dyn_max[slot] = lim;
   });
   constexpr int NC = kNcw * 32;
-  const int gbytes = p.row_bytes / p.gpr + (Fmt::kScales ? 4 : 0);  // per group, rounded down
-  // Chunk width: a stage is SR x G groups with SR * G = 2 * NC, i.e. one
-  // row pair per consumer thread; narrower when a row has fewer groups.
-  p.G = std::min(gbytes <= 24 ? 64 : 32, round_up(p.gpr, 4));
-  p.SR = std::min(32, 2 * NC / p.G);    // rows per stage (one producer lane each)
-  const int rows_per_cta = (p.m + std::min(p.m, di.sm_count) - 1) / std::min(p.m, di.sm_count);
-  p.RP = std::min(kMaxRowsPerPass, rows_per_cta);
-  p.tstride = p.G + 4;
-  const int64_t slice = static_cast<int64_t>(p.G) * p.row_bytes / p.gpr;
-  // Shared row pitch: 128-byte multiple, so every TMA destination (a whole
-  // stage or one row of it) is 128-byte aligned; the boxes are this wide.
-  p.slice_pitch = round_up(static_cast<int>(slice), 128);
+  // Tile height: about one row pair x one group per consumer thread, at most
+  // 32 rows (one folder lane each) and 64 KB of weights+scales per stage.
+  const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
+  p.rt = std::max(1, std::min({32, (2 * NC + p.gpr - 1) / p.gpr, (64 * 1024) / std::max(row_total, 1)}));
+  p.rt = std::min(p.rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
+  if (p.rt > 1) p.rt &= ~1;  // whole row pairs
+  p.tstride = round_up(std::max(p.gpr, 1), 32) + 4;
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
-  p.stage_w_bytes = p.SR * p.slice_pitch;
-  p.spitch = round_up(p.G * 4, 128) / 4;  // scale rows: 128-byte pitch, as wide a box
-  p.stage_s_bytes = Fmt::kScales ? p.SR * p.spitch * 4 : 0;
-  const int terms_bytes = 2 * p.RP * p.tstride * 4;
-  const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 16 + 8 * (2 * kMaxStages + 4);
+  p.stage_w_bytes = round_up(p.rt * p.row_bytes, 128);
+  p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 128) : 0;
+  const int terms_bytes = kTermBufs * p.rt * p.tstride * 4;
+  const int fixed = 128 + round_up(p.x_bytes, 128) + round_up(terms_bytes, 128) + 8 * (2 * kMaxStages + 2 * kTermBufs);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  // All the shared memory goes to stages: the weight stream needs about a
-  // microsecond of HBM bandwidth per SM in flight.
-  const int budget = dyn_max[slot];
-  p.stages = std::min(kMaxStages, (budget - fixed) / per_stage);
+  // All remaining shared memory goes to stages: the weight stream needs about
+  // a microsecond of HBM bandwidth per SM in flight.
+  p.stages = std::min(kMaxStages, (dyn_max[slot] - fixed) / per_stage);
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
-  // Bulk copies need 16-byte aligned row slices of weights and scales.
+  // Bulk copies need 16-byte aligned, 16-byte multiple rows of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
   const uintptr_t sa = reinterpret_cast<uintptr_t>(p.ws);
-  p.bulk = (p.row_bytes % 16 == 0) && (slice % 16 == 0) && (p.slice_pitch / 8 <= 256) &&
-           (wa % 16 == 0) && (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
-  if (p.bulk) {
-    const bool ok =
-        encode_2d(&p.tw_full, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, p.w, p.row_bytes / 8, p.m,
-                  p.row_bytes, p.slice_pitch / 8, p.SR) &&
-        encode_2d(&p.tw_row, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, p.w, p.row_bytes / 8, p.m,
-                  p.row_bytes, p.slice_pitch / 8, 1) &&
-        (!Fmt::kScales ||
-         (encode_2d(&p.ts_full, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
-                    p.spitch, p.SR) &&
-          encode_2d(&p.ts_row, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.ws, p.gpr, p.m, p.gpr * 4,
-                    p.spitch, 1)));
-    if (!ok) p.bulk = 0;
-  }
+  p.bulk = (p.row_bytes % 16 == 0) && (wa % 16 == 0) &&
+           (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
   p.off_w = round_up(p.x_bytes, 128);
   p.off_s = p.off_w + p.stages * p.stage_w_bytes;
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
-  p.off_b = round_up(p.off_t + terms_bytes, 16);
-  const int smem = 128 + p.off_b + 8 * (2 * p.stages + 4);  // + base alignment slack
+  p.off_b = p.off_t + round_up(terms_bytes, 128);
+  const int smem = 128 + p.off_b + 8 * (2 * p.stages + 2 * kTermBufs);  // + base alignment slack
   const int grid = std::min(p.m, di.sm_count);
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream drains; it prefetches its weights at once and waits
   // for that kernel (griddepcontrol.wait) before it reads x or writes y.
+  // Only GEMV kernels release their dependents early, and a GEMV writes
+  // nothing but y, which never aliases another GEMV's weights, so the early
+  // weight stream cannot read memory still being written.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(32 * (kNcw + 2));

@@ -9,7 +9,6 @@
 // multiply feeding an add into an FMA.
 #pragma once
 #include <cstdint>
-#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -96,21 +95,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(saddr(bar)), "l"(policy)
       : "memory");
 }
-// 2-D tiled TMA load of box (c0, c1) of `tmap` into this CTA's shared
-// memory (no multicast), completion counted on `bar` in bytes.  c0 counts
-// elements of the innermost dimension; c0 * element size is a multiple of 16.
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1,
-                                            uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(saddr(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(saddr(bar)), "l"(policy)
-      : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
-}
-
 // L2 policy for a one-pass weight stream: evict first.
 __device__ __forceinline__ uint64_t l2_evict_first() {
   uint64_t p;
