@@ -63,6 +63,21 @@ int lp_device_error(void);
 
 /* ======================= fp32-activation fused dequant-GEMVs ========== */
 
+/* Arithmetic of the fp32-activation GEMVs (process-wide, default FAST).
+ *   LP_FP32_FAST   activations as block-float integers (22-bit per group,
+ *                  three int8 planes), exact integer group dots: within a few
+ *                  ulp of the exact dot, inside the reference's 1e-5 relative
+ *                  tolerance, not bit-identical to its summation order.  Used
+ *                  when the group size is a multiple of 8.
+ *   LP_FP32_EXACT  the reference scalar path's exact operation order
+ *                  (simd/dequant.nim:253-256 and kin): bit-identical results.
+ * No counterpart in the reference (its x86 build runs the scalar order).
+ * Returns LP_ERR_ARG for an unknown mode. */
+#define LP_FP32_FAST 0
+#define LP_FP32_EXACT 1
+int lp_set_fp32_mode(int mode);
+int lp_get_fp32_mode(void);
+
 /* dequantGemv: int8 weights M x K, scales M x (K/groupSize), fp32 x -> y.
  * Replaces simd/dequant.nim:210-257 (proc dequantGemv*). */
 int lp_dequant_gemv(const int8_t *wq, int64_t wq_len, const float *scales, int64_t scales_len,

@@ -12,7 +12,8 @@ from .dequant import (  # noqa: F401
     dequantGemvF4, dequantGemvI4, dequantGemvI4Q8, dequantGemvQ4_0, dequantGemvQ4_0Q8,
     dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantizeQ4_0Batch,
     dequantizeQ8_0Batch, quantizeBatch, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0,
-    quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split)
+    quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split, fp32_mode,
+    fp32Mode, setFp32Mode)
 from .ggml import QK, BlockQ4_0, BlockQ8_0  # noqa: F401
 
 _native.lib()  # fail loudly at import if the CUDA library is missing

@@ -21,6 +21,9 @@ LP_ERR_TIMEOUT = 5
 LP_ERR_UNSUPPORTED = 6
 LP_ERR_NO_DEVICE = 7
 
+LP_FP32_FAST = 0
+LP_FP32_EXACT = 1
+
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
 _vp = ctypes.c_void_p
@@ -66,6 +69,8 @@ SIGNATURES = {
     "lph_quantize_q8_0_batch": "pnpn",
     "lph_quantize_q4_0_batch": "pnpn",
     "lph_quantize_batch": "pnpnnpn",
+    "lp_set_fp32_mode": "i",
+    "lp_get_fp32_mode": "",
 }
 
 

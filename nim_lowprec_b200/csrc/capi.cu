@@ -5,6 +5,7 @@
 // (e.g. simd/dequant.nim:221-226, 768-771, 1392-1400).  A failed rule
 // returns LP_ERR_SHAPE before anything is launched.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -26,6 +27,8 @@ const DeviceInfo& device_info() {
     d.ordinal = dev;
     cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&d.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&d.smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
     cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
   });
@@ -84,6 +87,11 @@ GemvParams base(const void* w, const float* ws, const void* x, const float* xs, 
 
 constexpr int64_t kIntMax = 0x7fffffff;
 
+std::atomic<int> g_fp32_mode{LP_FP32_FAST};
+
+// The block-float path needs whole 8-element chunks per group.
+inline bool fast_fp32(int64_t gs) { return g_fp32_mode.load() == LP_FP32_FAST && gs % 8 == 0; }
+
 // A pointer may be null only when its array is empty.
 inline bool bad(const void* p, int64_t len) { return len > 0 && p == nullptr; }
 
@@ -111,6 +119,14 @@ const char* lp_status_string(int s) {
 
 const char* lp_last_error_detail(void) { return lp::t_detail_ptr(); }
 
+int lp_set_fp32_mode(int mode) {
+  if (mode != LP_FP32_FAST && mode != LP_FP32_EXACT) return LP_ERR_ARG;
+  g_fp32_mode.store(mode);
+  return LP_OK;
+}
+
+int lp_get_fp32_mode(void) { return g_fp32_mode.load(); }
+
 int lp_device_error(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LP_ERR_CUDA;
   const unsigned int e = lp::take_error_gemv();
@@ -133,6 +149,13 @@ static int gemv_f32_group(int fmt, const void* w, int64_t w_len, const float* sc
   if (bad(w, w_len) || bad(scales, scales_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   GemvParams p = base(w, scales, x, nullptr, y, m, k, gs, gpr, rb);
+  if (fast_fp32(gs)) {
+    switch (fmt) {
+      case 0: return lp::launch_gemv<lp::FmtI8F>(p, S(st));
+      case 1: return lp::launch_gemv<lp::FmtI4F>(p, S(st));
+      default: return lp::launch_gemv<lp::FmtF4F>(p, S(st));
+    }
+  }
   switch (fmt) {
     case 0: return lp::launch_gemv<lp::FmtI8>(p, S(st));
     case 1: return lp::launch_gemv<lp::FmtI4>(p, S(st));
@@ -165,6 +188,8 @@ static int gemv_f32_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, co
   LP_VALIDATED();
   const int64_t rb = bpr * (q4 ? 18 : 34);
   GemvParams p = base(w, nullptr, x, nullptr, y, m, bpr * 32, 32, bpr, rb);
+  if (fast_fp32(32))
+    return q4 ? lp::launch_gemv<lp::FmtQ4_0F>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0F>(p, S(st));
   return q4 ? lp::launch_gemv<lp::FmtQ4_0>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0>(p, S(st));
 }
 

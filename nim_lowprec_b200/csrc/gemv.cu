@@ -20,31 +20,36 @@ unsigned int take_error_gemv() {
 
 namespace {
 
-constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
+constexpr int kNcw = 8;          // consumer warps per CTA (256 threads)
 constexpr int kMaxStages = 12;
 
+inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+// Shared bytes of the staged activations.
 template <class Fmt>
 int x_stage_bytes(const GemvParams& p);
-template <>
-int x_stage_bytes<FmtI8>(const GemvParams& p) { return p.k * 4; }
-template <>
-int x_stage_bytes<FmtI4>(const GemvParams& p) { return p.k * 4; }
-template <>
-int x_stage_bytes<FmtF4>(const GemvParams& p) { return p.k * 4; }
-template <>
-int x_stage_bytes<FmtQ8_0>(const GemvParams& p) { return p.k * 4; }
-template <>
-int x_stage_bytes<FmtQ4_0>(const GemvParams& p) { return p.k * 4; }
-template <>
-int x_stage_bytes<FmtQ8>(const GemvParams& p) { return ((p.k + 15) & ~15) + p.gpr * 4; }
-template <>
-int x_stage_bytes<FmtI4Q8>(const GemvParams& p) { return ((p.k + 15) & ~15) + p.gpr * 4; }
-template <>
-int x_stage_bytes<FmtQ8_0Q8>(const GemvParams& p) { return ((p.k + 15) & ~15) + p.gpr * 4; }
-template <>
-int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return ((p.k + 15) & ~15) + p.gpr * 4; }
+inline int f32_bytes(const GemvParams& p) { return round_up(p.k, 32) * 4; }  // swizzled blocks
+inline int q8_bytes(const GemvParams& p) { return round_up(p.k, 16) + p.gpr * 4; }
+inline int planes_bytes(const GemvParams& p) { return 3 * round_up(p.k, 16) + 16 * p.gpr; }
+template <> int x_stage_bytes<FmtI8>(const GemvParams& p) { return f32_bytes(p); }
+template <> int x_stage_bytes<FmtI4>(const GemvParams& p) { return f32_bytes(p); }
+template <> int x_stage_bytes<FmtF4>(const GemvParams& p) { return f32_bytes(p); }
+template <> int x_stage_bytes<FmtQ8_0>(const GemvParams& p) { return f32_bytes(p); }
+template <> int x_stage_bytes<FmtQ4_0>(const GemvParams& p) { return f32_bytes(p); }
+template <> int x_stage_bytes<FmtI8F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtI4F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtF4F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtQ8_0F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtQ4_0F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtQ8>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtI4Q8>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtQ8_0Q8>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return q8_bytes(p); }
 
-inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+struct SmemLimits {
+  int one = 0;  // dynamic shared bytes one CTA may use
+  int two = 0;  // ... with a second CTA resident on the same SM
+};
 
 }  // namespace
 
@@ -56,36 +61,49 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   const DeviceInfo& di = device_info();
   auto kern = gemv_kernel<Fmt, kNcw>;
   // Dynamic shared memory may use the opt-in maximum minus the kernel's
-  // static shared memory; set once per device.  Rows per CTA beyond
-  // kMaxRowsPerPass are processed in several passes.
-  static int dyn_max[kMaxDevices];
+  // static shared memory; set once per device.
+  static SmemLimits lim[kMaxDevices];
   static std::once_flag once[kMaxDevices];
   const int slot = di.ordinal % kMaxDevices;
   std::call_once(once[slot], [&] {
     cudaFuncAttributes fa;
-    int lim = di.max_smem_optin;
-    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) lim -= static_cast<int>(fa.sharedSizeBytes);
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim) != cudaSuccess)
-      lim = 48 * 1024 - 256;
-    dyn_max[slot] = lim;
+    int st_bytes = 0;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) st_bytes = static_cast<int>(fa.sharedSizeBytes);
+    int one = di.max_smem_optin - st_bytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, one) != cudaSuccess)
+      one = 48 * 1024 - 256;
+    lim[slot].one = one;
+    lim[slot].two = std::min(one, di.smem_per_sm / 2 - di.smem_reserved - st_bytes);
   });
   constexpr int NC = kNcw * 32;
-  // Tile height: about one row pair x one group per consumer thread, at most
-  // 32 rows (one folder lane each) and 64 KB of weights+scales per stage.
+  // Tile height: about two (row pair, group) units per consumer thread, in
+  // whole row pairs, at most 32 rows and 32 KB of weights + scales.
   const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
-  p.rt = std::max(1, std::min({32, (2 * NC + p.gpr - 1) / p.gpr, (64 * 1024) / std::max(row_total, 1)}));
-  p.rt = std::min(p.rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
-  if (p.rt > 1) p.rt &= ~1;  // whole row pairs
-  p.tstride = round_up(std::max(p.gpr, 1), 32) + 4;
+  int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
+  rt = std::min(rt, std::max(2, (32 * 1024) / std::max(row_total, 1)));
+  rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
+  p.rt = std::max(1, rt & ~1);
+  p.tstride = round_up(p.gpr, 32) + 4;
+  // Ordered folds take fb tiles (<= 32 rows) per pass over a ring of two
+  // passes; the unordered fold goes tile by tile over four slots.
+  if (Fmt::kFold == Fold::Tree) {
+    p.fb = 1;
+    p.ring = 4;
+  } else {
+    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / p.rt));
+    while (p.fb > 1 && 2 * p.fb * p.rt * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
+    p.ring = 2 * p.fb;
+  }
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
   p.stage_w_bytes = round_up(p.rt * p.row_bytes, 128);
   p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 128) : 0;
-  const int terms_bytes = kTermBufs * p.rt * p.tstride * 4;
-  const int fixed = 128 + round_up(p.x_bytes, 128) + round_up(terms_bytes, 128) + 8 * (2 * kMaxStages + 2 * kTermBufs);
+  const int terms_bytes = round_up(p.ring * p.rt * p.tstride * 4, 128);
+  const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  // All remaining shared memory goes to stages: the weight stream needs about
-  // a microsecond of HBM bandwidth per SM in flight.
-  p.stages = std::min(kMaxStages, (dyn_max[slot] - fixed) / per_stage);
+  // Two CTAs per SM when three stages fit beside the second CTA (so the next
+  // launch overlaps this one's tail), else all of the SM's shared memory.
+  const int budget = (lim[slot].two - fixed) / per_stage >= 3 ? lim[slot].two : lim[slot].one;
+  p.stages = std::min(kMaxStages, (budget - fixed) / per_stage);
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
   // Bulk copies need 16-byte aligned, 16-byte multiple rows of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
@@ -95,8 +113,8 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   p.off_w = round_up(p.x_bytes, 128);
   p.off_s = p.off_w + p.stages * p.stage_w_bytes;
   p.off_t = p.off_s + p.stages * p.stage_s_bytes;
-  p.off_b = p.off_t + round_up(terms_bytes, 128);
-  const int smem = 128 + p.off_b + 8 * (2 * p.stages + 2 * kTermBufs);  // + base alignment slack
+  p.off_b = p.off_t + terms_bytes;
+  const int smem = 128 + p.off_b + 8 * (2 * p.stages + 2 * p.ring);  // + base alignment slack
   const int grid = std::min(p.m, di.sm_count);
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream drains; it prefetches its weights at once and waits
@@ -122,6 +140,11 @@ template int launch_gemv<FmtI4>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtF4>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8_0>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ4_0>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtI8F>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtI4F>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtF4F>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ8_0F>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ4_0F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtI4Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8_0Q8>(GemvParams, cudaStream_t);

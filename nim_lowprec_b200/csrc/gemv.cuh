@@ -15,32 +15,31 @@
 // parallelise freely; the fold must keep its order to stay bit-exact.
 //
 // Work layout.  Each CTA owns a contiguous, balanced range of rows (one CTA
-// per SM).  It walks them in tiles of RT consecutive rows -- one contiguous
-// stretch of HBM, so one large bulk copy (per-SM copy throughput on B200
-// grows with copy size: copies of 16 KB and up are needed to stream at full
-// HBM bandwidth).  RT is chosen so a tile holds about one row pair x one
-// group per consumer thread.
+// per SM; the planner sizes it so two fit on an SM, which lets the next
+// launch in the stream start streaming while this one drains).  It walks its
+// rows in tiles of RT consecutive rows -- one contiguous stretch of HBM, so
+// one large bulk copy (per-SM copy throughput on B200 grows with copy size:
+// copies of 16 KB and up are needed to stream at full HBM bandwidth).
 //
 //   warp 0   producer: per tile one 1-D bulk copy (TMA) of the weight rows and
 //            one of their scale rows, HBM -> shared, `stages` deep, tracked
 //            by mbarriers.  Rows that are not 16-byte multiples take a
-//            plain-load staging path.  It starts before the activations are
-//            staged and, under programmatic dependent launch, before the
-//            previous kernel in the stream has finished.
-//   warps 2+ consumers: the terms of row pairs x groups (two rows run as one
-//            packed f32x2 chain on the fp32 paths) into the tile's term
-//            matrix (kTermBufs buffers deep).
-//   warp 1   folder: lane r folds row r of a finished tile in group order
-//            (terms prefetched 32 at a time, so the add chain never waits on
-//            shared memory) and writes y.
+//            plain-load staging path.  It releases the next launch in the
+//            stream at once and starts before the activations are staged.
+//   warps 2+ consumers: the terms of row pairs x groups into a ring of
+//            per-tile term matrices (`ring` tiles deep).
+//   warp 1   folder: reduces each finished row to y.  Ordered folds (the
+//            bit-exact paths) give each lane one row and take `fb` tiles at a
+//            time so up to 32 independent chains run together; the
+//            unordered fold of the block-float path sums a row across lanes.
 #pragma once
 #include "lp_device.cuh"
 
 namespace lp {
 
-enum class Fold { Serial, Lanes4 };
+enum class Fold { Serial, Lanes4, Tree };
 
-constexpr int kTermBufs = 4;
+constexpr int kMaxRing = 16;  // term-ring slots (tiles), at most
 
 struct GemvParams {
   const uint8_t* w;   // weight rows, row_bytes each
@@ -55,6 +54,8 @@ struct GemvParams {
   int bulk;           // 1: bulk-copy staging, 0: plain loads
   int tstride;        // floats per term-matrix row
   int x_bytes;        // shared bytes for the staged activations
+  int fb;             // tiles per ordered fold batch (fb * rt <= 32)
+  int ring;           // term-ring slots, a multiple of fb
   int off_w, off_s, off_t, off_b;  // shared-memory offsets (128-byte aligned)
   int stage_w_bytes, stage_s_bytes;
   float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
@@ -130,9 +131,35 @@ __device__ __forceinline__ float fold_row(const float* T, int gpr) {
   return F == Fold::Serial ? l0 : fadd(fadd(l0, l1), fadd(l2, l3));
 }
 
+// Unordered row sums (block-float path): L lanes per row, L the largest
+// power of two with L * rows <= 32; each lane sums a strided subset of the
+// row's terms in four chains, then the L partial sums meet by shuffles.
+__device__ __forceinline__ void tree_fold(const float* T, int tstride, int rows, int gpr,
+                                          float* y, int lane) {
+  int lg = 5;
+  while (lg > 0 && (rows << lg) > 32) --lg;
+  const int L = 1 << lg;
+  const int r = lane >> lg, sub = lane & (L - 1);
+  float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+  if (r < rows) {
+    const float* row = T + r * tstride;
+    int g = sub;
+    for (; g + 3 * L < gpr; g += 4 * L) {
+      s0 = fadd(s0, row[g]);
+      s1 = fadd(s1, row[g + L]);
+      s2 = fadd(s2, row[g + 2 * L]);
+      s3 = fadd(s3, row[g + 3 * L]);
+    }
+    for (; g < gpr; g += L) s0 = fadd(s0, row[g]);
+  }
+  float s = fadd(fadd(s0, s1), fadd(s2, s3));
+  for (int o = L >> 1; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if (r < rows && sub == 0) y[r] = s;
+}
+
 // ----------------------------------------------------------- the kernel
 template <class Fmt, int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ volatile int s_abort;
   // Every bulk-copy destination is a 128-byte multiple from this base.
@@ -145,7 +172,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
   uint64_t* full = bars;
   uint64_t* empty = bars + p.stages;
   uint64_t* tfull = bars + 2 * p.stages;
-  uint64_t* tempty = tfull + kTermBufs;
+  uint64_t* tempty = tfull + p.ring;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -158,7 +185,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCW);
     }
-    for (int b = 0; b < kTermBufs; ++b) {
+    for (int b = 0; b < p.ring; ++b) {
       mbar_init(&tfull[b], NCW);
       mbar_init(&tempty[b], 1);
     }
@@ -170,14 +197,13 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
 
   if (warp == 0) {
     // ------------------------------------------------------ producer
-    // Weights never come from the kernel this launch may overlap with (see
-    // launch_gemv), so the stream starts before the grid dependency is
-    // resolved; the activations wait for it in the consumer warps.
+    // The next launch in the stream may start now: it streams only its own
+    // weights before its grid-dependency wait, and no GEMV writes weights.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint64_t pol = l2_evict_first();
     int t = 0;
     for (; t < ntiles; ++t) {
       const int s = t % p.stages;
-      if (t == p.stages) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
       if (t >= p.stages && !mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, &s_abort)) break;
       if (s_abort) break;
       const int r0 = row_begin + t * p.rt;
@@ -203,7 +229,6 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         if (lane == 0) mbar_arrive(&full[s]);
       }
     }
-    if (t <= p.stages) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // Drain: never leave the CTA with a bulk copy still landing in shared.
     if (p.bulk && lane == 0) {
       for (int u = max(0, t - p.stages); u < t; ++u)
@@ -211,16 +236,37 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- folder
-    for (int t = 0; t < ntiles; ++t) {
-      const int tb = t % kTermBufs;
-      if (!mbar_wait(&tfull[tb], (t / kTermBufs) & 1, &s_abort)) break;
-      if (s_abort) break;
-      const int r0 = row_begin + t * p.rt;
-      const int rows = min(p.rt, row_end - r0);
-      if (lane < rows)
-        p.y[r0 + lane] = fold_row<Fmt::kFold>(terms + (tb * p.rt + lane) * p.tstride, p.gpr);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[tb]);
+    if constexpr (Fmt::kFold == Fold::Tree) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int slot = t % p.ring;
+        if (!mbar_wait(&tfull[slot], (t / p.ring) & 1, &s_abort)) break;
+        if (s_abort) break;
+        const int r0 = row_begin + t * p.rt;
+        const int rows = min(p.rt, row_end - r0);
+        tree_fold(terms + slot * p.rt * p.tstride, p.tstride, rows, p.gpr, p.y + r0, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+      }
+    } else {
+      // Lane l folds row l % rt of tile t0 + l / rt of each batch.
+      const int ti = lane / p.rt, r = lane - ti * p.rt;
+      for (int t0 = 0; t0 < ntiles; t0 += p.fb) {
+        const int nt = min(p.fb, ntiles - t0);
+        bool ok = true;
+        for (int i = 0; i < nt && ok; ++i)
+          ok = mbar_wait(&tfull[(t0 + i) % p.ring], ((t0 + i) / p.ring) & 1, &s_abort);
+        if (!ok || s_abort) break;
+        if (ti < nt) {
+          const int t = t0 + ti;
+          const int r0 = row_begin + t * p.rt;
+          if (r < min(p.rt, row_end - r0))
+            p.y[r0 + r] =
+                fold_row<Fmt::kFold>(terms + ((t % p.ring) * p.rt + r) * p.tstride, p.gpr);
+        }
+        __syncwarp();
+        if (lane == 0)
+          for (int i = 0; i < nt; ++i) mbar_arrive(&tempty[(t0 + i) % p.ring]);
+      }
     }
   } else {
     // ------------------------------------------------------ consumers
@@ -239,9 +285,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % p.stages;
-      const int tb = t % kTermBufs;
+      const int tb = t % p.ring;
       bool ok = mbar_wait(&full[s], (t / p.stages) & 1, &s_abort);
-      if (ok && t >= kTermBufs) ok = mbar_wait(&tempty[tb], ((t / kTermBufs) - 1) & 1, &s_abort);
+      if (ok && t >= p.ring) ok = mbar_wait(&tempty[tb], ((t / p.ring) - 1) & 1, &s_abort);
       if (!ok || s_abort) break;
       const int r0 = row_begin + t * p.rt;
       const int rows = min(p.rt, row_end - r0);

@@ -348,6 +348,453 @@ struct FmtQ4_0 : StageXF32 {
   }
 };
 
+// ================================= fp32 activations, block-float path
+//
+// The fast fp32 path (the default; the scalar-order formats above are the
+// bit-exact mode).  Each activation group j (the weight group) is written as
+// integers X = rint(x * 2^(22 - E_j)) with 2^E_j > max|x| over the group, so
+// |X| <= 2^22 and the representation error is at most 2^-23 of the group's
+// largest magnitude.  X is split into three balanced signed bytes
+// X = d0 + 256 d1 + 65536 d2 (planes P0..P2), and every group dot becomes
+// three exact int32 dp4a sums of the integer weight codes against the
+// planes.  Formats whose codes carry an offset (Q4_0: u = w + 8; I4:
+// u = w + 8; F4: u = 2w + 12) start each plane sum at -offset * sum(d_p).
+// The group value is (65536 D2 + 256 D1 + D0) * 2^(E_j - 22); its only
+// roundings are the final int->float conversion and the scaling, so it is
+// within a few ulp of the exact dot -- well inside the reference's fp32
+// tolerance (1e-5 relative), not bit-identical to its sequential order.
+// Groups holding a non-finite activation are marked (scale NaN) and take
+// the scalar sequential path from global memory, so inf/NaN propagate as in
+// the reference.
+
+struct GInfo {
+  float s;       // 2^(E - 22); 0 for an all-zero group; NaN: non-finite x
+  int sx[3];     // sum of the group's digits in each plane
+};
+
+__device__ __forceinline__ int planes_stride(const GemvParams& p) { return (p.k + 15) & ~15; }
+
+// Smallest E with |m| < 2^E for finite m > 0.
+__device__ __forceinline__ int exp_above(float m) {
+  const uint32_t b = __float_as_uint(m) & 0x7FFFFFFFu;
+  const int e = static_cast<int>(b >> 23);
+  if (e) return e - 126;
+  return 32 - __clz(static_cast<int>(b)) - 149;  // subnormal: b * 2^-149
+}
+
+// 2^e as float for e in [-149, 127]; 0 below.
+__device__ __forceinline__ float pow2f(int e) {
+  if (e >= -126) return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+  if (e >= -149) return __uint_as_float(1u << (e + 149));
+  return 0.0f;
+}
+
+struct Digits {
+  int d[3];
+};
+__device__ __forceinline__ Digits split3(int X) {
+  Digits r;
+  r.d[0] = ((X + 128) & 255) - 128;
+  const int X1 = (X - r.d[0]) >> 8;
+  r.d[1] = ((X1 + 128) & 255) - 128;
+  r.d[2] = (X1 - r.d[1]) >> 8;
+  return r;
+}
+
+__device__ __forceinline__ double pow2d(int e) {  // e in [-1022, 1023]
+  return __hiloint2double((e + 1023) << 20, 0);
+}
+
+// kEvenOdd: within each 8-element chunk the planes hold the even columns
+// then the odd ones (the order of low and high nibbles of packed int4).
+template <bool kEvenOdd>
+struct StageXPlanes {
+  static __device__ __forceinline__ int pos(int k) {
+    if (!kEvenOdd) return k;
+    const int c = k & 7;
+    return (k & ~7) | ((c & 1) << 2) | (c >> 1);
+  }
+  static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
+    const float* x = static_cast<const float*>(p.x);
+    const int Kp = planes_stride(p);
+    int8_t* P = reinterpret_cast<int8_t*>(xsm);
+    GInfo* gi = reinterpret_cast<GInfo*>(xsm + 3 * Kp);
+    const int gs = p.gs;
+    const int lanes = gs >> 2;  // one lane per 4 elements when a group is 8..128 wide
+    const bool vec = (gs & (gs - 1)) == 0 && gs >= 8 && gs <= 128 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    if (vec) {
+      const int ntask = p.k >> 2;
+      const int lane = tid & 31;
+      for (int q0 = tid & ~31; q0 < ntask; q0 += nthr) {
+        const int q = q0 + lane;
+        const bool valid = q < ntask;
+        float4 v = valid ? __ldg(reinterpret_cast<const float4*>(x) + q)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        int nf = !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        for (int o = 1; o < lanes; o <<= 1) {
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          nf |= __shfl_xor_sync(0xffffffffu, nf, o);
+        }
+        const int E = (m > 0.0f && !nf) ? exp_above(m) : 0;
+        const double sc = pow2d(22 - E);
+        const float xv[4] = {v.x, v.y, v.z, v.w};
+        uint32_t word[3] = {0u, 0u, 0u};
+        int sum[3] = {0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int X = nf ? 0 : __double2int_rn(static_cast<double>(xv[i]) * sc);
+          const Digits dg = split3(X);
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) {
+            word[pl] |= (static_cast<uint32_t>(dg.d[pl]) & 255u) << (8 * i);
+            sum[pl] += dg.d[pl];
+          }
+        }
+        if (valid) {
+          if (!kEvenOdd) {
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl)
+              reinterpret_cast<uint32_t*>(P + pl * Kp)[q] = word[pl];
+          } else {
+            // elements 4h..4h+3 of chunk c: evens to 2h, 2h+1; odds to 4+2h, 5+2h
+            const int base = (q >> 1) * 8, h = q & 1;
+#pragma unroll
+            for (int pl = 0; pl < 3; ++pl) {
+              const uint32_t ev = prmt(word[pl], 0u, 0x0020u);
+              const uint32_t od = prmt(word[pl], 0u, 0x0031u);
+              reinterpret_cast<uint16_t*>(P + pl * Kp + base + 2 * h)[0] = static_cast<uint16_t>(ev);
+              reinterpret_cast<uint16_t*>(P + pl * Kp + base + 4 + 2 * h)[0] = static_cast<uint16_t>(od);
+            }
+          }
+        }
+        for (int o = 1; o < lanes; o <<= 1) {
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) sum[pl] += __shfl_xor_sync(0xffffffffu, sum[pl], o);
+        }
+        if (valid && (q & (lanes - 1)) == 0) {
+          GInfo g;
+          g.s = nf ? __uint_as_float(0x7FC00000u) : (m > 0.0f ? pow2f(E - 22) : 0.0f);
+          g.sx[0] = sum[0];
+          g.sx[1] = sum[1];
+          g.sx[2] = sum[2];
+          gi[q / lanes] = g;
+        }
+      }
+    } else {
+      for (int j = tid; j < p.gpr; j += nthr) {
+        const float* xg = x + j * gs;
+        int nf = 0;
+        float m = 0.0f;
+        for (int i = 0; i < gs; ++i) {
+          nf |= !isfinite(xg[i]);
+          m = fmaxf(m, fabsf(xg[i]));
+        }
+        const int E = (m > 0.0f && !nf) ? exp_above(m) : 0;
+        const double sc = pow2d(22 - E);
+        int sum[3] = {0, 0, 0};
+        for (int i = 0; i < gs; ++i) {
+          const int X = nf ? 0 : __double2int_rn(static_cast<double>(xg[i]) * sc);
+          const Digits dg = split3(X);
+          const int at = pos(j * gs + i);
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) {
+            P[pl * Kp + at] = static_cast<int8_t>(dg.d[pl]);
+            sum[pl] += dg.d[pl];
+          }
+        }
+        GInfo g;
+        g.s = nf ? __uint_as_float(0x7FC00000u) : (m > 0.0f ? pow2f(E - 22) : 0.0f);
+        g.sx[0] = sum[0];
+        g.sx[1] = sum[1];
+        g.sx[2] = sum[2];
+        gi[j] = g;
+      }
+    }
+  }
+};
+
+// The planes and group data of one group, cached across the rows a thread
+// visits (a thread keeps one group when the consumer count is a multiple of
+// the groups per row).  Only used for 32-element groups.
+template <int kOff>
+struct PlaneCache {
+  int g = -1;
+  uint32_t P[3][8];
+  int b[3];  // -kOff * sum(d_p)
+  float s;
+  __device__ __forceinline__ void load(const GemvParams& p, const uint8_t* xsm, int grp) {
+    if (grp == g) return;
+    g = grp;
+    const int Kp = planes_stride(p);
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) {
+      const uint4 u0 = reinterpret_cast<const uint4*>(xsm + pl * Kp + grp * 32)[0];
+      const uint4 u1 = reinterpret_cast<const uint4*>(xsm + pl * Kp + grp * 32)[1];
+      P[pl][0] = u0.x; P[pl][1] = u0.y; P[pl][2] = u0.z; P[pl][3] = u0.w;
+      P[pl][4] = u1.x; P[pl][5] = u1.y; P[pl][6] = u1.z; P[pl][7] = u1.w;
+    }
+    const GInfo gi = reinterpret_cast<const GInfo*>(xsm + 3 * Kp)[grp];
+    s = gi.s;
+#pragma unroll
+    for (int pl = 0; pl < 3; ++pl) b[pl] = -kOff * gi.sx[pl];
+  }
+};
+
+// (65536 D2 + 256 D1 + D0) as float.  kSmall: |D1| < 2^22 so 256 D1 + D0
+// stays in int32 (32-element groups).
+template <bool kSmall>
+__device__ __forceinline__ float bf_value(int a0, int a1, int a2) {
+  if (kSmall)
+    return fmaf(__int2float_rn(a2), 65536.0f, __int2float_rn(a1 * 256 + a0));
+  return fmaf(__int2float_rn(a2), 65536.0f, fmaf(__int2float_rn(a1), 256.0f, __int2float_rn(a0)));
+}
+
+// Three plane sums of 4 codes against plane words w0..w2.
+#define LP_DP3_US(acc, codes, w0, w1, w2)      \
+  do {                                         \
+    acc[0] = dp4a_us(codes, w0, acc[0]);       \
+    acc[1] = dp4a_us(codes, w1, acc[1]);       \
+    acc[2] = dp4a_us(codes, w2, acc[2]);       \
+  } while (0)
+#define LP_DP3_SS(acc, codes, w0, w1, w2)      \
+  do {                                         \
+    acc[0] = dp4a_ss(codes, w0, acc[0]);       \
+    acc[1] = dp4a_ss(codes, w1, acc[1]);       \
+    acc[2] = dp4a_ss(codes, w2, acc[2]);       \
+  } while (0)
+
+// Scalar sequential group sums from the unstaged fp32 activations (the
+// non-finite-group path of the block-float formats).
+__device__ __forceinline__ float seq_q4_0(const uint8_t* blk, const float* xg) {
+  float partial = 0.0f;
+  for (int i = 0; i < 16; ++i) {
+    const int b = blk[2 + i];
+    partial = fadd(partial, fmul(static_cast<float>((b & 15) - 8), xg[i]));
+    partial = fadd(partial, fmul(static_cast<float>((b >> 4) - 8), xg[i + 16]));
+  }
+  return fmul(partial, h2f(blk[0] | (blk[1] << 8)));
+}
+__device__ __forceinline__ float seq_q8_0(const uint8_t* blk, const float* xg) {
+  float partial = 0.0f;
+  for (int i = 0; i < 32; ++i)
+    partial = fadd(partial, fmul(static_cast<float>(static_cast<int8_t>(blk[2 + i])), xg[i]));
+  return fmul(partial, h2f(blk[0] | (blk[1] << 8)));
+}
+
+// dequantGemvQ4_0, block-float path: u = nibble (w = u - 8), low nibbles
+// against elements 0..15, high against 16..31.
+struct FmtQ4_0F : StageXPlanes<false> {
+  static constexpr bool kScales = false;
+  static constexpr Fold kFold = Fold::Tree;
+  PlaneCache<8> pc;
+  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
+                                        const uint8_t* wA, const uint8_t* wB, const float*,
+                                        const float*, int g, float& tA, float& tB) {
+    pc.load(p, xsm, g);
+    if (isnan(pc.s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * 32;
+      tA = seq_q4_0(wA + g * 18, xg);
+      tB = seq_q4_0(wB + g * 18, xg);
+      return;
+    }
+    uint32_t dA, dB, A[4], B[4];
+    load_q4_0(wA + g * 18, dA, A);
+    load_q4_0(wB + g * 18, dB, B);
+    int a[3] = {pc.b[0], pc.b[1], pc.b[2]};
+    int c[3] = {pc.b[0], pc.b[1], pc.b[2]};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t la = A[j] & 0x0F0F0F0Fu, ha = (A[j] >> 4) & 0x0F0F0F0Fu;
+      const uint32_t lb = B[j] & 0x0F0F0F0Fu, hb = (B[j] >> 4) & 0x0F0F0F0Fu;
+      LP_DP3_US(a, la, pc.P[0][j], pc.P[1][j], pc.P[2][j]);
+      LP_DP3_US(c, lb, pc.P[0][j], pc.P[1][j], pc.P[2][j]);
+      LP_DP3_US(a, ha, pc.P[0][j + 4], pc.P[1][j + 4], pc.P[2][j + 4]);
+      LP_DP3_US(c, hb, pc.P[0][j + 4], pc.P[1][j + 4], pc.P[2][j + 4]);
+    }
+    tA = bf_value<true>(a[0], a[1], a[2]) * (h2f(dA) * pc.s);
+    tB = bf_value<true>(c[0], c[1], c[2]) * (h2f(dB) * pc.s);
+  }
+};
+
+// dequantGemvQ8_0, block-float path: signed codes, natural order.
+struct FmtQ8_0F : StageXPlanes<false> {
+  static constexpr bool kScales = false;
+  static constexpr Fold kFold = Fold::Tree;
+  PlaneCache<0> pc;
+  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
+                                        const uint8_t* wA, const uint8_t* wB, const float*,
+                                        const float*, int g, float& tA, float& tB) {
+    pc.load(p, xsm, g);
+    if (isnan(pc.s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * 32;
+      tA = seq_q8_0(wA + g * 34, xg);
+      tB = seq_q8_0(wB + g * 34, xg);
+      return;
+    }
+    uint32_t dA, dB, A[8], B[8];
+    load_q8_0(wA + g * 34, dA, A);
+    load_q8_0(wB + g * 34, dB, B);
+    int a[3] = {0, 0, 0};
+    int c[3] = {0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      LP_DP3_SS(a, A[j], pc.P[0][j], pc.P[1][j], pc.P[2][j]);
+      LP_DP3_SS(c, B[j], pc.P[0][j], pc.P[1][j], pc.P[2][j]);
+    }
+    tA = bf_value<true>(a[0], a[1], a[2]) * (h2f(dA) * pc.s);
+    tB = bf_value<true>(c[0], c[1], c[2]) * (h2f(dB) * pc.s);
+  }
+};
+
+// Group-scale formats (I8, I4, F4) on the block-float path: any group size
+// that is a multiple of 8.  Codes per 8-element chunk c of group g come from
+// Codes::get (two words of byte codes in plane order); planes from the cache
+// (32-element groups) or shared memory.
+template <class Codes>
+struct FmtGroupF : StageXPlanes<Codes::kEvenOdd> {
+  static constexpr bool kScales = true;
+  static constexpr Fold kFold = Fold::Tree;
+  PlaneCache<Codes::kOff> pc;
+  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
+                                        const uint8_t* wA, const uint8_t* wB, const float* sA,
+                                        const float* sB, int g, float& tA, float& tB) {
+    const int Kp = planes_stride(p);
+    float s;
+    int a[3], c[3];
+    if (p.gs == 32) {
+      pc.load(p, xsm, g);
+      s = pc.s;
+      if (!isnan(s)) {
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) a[pl] = c[pl] = pc.b[pl];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t ua[2], ub[2];
+          Codes::get(wA, g * 32 + 8 * ch, ua);
+          Codes::get(wB, g * 32 + 8 * ch, ub);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            Codes::dp3(a, ua[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
+            Codes::dp3(c, ub[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
+          }
+        }
+      }
+    } else {
+      const GInfo gi = reinterpret_cast<const GInfo*>(xsm + 3 * Kp)[g];
+      s = gi.s;
+      if (!isnan(s)) {
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) a[pl] = c[pl] = -Codes::kOff * gi.sx[pl];
+        for (int e = g * p.gs; e < (g + 1) * p.gs; e += 8) {
+          uint32_t ua[2], ub[2];
+          Codes::get(wA, e, ua);
+          Codes::get(wB, e, ub);
+          uint2 w[3];
+#pragma unroll
+          for (int pl = 0; pl < 3; ++pl) w[pl] = *reinterpret_cast<const uint2*>(xsm + pl * Kp + e);
+          Codes::dp3(a, ua[0], w[0].x, w[1].x, w[2].x);
+          Codes::dp3(a, ua[1], w[0].y, w[1].y, w[2].y);
+          Codes::dp3(c, ub[0], w[0].x, w[1].x, w[2].x);
+          Codes::dp3(c, ub[1], w[0].y, w[1].y, w[2].y);
+        }
+      }
+    }
+    if (isnan(s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * p.gs;
+      tA = Codes::seq(wA, g, p.gs, xg, sA[g]);
+      tB = Codes::seq(wB, g, p.gs, xg, sB[g]);
+      return;
+    }
+    const float va = p.gs == 32 ? bf_value<true>(a[0], a[1], a[2]) : bf_value<false>(a[0], a[1], a[2]);
+    const float vb = p.gs == 32 ? bf_value<true>(c[0], c[1], c[2]) : bf_value<false>(c[0], c[1], c[2]);
+    tA = va * (Codes::scale(sA[g]) * s);
+    tB = vb * (Codes::scale(sB[g]) * s);
+  }
+};
+
+// int8 codes, natural order.
+struct CodesI8 {
+  static constexpr bool kEvenOdd = false;
+  static constexpr int kOff = 0;
+  static __device__ __forceinline__ void get(const uint8_t* row, int e, uint32_t (&u)[2]) {
+    const uint2 v = *reinterpret_cast<const uint2*>(row + e);
+    u[0] = v.x;
+    u[1] = v.y;
+  }
+  static __device__ __forceinline__ void dp3(int (&acc)[3], uint32_t u, uint32_t w0, uint32_t w1,
+                                             uint32_t w2) {
+    LP_DP3_SS(acc, u, w0, w1, w2);
+  }
+  static __device__ __forceinline__ float scale(float s) { return s; }
+  static __device__ float seq(const uint8_t* row, int g, int gs, const float* xg, float s) {
+    float partial = 0.0f;
+    for (int i = 0; i < gs; ++i)
+      partial = fadd(partial, fmul(static_cast<float>(static_cast<int8_t>(row[g * gs + i])), xg[i]));
+    return fmul(partial, s);
+  }
+};
+
+// packed two's-complement int4 (low nibble = even column): u = n ^ 8,
+// low nibbles are the even columns, high the odd (planes in even/odd order).
+struct CodesI4 {
+  static constexpr bool kEvenOdd = true;
+  static constexpr int kOff = 8;
+  static __device__ __forceinline__ void get(const uint8_t* row, int e, uint32_t (&u)[2]) {
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(row + (e >> 1));
+    u[0] = (v & 0x0F0F0F0Fu) ^ 0x08080808u;
+    u[1] = ((v >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+  }
+  static __device__ __forceinline__ void dp3(int (&acc)[3], uint32_t u, uint32_t w0, uint32_t w1,
+                                             uint32_t w2) {
+    LP_DP3_US(acc, u, w0, w1, w2);
+  }
+  static __device__ __forceinline__ float scale(float s) { return s; }
+  static __device__ float seq(const uint8_t* row, int g, int gs, const float* xg, float s) {
+    float partial = 0.0f;
+    for (int i = 0; i < gs; ++i) {
+      const int n = nib_at(row, g * gs + i);
+      partial = fadd(partial, fmul(static_cast<float>(n >= 8 ? n - 16 : n), xg[i]));
+    }
+    return fmul(partial, s);
+  }
+};
+
+// packed MXFP4 e2m1 codes: u = 2v + 12 via FmtF4::lut4, natural order.
+struct CodesF4 {
+  static constexpr bool kEvenOdd = false;
+  static constexpr int kOff = 12;
+  static __device__ __forceinline__ uint32_t lut4(uint32_t codes16) {
+    return prmt(0x0F0E0D0Cu, 0x18141210u, codes16) |
+           prmt(0x090A0B0Cu, 0x00040608u, codes16 ^ 0x8888u);
+  }
+  static __device__ __forceinline__ void get(const uint8_t* row, int e, uint32_t (&u)[2]) {
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(row + (e >> 1));
+    u[0] = lut4(v);
+    u[1] = lut4(v >> 16);
+  }
+  static __device__ __forceinline__ void dp3(int (&acc)[3], uint32_t u, uint32_t w0, uint32_t w1,
+                                             uint32_t w2) {
+    LP_DP3_US(acc, u, w0, w1, w2);
+  }
+  static __device__ __forceinline__ float scale(float s) { return s * 0.5f; }
+  static __device__ float seq(const uint8_t* row, int g, int gs, const float* xg, float s) {
+    const int lut[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+    float partial = 0.0f;
+    for (int i = 0; i < gs; ++i)
+      partial = fadd(partial, fmul(static_cast<float>(lut[nib_at(row, g * gs + i)]), xg[i]));
+    return fmul(partial, fmul(s, 0.5f));
+  }
+};
+
+struct FmtI8F : FmtGroupF<CodesI8> {};
+struct FmtI4F : FmtGroupF<CodesI4> {};
+struct FmtF4F : FmtGroupF<CodesF4> {};
+
 // ============================================= int8-activation formats
 
 // Group-scale int8 activations: xq (k bytes) then xScales (gpr floats).

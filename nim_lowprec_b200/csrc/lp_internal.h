@@ -13,6 +13,8 @@ struct DeviceInfo {
   int ordinal = -1;
   int sm_count = 0;
   int max_smem_optin = 0;
+  int smem_per_sm = 0;        // shared memory of one SM
+  int smem_reserved = 0;      // shared memory the runtime reserves per block
   int cc_major = 0, cc_minor = 0;
 };
 
@@ -25,6 +27,11 @@ struct FmtI4;
 struct FmtF4;
 struct FmtQ8_0;
 struct FmtQ4_0;
+struct FmtI8F;
+struct FmtI4F;
+struct FmtF4F;
+struct FmtQ8_0F;
+struct FmtQ4_0F;
 struct FmtQ8;
 struct FmtI4Q8;
 struct FmtQ8_0Q8;

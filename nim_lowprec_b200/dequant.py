@@ -149,6 +149,45 @@ def dequantGemvQ4_0(w, blocksPerRow, x, y):
     _gemv_blocks("dequant_gemv_q4_0", w, Q4_0_BYTES, blocksPerRow, x, y)
 
 
+# ------------------------------------------------ fp32 arithmetic mode
+
+_MODES = {"fast": N.LP_FP32_FAST, "exact": N.LP_FP32_EXACT}
+
+
+def setFp32Mode(mode: str) -> None:
+    """Arithmetic of the fp32-activation GEMVs, process-wide.
+
+    ``"fast"`` (default): block-float activations with exact integer group
+    dots, within the reference's fp32 tolerance (1e-5 relative).
+    ``"exact"``: the reference scalar path's operation order, bit-identical.
+    """
+    if mode not in _MODES:
+        raise ValueError(f"fp32 mode must be one of {sorted(_MODES)}, not {mode!r}")
+    N.check(N.lib().lp_set_fp32_mode(_MODES[mode]), "lp_set_fp32_mode")
+
+
+def fp32Mode() -> str:
+    v = int(N.lib().lp_get_fp32_mode())
+    return {b: a for a, b in _MODES.items()}[v]
+
+
+class fp32_mode:
+    """Context manager: ``with fp32_mode("exact"): ...``."""
+
+    def __init__(self, mode: str):
+        self.mode = mode
+        self.prev = None
+
+    def __enter__(self):
+        self.prev = fp32Mode()
+        setFp32Mode(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        setFp32Mode(self.prev)
+        return False
+
+
 # ====================================== int8-activation GEMVs ===========
 
 def _gemv_q8(name, w, wScales, groupSize, xq, xScales, y, wdt):

@@ -1,7 +1,8 @@
 """CUDA kernels vs the CPU oracle, through the C ABI (device and host forms).
 
 Bit-exact for every path (integer, encoder and fp32-activation GEMVs alike:
-the fp32 kernels reproduce the reference's scalar summation order), on
+every test here runs the fp32 kernels in their exact mode, which reproduces
+the reference's scalar summation order), on
   * the reference tests' own inputs (test_sdot.nim, test_parallel.nim,
     test_quant_simd.nim, test_scheme_conformance.nim goldens),
   * edge shapes (M = 1, odd M, block tails bpr = 3 mod 4, group tails),
@@ -37,8 +38,9 @@ def assert_bits(got, want):
 
 
 @pytest.fixture(autouse=True)
-def _no_device_error():
-    yield
+def _exact_fp32_and_no_device_error():
+    with L.fp32_mode("exact"):
+        yield
     assert N.device_error() == 0
 
 
