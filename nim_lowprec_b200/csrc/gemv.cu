@@ -20,7 +20,7 @@ unsigned int take_error_gemv() {
 
 namespace {
 
-constexpr int kNcw = 8;          // consumer warps per CTA (256 threads)
+constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
 constexpr int kMaxStages = 12;
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
@@ -48,7 +48,6 @@ template <> int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return q8_bytes(
 
 struct SmemLimits {
   int one = 0;  // dynamic shared bytes one CTA may use
-  int two = 0;  // ... with a second CTA resident on the same SM
 };
 
 }  // namespace
@@ -73,22 +72,29 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, one) != cudaSuccess)
       one = 48 * 1024 - 256;
     lim[slot].one = one;
-    lim[slot].two = std::min(one, di.smem_per_sm / 2 - di.smem_reserved - st_bytes);
   });
   constexpr int NC = kNcw * 32;
   // Tile height: about two (row pair, group) units per consumer thread, in
-  // whole row pairs, at most 32 rows and 32 KB of weights + scales.
+  // whole row pairs, at most 32 rows and 40 KB of weights + scales.
   const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
   int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
-  rt = std::min(rt, std::max(2, (32 * 1024) / std::max(row_total, 1)));
+  rt = std::min(rt, std::max(2, (40 * 1024) / std::max(row_total, 1)));
   rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
   p.rt = std::max(1, rt & ~1);
   p.tstride = round_up(p.gpr, 32) + 4;
   // Ordered folds take fb tiles (<= 32 rows) per pass over a ring of two
   // passes; the unordered fold goes tile by tile over four slots.
+  p.tcols = p.gpr;
+  p.wred = 0;
   if (Fmt::kFold == Fold::Tree) {
     p.fb = 1;
     p.ring = 4;
+    // consumer warps pre-reduce 32 groups when each warp holds 32 groups of
+    // one row pair for the whole launch
+    if (p.gpr % 32 == 0 && NC % p.gpr == 0) {
+      p.wred = 1;
+      p.tcols = p.gpr / 32;
+    }
   } else {
     p.fb = std::max(1, std::min(kMaxRing / 2, 32 / p.rt));
     while (p.fb > 1 && 2 * p.fb * p.rt * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
@@ -100,10 +106,7 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   const int terms_bytes = round_up(p.ring * p.rt * p.tstride * 4, 128);
   const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  // Two CTAs per SM when three stages fit beside the second CTA (so the next
-  // launch overlaps this one's tail), else all of the SM's shared memory.
-  const int budget = (lim[slot].two - fixed) / per_stage >= 3 ? lim[slot].two : lim[slot].one;
-  p.stages = std::min(kMaxStages, (budget - fixed) / per_stage);
+  p.stages = std::min(kMaxStages, (lim[slot].one - fixed) / per_stage);
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
   // Bulk copies need 16-byte aligned, 16-byte multiple rows of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);

@@ -15,8 +15,8 @@
 // parallelise freely; the fold must keep its order to stay bit-exact.
 //
 // Work layout.  Each CTA owns a contiguous, balanced range of rows (one CTA
-// per SM; the planner sizes it so two fit on an SM, which lets the next
-// launch in the stream start streaming while this one drains).  It walks its
+// per SM; under programmatic dependent launch the next launch's CTA takes
+// the SM as soon as this one exits and streams its weights at once).  It walks its
 // rows in tiles of RT consecutive rows -- one contiguous stretch of HBM, so
 // one large bulk copy (per-SM copy throughput on B200 grows with copy size:
 // copies of 16 KB and up are needed to stream at full HBM bandwidth).
@@ -56,6 +56,8 @@ struct GemvParams {
   int x_bytes;        // shared bytes for the staged activations
   int fb;             // tiles per ordered fold batch (fb * rt <= 32)
   int ring;           // term-ring slots, a multiple of fb
+  int wred;           // 1: unordered fold pre-reduced by consumer warps (32 groups each)
+  int tcols;          // term columns per row the folder sums (gpr, or gpr / 32)
   int off_w, off_s, off_t, off_b;  // shared-memory offsets (128-byte aligned)
   int stage_w_bytes, stage_s_bytes;
   float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
@@ -132,8 +134,8 @@ __device__ __forceinline__ float fold_row(const float* T, int gpr) {
 }
 
 // Unordered row sums (block-float path): L lanes per row, L the largest
-// power of two with L * rows <= 32; each lane sums a strided subset of the
-// row's terms in four chains, then the L partial sums meet by shuffles.
+// power of two with L * rows <= 32; each lane sums 4-term slices of the row
+// (four 16-byte loads in flight), then the L partial sums meet by shuffles.
 __device__ __forceinline__ void tree_fold(const float* T, int tstride, int rows, int gpr,
                                           float* y, int lane) {
   int lg = 5;
@@ -143,23 +145,62 @@ __device__ __forceinline__ void tree_fold(const float* T, int tstride, int rows,
   float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
   if (r < rows) {
     const float* row = T + r * tstride;
-    int g = sub;
-    for (; g + 3 * L < gpr; g += 4 * L) {
-      s0 = fadd(s0, row[g]);
-      s1 = fadd(s1, row[g + L]);
-      s2 = fadd(s2, row[g + 2 * L]);
-      s3 = fadd(s3, row[g + 3 * L]);
+    const int g4 = gpr & ~3;
+    int g = 4 * sub;
+    for (; g + 12 * L < g4; g += 16 * L) {
+      const float4 a = *reinterpret_cast<const float4*>(row + g);
+      const float4 b = *reinterpret_cast<const float4*>(row + g + 4 * L);
+      const float4 c = *reinterpret_cast<const float4*>(row + g + 8 * L);
+      const float4 d = *reinterpret_cast<const float4*>(row + g + 12 * L);
+      s0 = fadd(s0, fadd(fadd(a.x, b.x), fadd(c.x, d.x)));
+      s1 = fadd(s1, fadd(fadd(a.y, b.y), fadd(c.y, d.y)));
+      s2 = fadd(s2, fadd(fadd(a.z, b.z), fadd(c.z, d.z)));
+      s3 = fadd(s3, fadd(fadd(a.w, b.w), fadd(c.w, d.w)));
     }
-    for (; g < gpr; g += L) s0 = fadd(s0, row[g]);
+    for (; g < g4; g += 4 * L) {
+      const float4 a = *reinterpret_cast<const float4*>(row + g);
+      s0 = fadd(s0, a.x);
+      s1 = fadd(s1, a.y);
+      s2 = fadd(s2, a.z);
+      s3 = fadd(s3, a.w);
+    }
+    if (sub == 0)
+      for (int t = g4; t < gpr; ++t) s0 = fadd(s0, row[t]);
   }
   float s = fadd(fadd(s0, s1), fadd(s2, s3));
   for (int o = L >> 1; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(0xffffffffu, s, o));
   if (r < rows && sub == 0) y[r] = s;
 }
 
+// Unordered fold, first stage, in a consumer warp whose 32 lanes hold 32
+// consecutive groups of the same four rows (t0..t3 = rows ra, ra+1, rc,
+// rc+1): a reduce-scatter over the lanes (6 shuffles for the 4 rows) leaves
+// each row's 32-group sum in lanes 0, 8, 16 and 24, stored as column `col`
+// of the term matrix.  rc < 0: only rows ra, ra+1 exist.
+__device__ __forceinline__ void store_warp_sums(float* T, int tstride, int rows, int ra, int rc,
+                                                float t0, float t1, float t2, float t3, int col,
+                                                int lane) {
+  const bool h16 = lane & 16, h8 = lane & 8;
+  float ka = h16 ? t2 : t0, kb = h16 ? t3 : t1;
+  const float sa = h16 ? t0 : t2, sb = h16 ? t1 : t3;
+  ka = fadd(ka, __shfl_xor_sync(0xffffffffu, sa, 16));
+  kb = fadd(kb, __shfl_xor_sync(0xffffffffu, sb, 16));
+  float k = h8 ? kb : ka;
+  const float sd = h8 ? ka : kb;
+  k = fadd(k, __shfl_xor_sync(0xffffffffu, sd, 8));
+  k = fadd(k, __shfl_xor_sync(0xffffffffu, k, 4));
+  k = fadd(k, __shfl_xor_sync(0xffffffffu, k, 2));
+  k = fadd(k, __shfl_xor_sync(0xffffffffu, k, 1));
+  if ((lane & 7) == 0) {
+    const int slot = lane >> 3;
+    const int row = (slot < 2 ? ra : rc) + (slot & 1);
+    if ((slot < 2 || rc >= 0) && row < rows) T[row * tstride + col] = k;
+  }
+}
+
 // ----------------------------------------------------------- the kernel
 template <class Fmt, int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ volatile int s_abort;
   // Every bulk-copy destination is a 128-byte multiple from this base.
@@ -243,7 +284,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParam
         if (s_abort) break;
         const int r0 = row_begin + t * p.rt;
         const int rows = min(p.rt, row_end - r0);
-        tree_fold(terms + slot * p.rt * p.tstride, p.tstride, rows, p.gpr, p.y + r0, lane);
+        tree_fold(terms + slot * p.rt * p.tstride, p.tstride, rows, p.tcols, p.y + r0, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
       }
@@ -278,11 +319,13 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParam
     Fmt::stage_x(xsm, p, ct, NC);
     asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
     Fmt f;
-    f.init(p, xsm);
     // Unit q = pair * gpr + g walks q = ct, ct + NC, ...; stepped without a
-    // division per unit.
+    // division per unit.  When NC is a multiple of gpr (dg == 0) a thread
+    // keeps one group for the whole launch and takes two row pairs per step,
+    // two independent straight-line term2 calls the compiler interleaves.
     const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
     const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
+    if (dg == 0) f.prepare(p, xsm, g0);
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % p.stages;
       const int tb = t % p.ring;
@@ -295,20 +338,68 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 2) gemv_kernel(const GemvParam
       const float* S = reinterpret_cast<const float*>(sts + s * p.stage_s_bytes);
       float* T = terms + tb * p.rt * p.tstride;
       const int npairs = (rows + 1) >> 1;
-      int g = g0;
-      for (int pr = pr0; pr < npairs;) {
-        const int ra = 2 * pr;
-        const int rb = min(ra + 1, rows - 1);
-        float ta, tbv;
-        f.term2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
-                S + rb * p.gpr, g, ta, tbv);
-        T[ra * p.tstride + g] = ta;
-        if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = tbv;
-        g += dg;
-        pr += dpr;
-        if (g >= p.gpr) {
-          g -= p.gpr;
-          ++pr;
+      if (dg == 0) {
+        const int g = g0;
+        int pr = pr0;
+        for (; Fmt::kTwoPairs && pr + dpr < npairs; pr += 2 * dpr) {
+          const int ra = 2 * pr, rc = 2 * (pr + dpr);
+          const int rb = min(ra + 1, rows - 1), rd = min(rc + 1, rows - 1);
+          float t0, t1, t2, t3;
+          f.term2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                  S + rb * p.gpr, g, t0, t1);
+          f.term2(p, xsm, W + rc * p.row_bytes, W + rd * p.row_bytes, S + rc * p.gpr,
+                  S + rd * p.gpr, g, t2, t3);
+          if constexpr (Fmt::kFix) {
+            f.fix2(p, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                   S + rb * p.gpr, g, t0, t1);
+            f.fix2(p, W + rc * p.row_bytes, W + rd * p.row_bytes, S + rc * p.gpr,
+                   S + rd * p.gpr, g, t2, t3);
+          }
+          if (Fmt::kFold == Fold::Tree && p.wred) {
+            store_warp_sums(T, p.tstride, rows, ra, rc, t0, t1, t2, t3, g >> 5, lane);
+            continue;
+          }
+          T[ra * p.tstride + g] = t0;
+          if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+          T[rc * p.tstride + g] = t2;
+          if (rc + 1 < rows) T[(rc + 1) * p.tstride + g] = t3;
+        }
+        for (; pr < npairs; pr += dpr) {  // the rest one pair at a time
+          const int ra = 2 * pr;
+          const int rb = min(ra + 1, rows - 1);
+          float t0, t1;
+          f.term2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                  S + rb * p.gpr, g, t0, t1);
+          if constexpr (Fmt::kFix)
+            f.fix2(p, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                   S + rb * p.gpr, g, t0, t1);
+          if (Fmt::kFold == Fold::Tree && p.wred) {
+            store_warp_sums(T, p.tstride, rows, ra, -1, t0, t1, 0.0f, 0.0f, g >> 5, lane);
+          } else {
+            T[ra * p.tstride + g] = t0;
+            if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+          }
+        }
+      } else {
+        int g = g0;
+        for (int pr = pr0; pr < npairs;) {
+          const int ra = 2 * pr;
+          const int rb = min(ra + 1, rows - 1);
+          float t0, t1;
+          f.prepare(p, xsm, g);
+          f.term2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                  S + rb * p.gpr, g, t0, t1);
+          if constexpr (Fmt::kFix)
+            f.fix2(p, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                   S + rb * p.gpr, g, t0, t1);
+          T[ra * p.tstride + g] = t0;
+          if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+          g += dg;
+          pr += dpr;
+          if (g >= p.gpr) {
+            g -= p.gpr;
+            ++pr;
+          }
         }
       }
       __syncwarp();

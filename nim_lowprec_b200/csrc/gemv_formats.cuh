@@ -4,7 +4,13 @@
 //                the weights) rather than scales inline in ggml blocks;
 //   kFold        Serial (from 0.0, group order) or Lanes4 (ggml int8 forms);
 //   stage_x      copies the activations into shared memory once per CTA;
-//   term2        the terms of two rows that share group g.
+//   prepare      loads what a thread keeps of group g's activations into
+//                registers (called before term2 whenever g changes);
+//   term2        the terms of two rows that share the prepared group g --
+//                straight-line code, so two calls back to back interleave;
+//   kFix / fix2  formats whose term2 can meet a group it does not handle
+//                (block-float groups with a non-finite activation) redo those
+//                terms in fix2.
 //
 // Exactness notes.  fp32 chains use mul.rn then add.rn (two roundings, no
 // FMA), in the reference's scalar element order.  Small integers become
@@ -116,14 +122,17 @@ struct StageXF32 {
 struct FmtI8 : StageXF32 {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;  // 64 registers of duplicated activations
   XPairs xp;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs == 32) xp.load(reinterpret_cast<const float*>(xsm), g);
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float* sA,
                                         const float* sB, int g, float& tA, float& tB) {
     const float* x = reinterpret_cast<const float*>(xsm);
     if (p.gs == 32) {
-      xp.load(x, g);
       const uint4* pa = reinterpret_cast<const uint4*>(wA + g * 32);
       const uint4* pb = reinterpret_cast<const uint4*>(wB + g * 32);
       const uint4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
@@ -164,14 +173,17 @@ struct FmtI8 : StageXF32 {
 struct FmtI4 : StageXF32 {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;  // 64 registers of duplicated activations
   XPairs xp;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs == 32) xp.load(reinterpret_cast<const float*>(xsm), g);
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float* sA,
                                         const float* sB, int g, float& tA, float& tB) {
     const float* x = reinterpret_cast<const float*>(xsm);
     if (p.gs == 32) {
-      xp.load(x, g);
       const uint4 a = *reinterpret_cast<const uint4*>(wA + g * 16);
       const uint4 bq = *reinterpret_cast<const uint4*>(wB + g * 16);
       const uint32_t A[4] = {a.x, a.y, a.z, a.w};
@@ -224,8 +236,12 @@ struct FmtI4 : StageXF32 {
 struct FmtF4 : StageXF32 {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;  // 64 registers of duplicated activations
   XPairs xp;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs == 32) xp.load(reinterpret_cast<const float*>(xsm), g);
+  }
   static __device__ __forceinline__ uint32_t lut4(uint32_t codes16) {
     // positive codes 0..7: 2v + 12 = 12,13,14,15,16,18,20,24
     // negative codes 8..15 (index c ^ 8): 12,11,10,9,8,6,4,0
@@ -237,7 +253,6 @@ struct FmtF4 : StageXF32 {
                                         const float* sB, int g, float& tA, float& tB) {
     const float* x = reinterpret_cast<const float*>(xsm);
     if (p.gs == 32) {
-      xp.load(x, g);
       const uint4 a = *reinterpret_cast<const uint4*>(wA + g * 16);
       const uint4 bq = *reinterpret_cast<const uint4*>(wB + g * 16);
       const uint32_t A[4] = {a.x, a.y, a.z, a.w};
@@ -282,12 +297,15 @@ struct FmtF4 : StageXF32 {
 struct FmtQ8_0 : StageXF32 {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;  // 64 registers of duplicated activations
   XPairs xp;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams&, const uint8_t* xsm, int g) {
+    xp.load(reinterpret_cast<const float*>(xsm), g);
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float*,
                                         const float*, int g, float& tA, float& tB) {
-    xp.load(reinterpret_cast<const float*>(xsm), g);
     uint32_t dA, dB, A[8], B[8];
     load_q8_0(wA + g * 34, dA, A);
     load_q8_0(wB + g * 34, dB, B);
@@ -316,12 +334,15 @@ struct FmtQ8_0 : StageXF32 {
 struct FmtQ4_0 : StageXF32 {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;  // 64 registers of duplicated activations
   XPairs xp;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams&, const uint8_t* xsm, int g) {
+    xp.load(reinterpret_cast<const float*>(xsm), g);
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float*,
                                         const float*, int g, float& tA, float& tB) {
-    xp.load(reinterpret_cast<const float*>(xsm), g);
     uint32_t dA, dB, A[4], B[4];
     load_q4_0(wA + g * 18, dA, A);
     load_q4_0(wB + g * 18, dB, B);
@@ -354,32 +375,36 @@ struct FmtQ4_0 : StageXF32 {
 // bit-exact mode).  Each activation group j (the weight group) is written as
 // integers X = rint(x * 2^(22 - E_j)) with 2^E_j > max|x| over the group, so
 // |X| <= 2^22 and the representation error is at most 2^-23 of the group's
-// largest magnitude.  X is split into three balanced signed bytes
-// X = d0 + 256 d1 + 65536 d2 (planes P0..P2), and every group dot becomes
-// three exact int32 dp4a sums of the integer weight codes against the
-// planes.  Formats whose codes carry an offset (Q4_0: u = w + 8; I4:
-// u = w + 8; F4: u = 2w + 12) start each plane sum at -offset * sum(d_p).
-// The group value is (65536 D2 + 256 D1 + D0) * 2^(E_j - 22); its only
-// roundings are the final int->float conversion and the scaling, so it is
-// within a few ulp of the exact dot -- well inside the reference's fp32
-// tolerance (1e-5 relative), not bit-identical to its sequential order.
-// Groups holding a non-finite activation are marked (scale NaN) and take
-// the scalar sequential path from global memory, so inf/NaN propagate as in
-// the reference.
+// largest magnitude.  X's two's-complement bytes are the digits:
+// X = d0 + 256 d1 + 65536 d2 with d0, d1 unsigned and d2 = X >> 16 signed
+// (planes P0..P2), and every group dot becomes three exact int32 dp4a sums
+// of the integer weight codes against the planes.  Formats whose codes carry
+// an offset (Q4_0: u = w + 8; I4: u = w + 8; F4: u = 2w + 12) start each
+// plane sum at -offset * sum(d_p).  The group value is
+// (65536 D2 + 256 D1 + D0) * 2^(E_j - 22); its only roundings are the final
+// int->float conversions and the scaling, so it is within a few ulp of the
+// exact dot -- well inside the reference's fp32 tolerance (1e-5 relative),
+// not bit-identical to its sequential order.
+// Groups holding a non-finite activation, or one of magnitude 2^100 or more
+// (where the reference's fp32 partial sums can overflow), are marked (scale
+// NaN) and take the scalar sequential path from global memory, so inf, NaN
+// and overflow come out as in the reference.
 
 struct GInfo {
-  float s;       // 2^(E - 22); 0 for an all-zero group; NaN: non-finite x
-  int sx[3];     // sum of the group's digits in each plane
+  float s;       // 2^(E - 22); 0 for an all-zero group; NaN: sequential path
+  int sx[3];     // sum of the group's digits in each plane (groups other than
+                 // 32 wide; 32-wide groups leave them to PlaneCache)
 };
+
+constexpr uint32_t kBigBits = (100u + 127u) << 23;  // |x| >= 2^100
 
 __device__ __forceinline__ int planes_stride(const GemvParams& p) { return (p.k + 15) & ~15; }
 
-// Smallest E with |m| < 2^E for finite m > 0.
-__device__ __forceinline__ int exp_above(float m) {
-  const uint32_t b = __float_as_uint(m) & 0x7FFFFFFFu;
-  const int e = static_cast<int>(b >> 23);
+// Smallest E with m < 2^E for the bit pattern mb of a finite m > 0.
+__device__ __forceinline__ int exp_above_bits(uint32_t mb) {
+  const int e = static_cast<int>(mb >> 23);
   if (e) return e - 126;
-  return 32 - __clz(static_cast<int>(b)) - 149;  // subnormal: b * 2^-149
+  return 32 - __clz(static_cast<int>(mb)) - 149;  // subnormal: mb * 2^-149
 }
 
 // 2^e as float for e in [-149, 127]; 0 below.
@@ -389,20 +414,29 @@ __device__ __forceinline__ float pow2f(int e) {
   return 0.0f;
 }
 
-struct Digits {
-  int d[3];
-};
-__device__ __forceinline__ Digits split3(int X) {
-  Digits r;
-  r.d[0] = ((X + 128) & 255) - 128;
-  const int X1 = (X - r.d[0]) >> 8;
-  r.d[1] = ((X1 + 128) & 255) - 128;
-  r.d[2] = (X1 - r.d[1]) >> 8;
-  return r;
+// rint(x * 2^sh) for |x * 2^sh| < 2^22 and sh in [-106, 171], in fp32 only:
+// two exact power-of-two scalings (the first may only lose bits of values far
+// below one half, which round to 0 either way), then round-to-nearest-even by
+// adding 1.5 * 2^23, whose bit pattern then holds the integer.
+__device__ __forceinline__ int scaled_rint(float x, float sa, float sb) {
+  const float f = (x * sa) * sb;
+  return __float_as_int(f + 12582912.0f) - 0x4B400000;
+}
+__device__ __forceinline__ void scale_pair(int sh, float& sa, float& sb) {
+  const int a = min(sh, 127);
+  sa = pow2f(a);
+  sb = pow2f(sh - a);
 }
 
-__device__ __forceinline__ double pow2d(int e) {  // e in [-1022, 1023]
-  return __hiloint2double((e + 1023) << 20, 0);
+// Group header from the largest |x| bit pattern of the group.
+__device__ __forceinline__ GInfo group_info(uint32_t mb, const int (&sum)[3], bool special) {
+  GInfo g;
+  g.s = special ? __uint_as_float(0x7FC00000u)
+                : (mb ? pow2f(exp_above_bits(mb) - 22) : 0.0f);
+  g.sx[0] = sum[0];
+  g.sx[1] = sum[1];
+  g.sx[2] = sum[2];
+  return g;
 }
 
 // kEvenOdd: within each 8-element chunk the planes hold the even columns
@@ -414,102 +448,90 @@ struct StageXPlanes {
     const int c = k & 7;
     return (k & ~7) | ((c & 1) << 2) | (c >> 1);
   }
+  // Four lanes per 32-element group, eight activations each: the two 16-byte
+  // loads of every lane go out together (under the weight stream an
+  // activation load waits on the order of a microsecond) and only the group
+  // maximum crosses lanes (two shuffles).  The digit sums are left to the
+  // consumer threads (PlaneCache), which need them once per group.
+  static __device__ __noinline__ void stage_g32(const float* x, int gpr, int8_t* P, int Kp,
+                                                GInfo* gi, int tid, int nthr) {
+    const int ntask = gpr * 4;
+    for (int q0 = tid & ~31; q0 < ntask; q0 += nthr) {
+      const int q = q0 + (tid & 31);
+      const bool valid = q < ntask;
+      const float4* xv4 = reinterpret_cast<const float4*>(x) + 2 * q;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 f0 = valid ? __ldg(xv4) : z, f1 = valid ? __ldg(xv4 + 1) : z;
+      const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+      uint32_t mb = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+      const bool special = mb >= kBigBits;  // also inf / NaN
+      float sa, sb;
+      scale_pair(22 - (mb ? exp_above_bits(mb) : 0), sa, sb);
+      uint32_t word[3][2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        int X[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) X[i] = special ? 0 : scaled_rint(v[4 * c + i], sa, sb);
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+          const uint32_t sel = 0x0040u + 0x11u * pl;
+          word[pl][c] = prmt(prmt(X[0], X[1], sel), prmt(X[2], X[3], sel), 0x5410u);
+        }
+      }
+      if (valid) {
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+          uint32_t a = word[pl][0], b = word[pl][1];
+          if (kEvenOdd) {  // the 8-element chunk: even columns, then odd
+            const uint32_t e = prmt(a, b, 0x6420u), o = prmt(a, b, 0x7531u);
+            a = e;
+            b = o;
+          }
+          reinterpret_cast<uint2*>(P + pl * Kp)[q] = make_uint2(a, b);
+        }
+        if ((q & 3) == 0) {
+          GInfo g;
+          g.s = special ? __uint_as_float(0x7FC00000u) : (mb ? pow2f(exp_above_bits(mb) - 22) : 0.0f);
+          g.sx[0] = g.sx[1] = g.sx[2] = 0;
+          gi[q >> 2] = g;
+        }
+      }
+    }
+  }
+
   static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
     const float* x = static_cast<const float*>(p.x);
     const int Kp = planes_stride(p);
     int8_t* P = reinterpret_cast<int8_t*>(xsm);
     GInfo* gi = reinterpret_cast<GInfo*>(xsm + 3 * Kp);
     const int gs = p.gs;
-    const int lanes = gs >> 2;  // one lane per 4 elements when a group is 8..128 wide
-    const bool vec = (gs & (gs - 1)) == 0 && gs >= 8 && gs <= 128 &&
-                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    if (vec) {
-      const int ntask = p.k >> 2;
-      const int lane = tid & 31;
-      for (int q0 = tid & ~31; q0 < ntask; q0 += nthr) {
-        const int q = q0 + lane;
-        const bool valid = q < ntask;
-        float4 v = valid ? __ldg(reinterpret_cast<const float4*>(x) + q)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        int nf = !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        for (int o = 1; o < lanes; o <<= 1) {
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          nf |= __shfl_xor_sync(0xffffffffu, nf, o);
-        }
-        const int E = (m > 0.0f && !nf) ? exp_above(m) : 0;
-        const double sc = pow2d(22 - E);
-        const float xv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t word[3] = {0u, 0u, 0u};
-        int sum[3] = {0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int X = nf ? 0 : __double2int_rn(static_cast<double>(xv[i]) * sc);
-          const Digits dg = split3(X);
-#pragma unroll
-          for (int pl = 0; pl < 3; ++pl) {
-            word[pl] |= (static_cast<uint32_t>(dg.d[pl]) & 255u) << (8 * i);
-            sum[pl] += dg.d[pl];
-          }
-        }
-        if (valid) {
-          if (!kEvenOdd) {
-#pragma unroll
-            for (int pl = 0; pl < 3; ++pl)
-              reinterpret_cast<uint32_t*>(P + pl * Kp)[q] = word[pl];
-          } else {
-            // elements 4h..4h+3 of chunk c: evens to 2h, 2h+1; odds to 4+2h, 5+2h
-            const int base = (q >> 1) * 8, h = q & 1;
-#pragma unroll
-            for (int pl = 0; pl < 3; ++pl) {
-              const uint32_t ev = prmt(word[pl], 0u, 0x0020u);
-              const uint32_t od = prmt(word[pl], 0u, 0x0031u);
-              reinterpret_cast<uint16_t*>(P + pl * Kp + base + 2 * h)[0] = static_cast<uint16_t>(ev);
-              reinterpret_cast<uint16_t*>(P + pl * Kp + base + 4 + 2 * h)[0] = static_cast<uint16_t>(od);
-            }
-          }
-        }
-        for (int o = 1; o < lanes; o <<= 1) {
-#pragma unroll
-          for (int pl = 0; pl < 3; ++pl) sum[pl] += __shfl_xor_sync(0xffffffffu, sum[pl], o);
-        }
-        if (valid && (q & (lanes - 1)) == 0) {
-          GInfo g;
-          g.s = nf ? __uint_as_float(0x7FC00000u) : (m > 0.0f ? pow2f(E - 22) : 0.0f);
-          g.sx[0] = sum[0];
-          g.sx[1] = sum[1];
-          g.sx[2] = sum[2];
-          gi[q / lanes] = g;
-        }
-      }
+    if (gs == 32 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      stage_g32(x, p.gpr, P, Kp, gi, tid, nthr);
     } else {
       for (int j = tid; j < p.gpr; j += nthr) {
         const float* xg = x + j * gs;
-        int nf = 0;
-        float m = 0.0f;
-        for (int i = 0; i < gs; ++i) {
-          nf |= !isfinite(xg[i]);
-          m = fmaxf(m, fabsf(xg[i]));
-        }
-        const int E = (m > 0.0f && !nf) ? exp_above(m) : 0;
-        const double sc = pow2d(22 - E);
+        uint32_t mb = 0;
+        for (int i = 0; i < gs; ++i) mb = max(mb, __float_as_uint(xg[i]) & 0x7FFFFFFFu);
+        const bool special = mb >= kBigBits;
+        float sa, sb;
+        scale_pair(22 - (mb ? exp_above_bits(mb) : 0), sa, sb);
         int sum[3] = {0, 0, 0};
         for (int i = 0; i < gs; ++i) {
-          const int X = nf ? 0 : __double2int_rn(static_cast<double>(xg[i]) * sc);
-          const Digits dg = split3(X);
+          const int X = special ? 0 : scaled_rint(xg[i], sa, sb);
+          const int d[3] = {X & 255, (X >> 8) & 255, X >> 16};
           const int at = pos(j * gs + i);
 #pragma unroll
           for (int pl = 0; pl < 3; ++pl) {
-            P[pl * Kp + at] = static_cast<int8_t>(dg.d[pl]);
-            sum[pl] += dg.d[pl];
+            P[pl * Kp + at] = static_cast<int8_t>(d[pl]);
+            sum[pl] += d[pl];
           }
         }
-        GInfo g;
-        g.s = nf ? __uint_as_float(0x7FC00000u) : (m > 0.0f ? pow2f(E - 22) : 0.0f);
-        g.sx[0] = sum[0];
-        g.sx[1] = sum[1];
-        g.sx[2] = sum[2];
-        gi[j] = g;
+        gi[j] = group_info(mb, sum, special);
       }
     }
   }
@@ -535,15 +557,25 @@ struct PlaneCache {
       P[pl][0] = u0.x; P[pl][1] = u0.y; P[pl][2] = u0.z; P[pl][3] = u0.w;
       P[pl][4] = u1.x; P[pl][5] = u1.y; P[pl][6] = u1.z; P[pl][7] = u1.w;
     }
-    const GInfo gi = reinterpret_cast<const GInfo*>(xsm + 3 * Kp)[grp];
-    s = gi.s;
+    s = reinterpret_cast<const GInfo*>(xsm + 3 * Kp)[grp].s;
+    if (kOff) {
+      int sum[3] = {0, 0, 0};
 #pragma unroll
-    for (int pl = 0; pl < 3; ++pl) b[pl] = -kOff * gi.sx[pl];
+      for (int j = 0; j < 8; ++j) {
+        sum[0] = dp4a_uu(0x01010101u, P[0][j], sum[0]);
+        sum[1] = dp4a_uu(0x01010101u, P[1][j], sum[1]);
+        sum[2] = dp4a_us(0x01010101u, P[2][j], sum[2]);
+      }
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) b[pl] = -kOff * sum[pl];
+    } else {
+      b[0] = b[1] = b[2] = 0;
+    }
   }
 };
 
-// (65536 D2 + 256 D1 + D0) as float.  kSmall: |D1| < 2^22 so 256 D1 + D0
-// stays in int32 (32-element groups).
+// (65536 D2 + 256 D1 + D0) as float.  kSmall: 32-element groups, where
+// |D1| <= 32 * 255 * 255 < 2^21 so 256 D1 + D0 stays in int32.
 template <bool kSmall>
 __device__ __forceinline__ float bf_value(int a0, int a1, int a2) {
   if (kSmall)
@@ -551,17 +583,18 @@ __device__ __forceinline__ float bf_value(int a0, int a1, int a2) {
   return fmaf(__int2float_rn(a2), 65536.0f, fmaf(__int2float_rn(a1), 256.0f, __int2float_rn(a0)));
 }
 
-// Three plane sums of 4 codes against plane words w0..w2.
+// Three plane sums of 4 codes against plane words w0..w2 (planes 0 and 1
+// hold unsigned digits, plane 2 signed ones); codes unsigned (US) or signed (SS).
 #define LP_DP3_US(acc, codes, w0, w1, w2)      \
   do {                                         \
-    acc[0] = dp4a_us(codes, w0, acc[0]);       \
-    acc[1] = dp4a_us(codes, w1, acc[1]);       \
+    acc[0] = dp4a_uu(codes, w0, acc[0]);       \
+    acc[1] = dp4a_uu(codes, w1, acc[1]);       \
     acc[2] = dp4a_us(codes, w2, acc[2]);       \
   } while (0)
 #define LP_DP3_SS(acc, codes, w0, w1, w2)      \
   do {                                         \
-    acc[0] = dp4a_ss(codes, w0, acc[0]);       \
-    acc[1] = dp4a_ss(codes, w1, acc[1]);       \
+    acc[0] = dp4a_su(codes, w0, acc[0]);       \
+    acc[1] = dp4a_su(codes, w1, acc[1]);       \
     acc[2] = dp4a_ss(codes, w2, acc[2]);       \
   } while (0)
 
@@ -588,18 +621,23 @@ __device__ __forceinline__ float seq_q8_0(const uint8_t* blk, const float* xg) {
 struct FmtQ4_0F : StageXPlanes<false> {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Tree;
+  static constexpr bool kFix = true;
+  static constexpr bool kTwoPairs = true;
   PlaneCache<8> pc;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
-  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
-                                        const uint8_t* wA, const uint8_t* wB, const float*,
-                                        const float*, int g, float& tA, float& tB) {
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
     pc.load(p, xsm, g);
+  }
+  __device__ __forceinline__ void fix2(const GemvParams& p, const uint8_t* wA, const uint8_t* wB,
+                                       const float*, const float*, int g, float& tA, float& tB) {
     if (isnan(pc.s)) {
       const float* xg = static_cast<const float*>(p.x) + g * 32;
       tA = seq_q4_0(wA + g * 18, xg);
       tB = seq_q4_0(wB + g * 18, xg);
-      return;
     }
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*,
+                                        const uint8_t* wA, const uint8_t* wB, const float*,
+                                        const float*, int g, float& tA, float& tB) {
     uint32_t dA, dB, A[4], B[4];
     load_q4_0(wA + g * 18, dA, A);
     load_q4_0(wB + g * 18, dB, B);
@@ -623,18 +661,23 @@ struct FmtQ4_0F : StageXPlanes<false> {
 struct FmtQ8_0F : StageXPlanes<false> {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Tree;
+  static constexpr bool kFix = true;
+  static constexpr bool kTwoPairs = true;
   PlaneCache<0> pc;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
-  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
-                                        const uint8_t* wA, const uint8_t* wB, const float*,
-                                        const float*, int g, float& tA, float& tB) {
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
     pc.load(p, xsm, g);
+  }
+  __device__ __forceinline__ void fix2(const GemvParams& p, const uint8_t* wA, const uint8_t* wB,
+                                       const float*, const float*, int g, float& tA, float& tB) {
     if (isnan(pc.s)) {
       const float* xg = static_cast<const float*>(p.x) + g * 32;
       tA = seq_q8_0(wA + g * 34, xg);
       tB = seq_q8_0(wB + g * 34, xg);
-      return;
     }
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*,
+                                        const uint8_t* wA, const uint8_t* wB, const float*,
+                                        const float*, int g, float& tA, float& tB) {
     uint32_t dA, dB, A[8], B[8];
     load_q8_0(wA + g * 34, dA, A);
     load_q8_0(wB + g * 34, dB, B);
@@ -658,8 +701,21 @@ template <class Codes>
 struct FmtGroupF : StageXPlanes<Codes::kEvenOdd> {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Tree;
+  static constexpr bool kFix = true;
+  static constexpr bool kTwoPairs = true;
   PlaneCache<Codes::kOff> pc;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs == 32) pc.load(p, xsm, g);
+  }
+  __device__ __forceinline__ void fix2(const GemvParams& p, const uint8_t* wA, const uint8_t* wB,
+                                       const float* sA, const float* sB, int g, float& tA,
+                                       float& tB) {
+    if (p.gs == 32 && isnan(pc.s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * 32;
+      tA = Codes::seq(wA, g, 32, xg, sA[g]);
+      tB = Codes::seq(wB, g, 32, xg, sB[g]);
+    }
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float* sA,
                                         const float* sB, int g, float& tA, float& tB) {
@@ -667,23 +723,23 @@ struct FmtGroupF : StageXPlanes<Codes::kEvenOdd> {
     float s;
     int a[3], c[3];
     if (p.gs == 32) {
-      pc.load(p, xsm, g);
       s = pc.s;
-      if (!isnan(s)) {
 #pragma unroll
-        for (int pl = 0; pl < 3; ++pl) a[pl] = c[pl] = pc.b[pl];
+      for (int pl = 0; pl < 3; ++pl) a[pl] = c[pl] = pc.b[pl];
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t ua[2], ub[2];
-          Codes::get(wA, g * 32 + 8 * ch, ua);
-          Codes::get(wB, g * 32 + 8 * ch, ub);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t ua[2], ub[2];
+        Codes::get(wA, g * 32 + 8 * ch, ua);
+        Codes::get(wB, g * 32 + 8 * ch, ub);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            Codes::dp3(a, ua[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
-            Codes::dp3(c, ub[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
-          }
+        for (int h = 0; h < 2; ++h) {
+          Codes::dp3(a, ua[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
+          Codes::dp3(c, ub[h], pc.P[0][2 * ch + h], pc.P[1][2 * ch + h], pc.P[2][2 * ch + h]);
         }
       }
+      tA = bf_value<true>(a[0], a[1], a[2]) * (Codes::scale(sA[g]) * s);
+      tB = bf_value<true>(c[0], c[1], c[2]) * (Codes::scale(sB[g]) * s);
+      return;
     } else {
       const GInfo gi = reinterpret_cast<const GInfo*>(xsm + 3 * Kp)[g];
       s = gi.s;
@@ -710,10 +766,8 @@ struct FmtGroupF : StageXPlanes<Codes::kEvenOdd> {
       tB = Codes::seq(wB, g, p.gs, xg, sB[g]);
       return;
     }
-    const float va = p.gs == 32 ? bf_value<true>(a[0], a[1], a[2]) : bf_value<false>(a[0], a[1], a[2]);
-    const float vb = p.gs == 32 ? bf_value<true>(c[0], c[1], c[2]) : bf_value<false>(c[0], c[1], c[2]);
-    tA = va * (Codes::scale(sA[g]) * s);
-    tB = vb * (Codes::scale(sB[g]) * s);
+    tA = bf_value<false>(a[0], a[1], a[2]) * (Codes::scale(sA[g]) * s);
+    tB = bf_value<false>(c[0], c[1], c[2]) * (Codes::scale(sB[g]) * s);
   }
 };
 
@@ -814,23 +868,25 @@ struct StageXQ8 {
 struct FmtQ8 : StageXQ8 {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = true;
   int cg = -1;
   uint32_t X[8];
   float xsg;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs != 32 || g == cg) return;
+    cg = g;
+    const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
+    const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
+    X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
+    X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
+    xsg = xscales(p, xsm)[g];
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float* sA,
                                         const float* sB, int g, float& tA, float& tB) {
     const float* xs = xscales(p, xsm);
     if (p.gs == 32) {
-      if (g != cg) {
-        cg = g;
-        const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
-        const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
-        X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
-        X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
-        xsg = xs[g];
-      }
       const uint4* pa = reinterpret_cast<const uint4*>(wA + g * 32);
       const uint4* pb = reinterpret_cast<const uint4*>(wB + g * 32);
       const uint4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
@@ -867,32 +923,34 @@ struct FmtQ8 : StageXQ8 {
 struct FmtI4Q8 : StageXQ8 {
   static constexpr bool kScales = true;
   static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = true;
   int cg = -1;
   uint32_t XE[4], XO[4];
   int sumx8;
   float xsg;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (p.gs != 32 || g == cg) return;
+    cg = g;
+    const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
+    const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
+    const uint32_t X[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    int sx = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      XE[j] = prmt(X[2 * j], X[2 * j + 1], 0x6420u);
+      XO[j] = prmt(X[2 * j], X[2 * j + 1], 0x7531u);
+      sx = dp4a_us(0x01010101u, X[2 * j], sx);
+      sx = dp4a_us(0x01010101u, X[2 * j + 1], sx);
+    }
+    sumx8 = 8 * sx;
+    xsg = xscales(p, xsm)[g];
+  }
   __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
                                         const uint8_t* wA, const uint8_t* wB, const float* sA,
                                         const float* sB, int g, float& tA, float& tB) {
     const float* xs = xscales(p, xsm);
     if (p.gs == 32) {
-      if (g != cg) {
-        cg = g;
-        const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
-        const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
-        const uint32_t X[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        int sx = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          XE[j] = prmt(X[2 * j], X[2 * j + 1], 0x6420u);
-          XO[j] = prmt(X[2 * j], X[2 * j + 1], 0x7531u);
-          sx = dp4a_us(0x01010101u, X[2 * j], sx);
-          sx = dp4a_us(0x01010101u, X[2 * j + 1], sx);
-        }
-        sumx8 = 8 * sx;
-        xsg = xs[g];
-      }
       const uint4 a = *reinterpret_cast<const uint4*>(wA + g * 16);
       const uint4 bq = *reinterpret_cast<const uint4*>(wB + g * 16);
       const uint32_t A[4] = {a.x, a.y, a.z, a.w};
@@ -945,21 +1003,23 @@ struct StageXBlocks {
 struct FmtQ8_0Q8 : StageXBlocks {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Lanes4;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = true;
   int cg = -1;
   uint32_t X[8];
   float xdg;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
-  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (g == cg) return;
+    cg = g;
+    const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
+    const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
+    X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
+    X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
+    xdg = xd(p, xsm)[g];
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*,
                                         const uint8_t* wA, const uint8_t* wB, const float*,
                                         const float*, int g, float& tA, float& tB) {
-    if (g != cg) {
-      cg = g;
-      const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
-      const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
-      X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
-      X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
-      xdg = xd(p, xsm)[g];
-    }
     uint32_t dA, dB, A[8], B[8];
     load_q8_0(wA + g * 34, dA, A);
     load_q8_0(wB + g * 34, dB, B);
@@ -979,26 +1039,28 @@ struct FmtQ8_0Q8 : StageXBlocks {
 struct FmtQ4_0Q8 : StageXBlocks {
   static constexpr bool kScales = false;
   static constexpr Fold kFold = Fold::Lanes4;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = true;
   int cg = -1;
   uint32_t X[8];
   int sumx8;
   float xdg;
-  __device__ void init(const GemvParams&, const uint8_t*) {}
-  __device__ __forceinline__ void term2(const GemvParams& p, const uint8_t* xsm,
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    if (g == cg) return;
+    cg = g;
+    const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
+    const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
+    X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
+    X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
+    int sx = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sx = dp4a_us(0x01010101u, X[j], sx);
+    sumx8 = 8 * sx;
+    xdg = xd(p, xsm)[g];
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*,
                                         const uint8_t* wA, const uint8_t* wB, const float*,
                                         const float*, int g, float& tA, float& tB) {
-    if (g != cg) {
-      cg = g;
-      const uint4 u0 = reinterpret_cast<const uint4*>(xsm + g * 32)[0];
-      const uint4 u1 = reinterpret_cast<const uint4*>(xsm + g * 32)[1];
-      X[0] = u0.x; X[1] = u0.y; X[2] = u0.z; X[3] = u0.w;
-      X[4] = u1.x; X[5] = u1.y; X[6] = u1.z; X[7] = u1.w;
-      int sx = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sx = dp4a_us(0x01010101u, X[j], sx);
-      sumx8 = 8 * sx;
-      xdg = xd(p, xsm)[g];
-    }
     uint32_t dA, dB, A[4], B[4];
     load_q4_0(wA + g * 18, dA, A);
     load_q4_0(wB + g * 18, dB, B);

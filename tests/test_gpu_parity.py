@@ -213,7 +213,8 @@ def test_gemv_q8_i4q8_q8_0_split_random(M, K):
 # ------------------------------------------- fp32-activation GEMVs ------
 
 def _fp32_cases():
-    return [(1, 64), (7, 96), (5, 384), (37, 4096), (300, 512), (1024, 4096)]
+    # 2960 rows = 20 per CTA: several row pairs per consumer thread per tile
+    return [(1, 64), (7, 96), (5, 384), (37, 4096), (300, 512), (1024, 4096), (2960, 4096)]
 
 
 @pytest.mark.parametrize("M,K", _fp32_cases())
