@@ -129,7 +129,9 @@ int lp_get_fp32_mode(void) { return g_fp32_mode.load(); }
 
 int lp_device_error(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LP_ERR_CUDA;
-  const unsigned int e = lp::take_error_gemv();
+  unsigned int e = lp::take_error_gemv();
+  const unsigned int e2 = lp::take_error_gemm_tc();
+  if (!e) e = e2;
   return static_cast<int>(e);
 }
 
@@ -274,6 +276,10 @@ static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, in
   if (bad(w, w_len) || bad(ws, ws_len) || bad(xq, xq_len) || bad(xs, xs_len) || bad(y, y_len))
     return LP_ERR_ARG;
   LP_VALIDATED();
+  if (!i4) {
+    const int r = lp::launch_gemm_tc(static_cast<const int8_t*>(w), ws, gs, xq, xs, n, y, m, k, S(st));
+    if (r != LP_ERR_UNSUPPORTED) return r;
+  }
   return lp::launch_gemm(static_cast<const uint8_t*>(w), i4, ws, gs, xq, xs, n, y, m, k, S(st));
 }
 

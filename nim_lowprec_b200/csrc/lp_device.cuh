@@ -125,6 +125,11 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 // Rounded packed product a*b computed as fma(a, b, z) with z = -0.0 supplied
 // at run time (a kernel parameter).  fma(a, b, -0) is exactly round(a*b),
 // signed zeros included, and because the compiler cannot see that z is zero

@@ -53,12 +53,15 @@ int launch_quantize_packed(const float* x, int64_t n, const float* scales, int64
 int launch_dequantize_blocks(const uint8_t* blocks, int64_t nblocks, int q4, float* dst,
                              cudaStream_t st);
 
-// GEMM (gemm.cu)
+// GEMM (gemm_tc.cu: tcgen05, LP_ERR_UNSUPPORTED outside its shapes; gemm.cu: CUDA cores)
+int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* xq,
+                   const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
 int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
                 const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
 
 // error words of the translation units whose kernels wait (read + clear)
 unsigned int take_error_gemv();
+unsigned int take_error_gemm_tc();
 
 // Records the CUDA error text for lp_last_error_detail() and maps to a status.
 void note_cuda_error(cudaError_t e);

@@ -349,6 +349,22 @@ def test_gemm_config3_full(n):
     assert_bits(to_host(y), want)
 
 
+@pytest.mark.parametrize("M,K,n", [(128, 128, 16), (128, 128, 8), (129, 512, 5), (300, 256, 64),
+                                   (256, 512, 100), (128, 4096, 512), (1, 128, 1), (257, 384, 65)])
+def test_gemm_q8_tensor_core_shapes(M, K, n):
+    """32-wide groups with K a multiple of 128 run on tcgen05 (ragged M and n
+    tiles included); bit-exact like every other path."""
+    w = weights(M + K + n, M * K)
+    x = acts(M + K + n, K * n)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)
+    want = O.dequantGemmQ8(wq, wd, 32, xq, xd, n)
+    d = to_dev(wq, wd, xq, xd)
+    y = dev_y(M * n)
+    L.dequantGemmQ8(*d[:2], 32, *d[2:], n, y)
+    assert_bits(to_host(y), want)
+
+
 def test_gemm_column_equals_gemv_on_device():
     """test_sdot.nim:243-282 on the device: every GEMM column is the GEMV."""
     M, K, n = 129, 512, 5
