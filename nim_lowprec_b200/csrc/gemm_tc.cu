@@ -41,7 +41,7 @@ constexpr int kThreads = 32 * (4 + kEpiWarps);
 // Stages: narrow tiles are few (one per 128 rows) and must keep more bytes in
 // flight per SM.
 template <int NT>
-constexpr int stages_for() { return NT <= 16 ? 10 : 6; }
+constexpr int stages_for() { return NT <= 16 ? 10 : 8; }
 
 // Tensor-memory columns per CTA: 16-column tiles take half of TMEM, so two
 // CTAs can share an SM; wider tiles take all of it.
@@ -223,8 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int h = (warp - 4) >> 2;          // column slice
     const int et = threadIdx.x - 128;
     // activation scales of this column tile, transposed: xsT[g][c]
+    // (consecutive threads take consecutive columns: conflict-free stores)
     for (int idx = et; idx < NT * a.gpr; idx += kEpiWarps * 32) {
-      const int c = idx / a.gpr, g = idx - c * a.gpr;
+      const int g = idx / NT, c = idx - g * NT;
       xsT[g * NT + c] = (n0 + c < a.n) ? a.xs[static_cast<int64_t>(n0 + c) * a.gpr + g] : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
@@ -406,7 +407,7 @@ int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* 
     return launch_nt<16>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
                          static_cast<int>(k), st);
   }
-  return launch_nt<64>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
+  return launch_nt<32>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
                        static_cast<int>(k), st);
 }
 
