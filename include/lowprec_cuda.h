@@ -245,6 +245,67 @@ int lph_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int
 int lph_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
                        int64_t group_size, int8_t *dst, int64_t dst_len);
 
+/* ======================= LpPool: row-sharded forms across GPUs ======== *
+ * One process (rank) per GPU of a box.  Rank r owns the rows
+ * [per*r, per*r + per) of every weight matrix, per = m div P, and the last
+ * rank the remainder -- the slicing of parallel.nim:118-124, so sharded ==
+ * serial bit for bit.  A pooled call takes this rank's weight (and weight
+ * scale) row slice, the whole activations and the whole y; it computes the
+ * slice's rows and gathers every rank's rows into y over NCCL, in stream
+ * order.  Replaces LpPool / initPool / shutdown (parallel.nim:82-184) and the
+ * pooled and per-call par* procs (:186-474).  NCCL is loaded when a pool is
+ * created; without it these calls return LP_ERR_NCCL. */
+typedef struct lp_pool *lp_pool_t;
+
+/* The row slice of rank `rank` among `nranks` for m rows (parallel.nim:118-124). */
+int lp_pool_rows(int64_t m, int nranks, int rank, int64_t *begin, int64_t *end);
+/* 128-byte NCCL unique id: create on one rank, hand to all (e.g. a torch store). */
+int lp_pool_unique_id(uint8_t *id128);
+/* Join the pool as `rank` of `nranks` on CUDA device `device` (initPool). */
+int lp_pool_init(lp_pool_t *pool, const uint8_t *id128, int nranks, int rank, int device);
+/* Leave and free the pool; NULL is accepted (shutdown is idempotent). */
+int lp_pool_destroy(lp_pool_t pool);
+int lp_pool_size(lp_pool_t pool, int *nranks, int *rank);
+/* Gather every rank's row slice of y (m rows of per_row floats) in place. */
+int lp_pool_gather_rows(lp_pool_t pool, float *y, int64_t m, int64_t per_row, lp_stream_t stream);
+
+/* Pooled forms of the GEMVs / GEMMs above (parDequantGemv*, parDequantGemm*). */
+int lp_pool_dequant_gemv(lp_pool_t pool, const int8_t *wq, int64_t wq_len, const float *scales,
+                         int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                         float *y, int64_t y_len, lp_stream_t stream);
+int lp_pool_dequant_gemv_i4(lp_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                            const float *scales, int64_t scales_len, int64_t group_size,
+                            const float *x, int64_t x_len, float *y, int64_t y_len,
+                            lp_stream_t stream);
+int lp_pool_dequant_gemv_f4(lp_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                            const float *scales, int64_t scales_len, int64_t group_size,
+                            const float *x, int64_t x_len, float *y, int64_t y_len,
+                            lp_stream_t stream);
+int lp_pool_dequant_gemv_q8_0(lp_pool_t pool, const void *w, int64_t w_len,
+                              int64_t blocks_per_row, const float *x, int64_t x_len, float *y,
+                              int64_t y_len, lp_stream_t stream);
+int lp_pool_dequant_gemv_q4_0(lp_pool_t pool, const void *w, int64_t w_len,
+                              int64_t blocks_per_row, const float *x, int64_t x_len, float *y,
+                              int64_t y_len, lp_stream_t stream);
+int lp_pool_dequant_gemv_q8(lp_pool_t pool, const int8_t *wq, int64_t wq_len,
+                            const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                            const int8_t *xq, int64_t xq_len, const float *x_scales,
+                            int64_t x_scales_len, float *y, int64_t y_len, lp_stream_t stream);
+int lp_pool_dequant_gemv_i4q8(lp_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                              const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                              const int8_t *xq, int64_t xq_len, const float *x_scales,
+                              int64_t x_scales_len, float *y, int64_t y_len, lp_stream_t stream);
+int lp_pool_dequant_gemm_q8(lp_pool_t pool, const int8_t *wq, int64_t wq_len,
+                            const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                            const int8_t *xq, int64_t xq_len, const float *x_scales,
+                            int64_t x_scales_len, int64_t n, float *y, int64_t y_len,
+                            lp_stream_t stream);
+int lp_pool_dequant_gemm_i4q8(lp_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                              const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                              const int8_t *xq, int64_t xq_len, const float *x_scales,
+                              int64_t x_scales_len, int64_t n, float *y, int64_t y_len,
+                              lp_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

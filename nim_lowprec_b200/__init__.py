@@ -15,6 +15,7 @@ from .dequant import (  # noqa: F401
     quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split, fp32_mode,
     fp32Mode, setFp32Mode)
 from .ggml import QK, BlockQ4_0, BlockQ8_0  # noqa: F401
+from . import parallel  # noqa: F401  (LpPool's row-sharded forms)
 
 _native.lib()  # fail loudly at import if the CUDA library is missing
 

@@ -71,6 +71,21 @@ SIGNATURES = {
     "lph_quantize_batch": "pnpnnpn",
     "lp_set_fp32_mode": "i",
     "lp_get_fp32_mode": "",
+    "lp_pool_rows": "niipp",
+    "lp_pool_unique_id": "p",
+    "lp_pool_init": "ppiii",
+    "lp_pool_destroy": "p",
+    "lp_pool_size": "ppp",
+    "lp_pool_gather_rows": "ppnnp",
+    "lp_pool_dequant_gemv": "ppnpnnpnpnp",
+    "lp_pool_dequant_gemv_i4": "ppnpnnpnpnp",
+    "lp_pool_dequant_gemv_f4": "ppnpnnpnpnp",
+    "lp_pool_dequant_gemv_q8_0": "ppnnpnpnp",
+    "lp_pool_dequant_gemv_q4_0": "ppnnpnpnp",
+    "lp_pool_dequant_gemv_q8": "ppnpnnpnpnpnp",
+    "lp_pool_dequant_gemv_i4q8": "ppnpnnpnpnpnp",
+    "lp_pool_dequant_gemm_q8": "ppnpnnpnpnnpnp",
+    "lp_pool_dequant_gemm_i4q8": "ppnpnnpnpnnpnp",
 }
 
 

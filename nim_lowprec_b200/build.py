@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if force or _stale(OUT, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs]
+        cmd = [NVCC, *ARCH, "-shared", "-o", OUT, *objs, "-ldl"]
         subprocess.run(cmd, check=True)
     return OUT
 

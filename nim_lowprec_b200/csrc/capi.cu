@@ -45,6 +45,8 @@ void note_cuda_error(cudaError_t e) {
   snprintf(t_detail, sizeof(t_detail), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
+void note_text(const char* text) { snprintf(t_detail, sizeof(t_detail), "%s", text); }
+
 }  // namespace lp
 
 using lp::GemvParams;

@@ -98,14 +98,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
           saddr(bar))
       : "memory");
 }
-// 32 lanes x 8 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7])
-      : "r"(taddr));
-}
 // 32 lanes x 4 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
@@ -402,7 +394,6 @@ int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* 
   const uintptr_t al = reinterpret_cast<uintptr_t>(wq) | reinterpret_cast<uintptr_t>(xq) |
                        reinterpret_cast<uintptr_t>(ws);
   if (al & 15) return LP_ERR_UNSUPPORTED;
-  const int gpr = static_cast<int>(k / 32);
   if (n <= 64) {
     return launch_nt<16>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
                          static_cast<int>(k), st);

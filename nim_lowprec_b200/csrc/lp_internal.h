@@ -65,6 +65,7 @@ unsigned int take_error_gemm_tc();
 
 // Records the CUDA error text for lp_last_error_detail() and maps to a status.
 void note_cuda_error(cudaError_t e);
+void note_text(const char* text);
 const char* t_detail_ptr();
 inline int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return LP_OK;

@@ -1,0 +1,265 @@
+"""LpPool's row-sharded forms across the GPUs of one box (parallel.nim:82-474).
+
+One process per GPU, joined by ``torch.distributed``.  Rank r of P owns the
+rows ``[per*r, per*r + per)`` of every weight matrix, ``per = m div P``, and
+the last rank takes the remainder -- the slicing of ``parallel.nim:118-124``
+(``shardRows``, computed by the library's ``lp_pool_rows``).  Every output row
+depends only on its own weight row, so a sharded call gives the serial bits.
+
+* ``Pool(group)`` gathers the row slices of y with ``torch.distributed``
+  (NCCL for CUDA tensors; any backend works, gloo included).
+* ``NcclPool(group, device)`` is the C-ABI pool (``lp_pool_*``): the library
+  runs the local slice and gathers y itself with one NCCL group of per-rank
+  broadcasts -- the form a Nim program uses through the shim.
+
+The ``par*`` procs take the reference's arguments.  The weight arrays are
+either whole (the reference's call: each rank slices its rows) or, with
+``sharded=True``, already this rank's slice (weights resident per GPU).
+Activations and ``y`` are whole; every rank ends with all of ``y``.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _native as N
+from . import dequant as D
+
+try:
+    import torch
+except Exception:  # pragma: no cover
+    torch = None
+
+
+def shardRows(m: int, nranks: int, rank: int):
+    """(begin, end) of rank's row slice (parallel.nim:118-124)."""
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    N.check(N.lib().lp_pool_rows(int(m), int(nranks), int(rank), ctypes.byref(b), ctypes.byref(e)),
+            "lp_pool_rows")
+    return b.value, e.value
+
+
+def _numel(a) -> int:
+    return int(a.numel()) if (torch is not None and isinstance(a, torch.Tensor)) else int(np.asarray(a).size)
+
+
+def _flat(a):
+    return a.reshape(-1)
+
+
+class Pool:
+    """A member of a row-sharded pool over a ``torch.distributed`` group."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self._dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+
+    # -- the reference's slicing -------------------------------------------
+    def rows(self, m: int):
+        return shardRows(m, self.size, self.rank)
+
+    def slice(self, a, m: int):
+        """This rank's rows of a row-major array holding m rows."""
+        n = _numel(a)
+        if m == 0 or n % m:
+            raise AssertionError(f"array of {n} elements is not {m} rows")
+        per = n // m
+        b, e = self.rows(m)
+        return _flat(a)[b * per:e * per]
+
+    # -- gather ------------------------------------------------------------
+    def gather(self, y, m: int, per_row: int = 1):
+        """Every rank's row slice of y (m rows of per_row values) into y."""
+        P = self.size
+        if P == 1 or m == 0:
+            return y
+        yf = _flat(y)
+        spans = [shardRows(m, P, r) for r in range(P)]
+        mx = max(e - b for b, e in spans) * per_row
+        b, e = spans[self.rank]
+        send = torch.zeros(mx, dtype=yf.dtype, device=yf.device)
+        send[:(e - b) * per_row] = yf[b * per_row:e * per_row]
+        recv = [torch.empty_like(send) for _ in range(P)]
+        self._dist.all_gather(recv, send, group=self.group)
+        for r, (rb, re_) in enumerate(spans):
+            yf[rb * per_row:re_ * per_row] = recv[r][:(re_ - rb) * per_row]
+        return y
+
+    def run(self, local, y, m: int, per_row: int = 1):
+        """local(y_slice) computes this rank's rows in place; then gather."""
+        b, e = self.rows(m)
+        local(_flat(y)[b * per_row:e * per_row])
+        return self.gather(y, m, per_row)
+
+    def shutdown(self):  # parallel.nim:153-167; the group belongs to the caller
+        pass
+
+
+class NcclPool:
+    """The library's own pool (``lp_pool_*``): NCCL communicator inside."""
+
+    def __init__(self, group=None, device: int | None = None):
+        import torch.distributed as dist
+        rank, size = dist.get_rank(group), dist.get_world_size(group)
+        ident = bytearray(128)
+        if rank == 0:
+            buf = (ctypes.c_uint8 * 128)()
+            N.check(N.lib().lp_pool_unique_id(buf), "lp_pool_unique_id")
+            ident = bytearray(bytes(buf))
+        obj = [bytes(ident)]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        dev = torch.cuda.current_device() if device is None else int(device)
+        self._h = ctypes.c_void_p()
+        idbuf = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
+        N.check(N.lib().lp_pool_init(ctypes.byref(self._h), idbuf, size, rank, dev), "lp_pool_init")
+        self.rank, self.size, self.device = rank, size, dev
+
+    def rows(self, m: int):
+        return shardRows(m, self.size, self.rank)
+
+    def slice(self, a, m: int):
+        n = _numel(a)
+        if m == 0 or n % m:
+            raise AssertionError(f"array of {n} elements is not {m} rows")
+        per = n // m
+        b, e = self.rows(m)
+        return _flat(a)[b * per:e * per]
+
+    def call(self, name: str, *args):
+        N.check(getattr(N.lib(), name)(self._h, *args), name)
+
+    def shutdown(self):
+        if self._h:
+            N.check(N.lib().lp_pool_destroy(self._h), "lp_pool_destroy")
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.shutdown()
+        except Exception:
+            pass
+
+
+def initPool(group=None, nccl: bool = False, device: int | None = None):
+    """initPool (parallel.nim:134-151): this process's member of the pool."""
+    return NcclPool(group, device) if nccl else Pool(group)
+
+
+# ------------------------------------------------------------ par* procs --
+
+def _w(pool, a, m, sharded):
+    return a if sharded else pool.slice(a, m)
+
+
+def _dev(a):
+    return a.data_ptr()
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _nccl_gemv(pool, name, wq, ws, gs, x, y, sharded):
+    m = _numel(y)
+    wq, ws = _w(pool, wq, m, sharded), _w(pool, ws, m, sharded)
+    pool.call(name, _dev(wq), _numel(wq), _dev(ws), _numel(ws), int(gs), _dev(x), _numel(x),
+              _dev(y), m, _stream())
+
+
+def parDequantGemv(pool, wq, scales, groupSize, x, y, sharded=False):
+    """parallel.nim:186-253 (defParGemv, int8 weights, fp32 activations)."""
+    m = _numel(y)
+    if isinstance(pool, NcclPool):
+        return _nccl_gemv(pool, "lp_pool_dequant_gemv", wq, scales, groupSize, x, y, sharded)
+    w, s = _w(pool, wq, m, sharded), _w(pool, scales, m, sharded)
+    pool.run(lambda ys: D.dequantGemv(w, s, groupSize, x, ys), y, m)
+
+
+def parDequantGemvI4(pool, wpacked, scales, groupSize, x, y, sharded=False):
+    """parallel.nim:186-255 (defParGemv over dequantGemvI4)."""
+    m = _numel(y)
+    if isinstance(pool, NcclPool):
+        return _nccl_gemv(pool, "lp_pool_dequant_gemv_i4", wpacked, scales, groupSize, x, y, sharded)
+    w, s = _w(pool, wpacked, m, sharded), _w(pool, scales, m, sharded)
+    pool.run(lambda ys: D.dequantGemvI4(w, s, groupSize, x, ys), y, m)
+
+
+def parDequantGemvF4(pool, wpacked, scales, groupSize, x, y, sharded=False):
+    """parallel.nim:186-257 (defParGemv over dequantGemvF4)."""
+    m = _numel(y)
+    if isinstance(pool, NcclPool):
+        return _nccl_gemv(pool, "lp_pool_dequant_gemv_f4", wpacked, scales, groupSize, x, y, sharded)
+    w, s = _w(pool, wpacked, m, sharded), _w(pool, scales, m, sharded)
+    pool.run(lambda ys: D.dequantGemvF4(w, s, groupSize, x, ys), y, m)
+
+
+def _blocks_rows(pool, w, m, sharded):
+    return w if sharded else pool.slice(w, m)
+
+
+def parDequantGemvQ8_0(pool, w, blocksPerRow, x, y, sharded=False):
+    """parallel.nim:260-307 (defParBlockGemv, ggml Q8_0 weights, fp32 activations)."""
+    m = _numel(y)
+    ws = _blocks_rows(pool, w, m, sharded)
+    if isinstance(pool, NcclPool):
+        return pool.call("lp_pool_dequant_gemv_q8_0", _dev(ws), D._blocks(ws, 34),
+                         int(blocksPerRow), _dev(x), _numel(x), _dev(y), m, _stream())
+    pool.run(lambda ys: D.dequantGemvQ8_0(ws, blocksPerRow, x, ys), y, m)
+
+
+def parDequantGemvQ4_0(pool, w, blocksPerRow, x, y, sharded=False):
+    """parallel.nim:260-308 (defParBlockGemv over dequantGemvQ4_0)."""
+    m = _numel(y)
+    ws = _blocks_rows(pool, w, m, sharded)
+    if isinstance(pool, NcclPool):
+        return pool.call("lp_pool_dequant_gemv_q4_0", _dev(ws), D._blocks(ws, 18),
+                         int(blocksPerRow), _dev(x), _numel(x), _dev(y), m, _stream())
+    pool.run(lambda ys: D.dequantGemvQ4_0(ws, blocksPerRow, x, ys), y, m)
+
+
+def _q8(pool, name, fn, w, wScales, groupSize, xq, xScales, y, sharded):
+    m = _numel(y)
+    wl, sl = _w(pool, w, m, sharded), _w(pool, wScales, m, sharded)
+    if isinstance(pool, NcclPool):
+        return pool.call(name, _dev(wl), _numel(wl), _dev(sl), _numel(sl), int(groupSize), _dev(xq),
+                         _numel(xq), _dev(xScales), _numel(xScales), _dev(y), m, _stream())
+    pool.run(lambda ys: fn(wl, sl, groupSize, xq, xScales, ys), y, m)
+
+
+def parDequantGemvQ8(pool, wq, wScales, groupSize, xq, xScales, y, sharded=False):
+    """parallel.nim:310-415 (defParQ8Gemv: pooled and per-call int8 x int8)."""
+    _q8(pool, "lp_pool_dequant_gemv_q8", D.dequantGemvQ8, wq, wScales, groupSize, xq, xScales, y,
+        sharded)
+
+
+def parDequantGemvI4Q8(pool, wpacked, wScales, groupSize, xq, xScales, y, sharded=False):
+    """parallel.nim:310-418 (defParQ8Gemv over dequantGemvI4Q8)."""
+    _q8(pool, "lp_pool_dequant_gemv_i4q8", D.dequantGemvI4Q8, wpacked, wScales, groupSize, xq,
+        xScales, y, sharded)
+
+
+def _gemm(pool, name, fn, w, wScales, groupSize, xq, xScales, n, y, sharded):
+    m = _numel(y) // n
+    wl, sl = _w(pool, w, m, sharded), _w(pool, wScales, m, sharded)
+    if isinstance(pool, NcclPool):
+        return pool.call(name, _dev(wl), _numel(wl), _dev(sl), _numel(sl), int(groupSize), _dev(xq),
+                         _numel(xq), _dev(xScales), _numel(xScales), int(n), _dev(y), _numel(y),
+                         _stream())
+    pool.run(lambda ys: fn(wl, sl, groupSize, xq, xScales, n, ys), y, m, per_row=n)
+
+
+def parDequantGemmQ8(pool, wq, wScales, groupSize, xq, xScales, n, y, sharded=False):
+    """parallel.nim:420-473 (defParGemm; y rows are row-major, n columns)."""
+    _gemm(pool, "lp_pool_dequant_gemm_q8", D.dequantGemmQ8, wq, wScales, groupSize, xq, xScales, n,
+          y, sharded)
+
+
+def parDequantGemmI4Q8(pool, wpacked, wScales, groupSize, xq, xScales, n, y, sharded=False):
+    """parallel.nim:420-474 (defParGemm over dequantGemmI4Q8)."""
+    _gemm(pool, "lp_pool_dequant_gemm_i4q8", D.dequantGemmI4Q8, wpacked, wScales, groupSize, xq,
+          xScales, n, y, sharded)

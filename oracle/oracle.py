@@ -84,6 +84,8 @@ def lib():
         L.lpo_pool_thread_count.argtypes = [vp]
         L.lpo_shard_count.restype = ctypes.c_int
         L.lpo_shard_count.argtypes = [i64, ctypes.c_int]
+        L.lpo_shard.restype = None
+        L.lpo_shard.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
         L.lpo_run.argtypes = [vp, ctypes.c_int, vp, vp, i64, vp, vp, i64, i64, vp, i64]
         _lib = L
     return _lib
@@ -310,6 +312,13 @@ def dequantGemmI4Q8(wpacked, wScales, groupSize, xq, xScales, n, pool=None):
     wp = _c(wpacked, np.uint8); ws = _c(wScales, np.float32); xq = _c(xq, np.int8); xs = _c(xScales, np.float32)
     k = xq.size // n
     return _run("gemm_i4q8", wp, ws, groupSize, xq, xs, k, n, wp.size // (k // 2), pool)
+
+
+def shard(rows: int, workers: int, worker: int):
+    """(first row, row count) of a worker's slice (parallel.nim:118-124)."""
+    r0, cnt = ctypes.c_int64(), ctypes.c_int64()
+    lib().lpo_shard(int(rows), int(workers), int(worker), ctypes.addressof(r0), ctypes.addressof(cnt))
+    return r0.value, cnt.value
 
 
 def shardCount(rows: int, threads: int) -> int:

@@ -1,0 +1,116 @@
+"""LpPool's row-sharded forms on several GPUs (one process per GPU, NCCL).
+
+Skipped unless at least two GPUs are visible.  Every rank computes the whole
+result on its own GPU with the ordinary entry points, then the pooled forms --
+``Pool`` (torch.distributed gather) and ``NcclPool`` (the C-ABI pool, NCCL
+inside the library) -- and the two must agree bit for bit: sharded == serial
+(test_parallel.nim), with an uneven row count so the last rank takes the
+remainder.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:  # pragma: no cover
+    pytest.skip("needs two or more GPUs", allow_module_level=True)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    bad = []
+    try:
+        import nim_lowprec_b200 as L
+        from nim_lowprec_b200 import parallel as P
+        g = torch.Generator(device="cuda").manual_seed(11)
+        M, K, n = 1001, 512, 8
+
+        def rnd(k, scale=1.0):
+            return torch.randn(k, device="cuda", generator=g) * scale
+
+        w = rnd(M * K, 0.02)
+        x = rnd(K * n)
+        wq = torch.empty(M * K, dtype=torch.int8, device="cuda")
+        wd = torch.empty(M * K // 32, device="cuda")
+        L.quantizeQ8_0Split(w, wq, wd)
+        xq = torch.empty(K * n, dtype=torch.int8, device="cuda")
+        xd = torch.empty(K * n // 32, device="cuda")
+        L.quantizeQ8_0Split(x, xq, xd)
+        blk = torch.empty(M * K // 32 * 18, dtype=torch.uint8, device="cuda")
+        L.quantizeQ4_0Batch(w, blk)
+        pools = [P.Pool(), P.NcclPool()]
+
+        def same(tag, a, b):
+            torch.cuda.synchronize()
+            if not torch.equal(a.view(torch.int32), b.view(torch.int32)):
+                bad.append(tag)
+
+        ref = torch.empty(M, device="cuda")
+        L.dequantGemvQ8(wq, wd, 32, xq[:K], xd[:K // 32], ref)
+        for i, pool in enumerate(pools):
+            y = torch.full((M,), float("nan"), device="cuda")
+            P.parDequantGemvQ8(pool, wq, wd, 32, xq[:K], xd[:K // 32], y)
+            same(f"q8/{i}", y, ref)
+            # weights already sharded: only this rank's rows are passed
+            y2 = torch.full((M,), float("nan"), device="cuda")
+            P.parDequantGemvQ8(pool, pool.slice(wq, M).clone(), pool.slice(wd, M).clone(), 32,
+                               xq[:K], xd[:K // 32], y2, sharded=True)
+            same(f"q8-sharded/{i}", y2, ref)
+        for mode in ("fast", "exact"):
+            with L.fp32_mode(mode):
+                ref = torch.empty(M, device="cuda")
+                L.dequantGemvQ4_0(blk, K // 32, x[:K], ref)
+                for i, pool in enumerate(pools):
+                    y = torch.full((M,), float("nan"), device="cuda")
+                    P.parDequantGemvQ4_0(pool, blk, K // 32, x[:K], y)
+                    same(f"q4_0-{mode}/{i}", y, ref)
+        ref = torch.empty(M * n, device="cuda")
+        L.dequantGemmQ8(wq, wd, 32, xq, xd, n, ref)
+        for i, pool in enumerate(pools):
+            y = torch.full((M * n,), float("nan"), device="cuda")
+            P.parDequantGemmQ8(pool, wq, wd, 32, xq, xd, n, y)
+            same(f"gemm/{i}", y, ref)
+        pools[1].shutdown()
+        from nim_lowprec_b200 import _native as N
+        if N.device_error() != 0:
+            bad.append("device_error")
+    except Exception as e:  # report, do not hang the other rank
+        bad.append(f"exception: {e!r}")
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    q.put((rank, bad))
+
+
+def test_pooled_forms_equal_single_gpu_bits():
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    assert all(not results[r] for r in range(world)), results
