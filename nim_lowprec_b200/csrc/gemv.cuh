@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     int t = 0;
     for (; t < ntiles; ++t) {
       const int s = t % p.stages;
-      if (t >= p.stages && !mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, &s_abort)) break;
+      if (t >= p.stages && !mbar_wait_idle(&empty[s], ((t / p.stages) - 1) & 1, &s_abort)) break;
       if (s_abort) break;
       const int r0 = row_begin + t * p.rt;
       const int rows = min(p.rt, row_end - r0);
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     if constexpr (Fmt::kFold == Fold::Tree) {
       for (int t = 0; t < ntiles; ++t) {
         const int slot = t % p.ring;
-        if (!mbar_wait(&tfull[slot], (t / p.ring) & 1, &s_abort)) break;
+        if (!mbar_wait_idle(&tfull[slot], (t / p.ring) & 1, &s_abort)) break;
         if (s_abort) break;
         const int r0 = row_begin + t * p.rt;
         const int rows = min(p.rt, row_end - r0);
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         const int nt = min(p.fb, ntiles - t0);
         bool ok = true;
         for (int i = 0; i < nt && ok; ++i)
-          ok = mbar_wait(&tfull[(t0 + i) % p.ring], ((t0 + i) / p.ring) & 1, &s_abort);
+          ok = mbar_wait_idle(&tfull[(t0 + i) % p.ring], ((t0 + i) / p.ring) & 1, &s_abort);
         if (!ok || s_abort) break;
         if (ti < nt) {
           const int t = t0 + ti;

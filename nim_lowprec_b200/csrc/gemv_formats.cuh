@@ -38,11 +38,13 @@ __device__ __forceinline__ uint64_t magic_pair(uint32_t wa, uint32_t wb, int b) 
 // window of `NW` words starting at or before p; returns the byte offset (0/2).
 template <int NW>
 __device__ __forceinline__ int load_window(const uint8_t* p, uint32_t (&w)[NW]) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* base = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  // (pointer arithmetic, not an integer round trip, so the compiler keeps
+  // the shared-memory address space and emits shared loads)
+  const int off = static_cast<int>(reinterpret_cast<uintptr_t>(p) & 3);
+  const uint32_t* base = reinterpret_cast<const uint32_t*>(p - off);
 #pragma unroll
   for (int i = 0; i < NW; ++i) w[i] = base[i];
-  return static_cast<int>(a & 3);
+  return off;
 }
 
 // ggml Q4_0 block (d:2, qs:16) at a 2-byte-aligned shared address.

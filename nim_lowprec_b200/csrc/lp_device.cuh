@@ -88,6 +88,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// Bounded wait for warps whose wait is not on the critical path (a producer
+// waiting for a free stage, a folder waiting for a finished tile): between
+// polls the thread sleeps 32..256 ns, so a waiting warp leaves the issue
+// slots of its sub-partition to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort = nullptr) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  uint32_t ns = 32;
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      raise_error(LP_ERR_TIMEOUT);
+      if (abort) *abort = 1;
+      return false;
+    }
+    if (ns < 256) ns <<= 1;
+  }
+}
+
 // ----------------------------------------------------- bulk (TMA) copies
 // 1-D bulk copy global -> this CTA's shared memory, completion counted on
 // `bar` in bytes.  dst, src and bytes must be multiples of 16.
