@@ -88,6 +88,8 @@ GemvParams base(const void* w, const float* ws, const void* x, const float* xs, 
 }
 
 constexpr int64_t kIntMax = 0x7fffffff;
+// Widest GEMM (activation columns) run by the GEMV skeleton's column formats.
+constexpr int64_t kGemmColsMax = 16;
 
 std::atomic<int> g_fp32_mode{LP_FP32_FAST};
 
@@ -278,6 +280,16 @@ static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, in
   if (bad(w, w_len) || bad(ws, ws_len) || bad(xq, xq_len) || bad(xs, xs_len) || bad(y, y_len))
     return LP_ERR_ARG;
   LP_VALIDATED();
+  // A few columns: the GEMV skeleton with one term per (row, group, column),
+  // one CTA per SM streaming its rows once (a 128-row tensor-core tile would
+  // leave most SMs idle at this width).
+  if (gs == 32 && n <= kGemmColsMax && m >= 1) {
+    GemvParams p = base(w, ws, xq, xs, y, m, k, gs, gpr, rb);
+    p.ncol = static_cast<int>(n);
+    const int r = i4 ? lp::launch_gemv<lp::FmtI4Q8Cols>(p, S(st))
+                     : lp::launch_gemv<lp::FmtQ8Cols>(p, S(st));
+    if (r != LP_ERR_UNSUPPORTED) return r;
+  }
   if (!i4) {
     const int r = lp::launch_gemm_tc(static_cast<const int8_t*>(w), ws, gs, xq, xs, n, y, m, k, S(st));
     if (r != LP_ERR_UNSUPPORTED) return r;

@@ -28,8 +28,8 @@
 #include <algorithm>
 #include <mutex>
 
-#include "lp_device.cuh"
 #include "lp_internal.h"
+#include "tc_ptx.cuh"
 
 namespace lp {
 namespace {
@@ -56,70 +56,7 @@ struct TcArgs {
   float neg_zero;   // -0.0f at run time (see mul2_rn)
 };
 
-// ------------------------------------------------------ PTX wrappers ---
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3}], [%4];" ::"r"(saddr(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(saddr(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(dst)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// D[tmem] = A * B (int8 x int8 -> int32), overwriting D.
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0u)
-      : "memory");
-}
-// The mbarrier completes one arrival once every tcgen05 op this thread issued
-// so far has finished.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          saddr(bar))
-      : "memory");
-}
-// 32 lanes x 4 consecutive 32-bit columns.
-__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major tile written by TMA with
-// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart (SBO),
-// descriptor version 1, layout SWIZZLE_128B.  Stepping K inside the 128-byte
-// swizzle row moves the start address only.
-__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
-  uint64_t d = static_cast<uint64_t>((saddr(p) & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(1) << 16;           // leading byte offset (unused here)
-  d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset
-  d |= static_cast<uint64_t>(1) << 46;           // version
-  d |= static_cast<uint64_t>(2) << 61;           // SWIZZLE_128B
-  return d;
-}
+using namespace tc;
 
 // Instruction descriptor: D s32, A s8, B s8, both K-major, N = NT, M = 128.
 template <int NT>
@@ -319,39 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (the
-// library links no driver library directly).
-EncodeFn encoder() {
-  static EncodeFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(p);
-  });
-  return fn;
-}
-
 // A K-major int8 matrix of `rows` rows x k bytes, boxes of box_rows x 128 B,
 // 128-byte swizzle.
 bool encode_rows(CUtensorMap* tm, const void* base, int64_t k, int64_t rows, int box_rows) {
-  EncodeFn fn = encoder();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKStage), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_u8(tm, base, k, rows, kKStage, box_rows, true);
 }
 
 template <int NT>

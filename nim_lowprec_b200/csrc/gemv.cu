@@ -45,6 +45,12 @@ template <> int x_stage_bytes<FmtQ8>(const GemvParams& p) { return q8_bytes(p); 
 template <> int x_stage_bytes<FmtI4Q8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ8_0Q8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtQ8Cols>(const GemvParams& p) {
+  return round_up(p.k * p.ncol, 16) + 4 * p.gpr * p.ncol;
+}
+template <> int x_stage_bytes<FmtI4Q8Cols>(const GemvParams& p) {
+  return round_up(p.k * p.ncol, 16) + 8 * p.gpr * p.ncol;  // xs, then 8 * sum(x)
+}
 
 struct SmemLimits {
   int one = 0;  // dynamic shared bytes one CTA may use
@@ -74,13 +80,26 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     lim[slot].one = one;
   });
   constexpr int NC = kNcw * 32;
-  // Tile height: about two (row pair, group) units per consumer thread, in
-  // whole row pairs, at most 32 rows and 40 KB of weights + scales.
+  constexpr bool kCols = ColsOf<Fmt>::value;
+  const int vr = kCols ? p.ncol : 1;  // virtual rows per weight row
   const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
-  int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
-  rt = std::min(rt, std::max(2, (40 * 1024) / std::max(row_total, 1)));
-  rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
-  p.rt = std::max(1, rt & ~1);
+  if constexpr (kCols) {
+    // Tile height: enough (row pair, group) units for every consumer
+    // thread (one pair per thread at gpr = 128), at most 40 KB of weights +
+    // scales and 64 virtual rows (rt * ncol, folded 32 at a time).
+    if (p.ncol < 1 || p.ncol > 64) return LP_ERR_UNSUPPORTED;
+    int rt = std::max(2, std::min(64 / p.ncol, (2 * NC) / std::max(p.gpr, 1)));
+    rt = std::min(rt, std::max(1, (40 * 1024) / std::max(row_total, 1)));
+    rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
+    p.rt = rt > 1 ? rt & ~1 : 1;  // whole row pairs
+  } else {
+    // Tile height: about two (row pair, group) units per consumer thread, in
+    // whole row pairs, at most 32 rows and 40 KB of weights + scales.
+    int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
+    rt = std::min(rt, std::max(2, (40 * 1024) / std::max(row_total, 1)));
+    rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
+    p.rt = std::max(1, rt & ~1);
+  }
   p.tstride = round_up(p.gpr, 32) + 4;
   // Ordered folds take fb tiles (<= 32 rows) per pass over a ring of two
   // passes; the unordered fold goes tile by tile over four slots.
@@ -96,14 +115,19 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
       p.tcols = p.gpr / 32;
     }
   } else {
-    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / p.rt));
-    while (p.fb > 1 && 2 * p.fb * p.rt * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
+    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / (p.rt * vr)));
+    while (p.fb > 1 && 2 * p.fb * p.rt * vr * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
     p.ring = 2 * p.fb;
+    if (kCols) {
+      // one tile per fold pass; up to four slots (the consumers run ahead)
+      p.fb = 1;
+      p.ring = p.rt * vr * p.tstride * 4 * 4 <= 72 * 1024 ? 4 : 2;
+    }
   }
   p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
   p.stage_w_bytes = round_up(p.rt * p.row_bytes, 128);
   p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 128) : 0;
-  const int terms_bytes = round_up(p.ring * p.rt * p.tstride * 4, 128);
+  const int terms_bytes = round_up(p.ring * p.rt * vr * p.tstride * 4, 128);
   const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
   const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
   p.stages = std::min(kMaxStages, (lim[slot].one - fixed) / per_stage);
@@ -152,5 +176,7 @@ template int launch_gemv<FmtQ8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtI4Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8_0Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ4_0Q8>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ8Cols>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtI4Q8Cols>(GemvParams, cudaStream_t);
 
 }  // namespace lp

@@ -33,6 +33,8 @@
 //            time so up to 32 independent chains run together; the
 //            unordered fold of the block-float path sums a row across lanes.
 #pragma once
+#include <type_traits>
+
 #include "lp_device.cuh"
 
 namespace lp {
@@ -61,7 +63,18 @@ struct GemvParams {
   int off_w, off_s, off_t, off_b;  // shared-memory offsets (128-byte aligned)
   int stage_w_bytes, stage_s_bytes;
   float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
+  int ncol;           // activation columns (the small-n GEMM formats); else unused
 };
+
+// Formats with a column dimension (kCols) compute, per (row, group), one term
+// for each of p.ncol activation columns.  The skeleton treats (row r, column
+// c) of a tile as virtual row r * ncol + c: that is y's own row-major index
+// (y is M x ncol), so tiles, folds and stores stay those of a GEMV with
+// rt * ncol rows.
+template <class F, class = void>
+struct ColsOf : std::false_type {};
+template <class F>
+struct ColsOf<F, std::void_t<decltype(F::kCols)>> : std::bool_constant<F::kCols> {};
 
 // ------------------------------------------------------------ x staging
 // Cooperative copy of `bytes` bytes global -> shared (activations are tiny
@@ -288,9 +301,28 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
       }
+    } else if constexpr (ColsOf<Fmt>::value) {
+      // one tile per pass; its rows * ncol virtual rows 32 at a time
+      for (int t = 0; t < ntiles; ++t) {
+        const int slot = t % p.ring;
+        if (!mbar_wait_idle(&tfull[slot], (t / p.ring) & 1, &s_abort)) break;
+        if (s_abort) break;
+        const int r0 = row_begin + t * p.rt;
+        const int nv = min(p.rt, row_end - r0) * p.ncol;
+        const float* T = terms + slot * p.rt * p.ncol * p.tstride;
+        for (int v = lane; v < nv; v += 32)
+          p.y[static_cast<int64_t>(r0) * p.ncol + v] =
+              fold_row<Fmt::kFold>(T + v * p.tstride, p.gpr);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[slot]);
+      }
     } else {
-      // Lane l folds row l % rt of tile t0 + l / rt of each batch.
-      const int ti = lane / p.rt, r = lane - ti * p.rt;
+      // Lane l folds (virtual) row l % (rt * vr) of tile t0 + l / (rt * vr)
+      // of each batch.
+      constexpr bool kCols = ColsOf<Fmt>::value;
+      const int vr = kCols ? p.ncol : 1;
+      const int vt = p.rt * vr;
+      const int ti = lane / vt, r = lane - ti * vt;
       for (int t0 = 0; t0 < ntiles; t0 += p.fb) {
         const int nt = min(p.fb, ntiles - t0);
         bool ok = true;
@@ -300,9 +332,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         if (ti < nt) {
           const int t = t0 + ti;
           const int r0 = row_begin + t * p.rt;
-          if (r < min(p.rt, row_end - r0))
-            p.y[r0 + r] =
-                fold_row<Fmt::kFold>(terms + ((t % p.ring) * p.rt + r) * p.tstride, p.gpr);
+          if (r < min(p.rt, row_end - r0) * vr)
+            p.y[static_cast<int64_t>(r0) * vr + r] =
+                fold_row<Fmt::kFold>(terms + ((t % p.ring) * vt + r) * p.tstride, p.gpr);
         }
         __syncwarp();
         if (lane == 0)
@@ -325,7 +357,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     // two independent straight-line term2 calls the compiler interleaves.
     const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
     const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
-    if (dg == 0) f.prepare(p, xsm, g0);
+    if constexpr (!ColsOf<Fmt>::value)
+      if (dg == 0) f.prepare(p, xsm, g0);
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % p.stages;
       const int tb = t % p.ring;
@@ -338,7 +371,18 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
       const float* S = reinterpret_cast<const float*>(sts + s * p.stage_s_bytes);
       float* T = terms + tb * p.rt * p.tstride;
       const int npairs = (rows + 1) >> 1;
-      if (dg == 0) {
+      if constexpr (ColsOf<Fmt>::value) {
+        // one (row pair, group) unit at a time, all columns of it: each
+        // column's activations are read once for both rows
+        T = terms + tb * p.rt * p.ncol * p.tstride;
+        for (int q = ct; q < npairs * p.gpr; q += NC) {
+          const int pr = q / p.gpr, g = q - pr * p.gpr;
+          const int ra = 2 * pr, rb = min(ra + 1, rows - 1);
+          f.termcols2(p, xsm, W + ra * p.row_bytes, W + rb * p.row_bytes, S + ra * p.gpr,
+                      S + rb * p.gpr, g, T + ra * p.ncol * p.tstride,
+                      ra + 1 < rows ? T + (ra + 1) * p.ncol * p.tstride : nullptr, p.tstride);
+        }
+      } else if (dg == 0) {
         const int g = g0;
         int pr = pr0;
         for (; Fmt::kTwoPairs && pr + dpr < npairs; pr += 2 * dpr) {

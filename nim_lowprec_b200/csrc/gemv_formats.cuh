@@ -983,6 +983,140 @@ struct FmtI4Q8 : StageXQ8 {
   }
 };
 
+// ----------------------------------------------- small-n GEMM (columns)
+// dequantGemmQ8 / dequantGemmI4Q8 for a few activation columns
+// (simd/dequant.nim:1382-1583; scalar :1449-1458):
+//   y[row * n + c] = fold_g fl(fl(f32(isum) * ws[row, g]) * xs[c * gpr + g]),
+// serial over g from 0.0 -- the GEMV term of each column.  Staged once per
+// CTA: the n columns of xq (K x n, column-major: column c is K bytes) and
+// xs (n x gpr).  Group size 32 only; the weight group is loaded once and
+// dotted with every column.
+struct StageXCols {
+  static __device__ __forceinline__ int xs_off(const GemvParams& p) {
+    return (p.k * p.ncol + 15) & ~15;
+  }
+  static __device__ __forceinline__ const float* xscales(const GemvParams& p,
+                                                         const uint8_t* xsm) {
+    return reinterpret_cast<const float*>(xsm + xs_off(p));
+  }
+};
+
+struct FmtQ8Cols : StageXCols {
+  static constexpr bool kScales = true;
+  static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;
+  static constexpr bool kCols = true;
+  static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
+    copy_bytes(xsm, static_cast<const uint8_t*>(p.x), p.k * p.ncol, tid, nthr);
+    copy_bytes(xsm + xs_off(p), reinterpret_cast<const uint8_t*>(p.xs), p.gpr * p.ncol * 4, tid,
+               nthr);
+  }
+  // Rows A and B (TB == nullptr: row B is a duplicate of A and not stored).
+  __device__ __forceinline__ void termcols2(const GemvParams& p, const uint8_t* xsm,
+                                            const uint8_t* wA, const uint8_t* wB, const float* sA,
+                                            const float* sB, int g, float* TA, float* TB,
+                                            int tstride) {
+    const uint4* pa = reinterpret_cast<const uint4*>(wA + g * 32);
+    const uint4* pb = reinterpret_cast<const uint4*>(wB + g * 32);
+    const uint4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
+    const float ga = sA[g], gb = sB[g];
+    const float* xs = xscales(p, xsm);
+#pragma unroll 2
+    for (int c = 0; c < p.ncol; ++c) {
+      const uint4* px = reinterpret_cast<const uint4*>(xsm + c * p.k + g * 32);
+      const uint4 x0 = px[0], x1 = px[1];
+      int ia = 0, ib = 0;
+      ia = dp4a_ss(a0.x, x0.x, ia); ib = dp4a_ss(b0.x, x0.x, ib);
+      ia = dp4a_ss(a0.y, x0.y, ia); ib = dp4a_ss(b0.y, x0.y, ib);
+      ia = dp4a_ss(a0.z, x0.z, ia); ib = dp4a_ss(b0.z, x0.z, ib);
+      ia = dp4a_ss(a0.w, x0.w, ia); ib = dp4a_ss(b0.w, x0.w, ib);
+      ia = dp4a_ss(a1.x, x1.x, ia); ib = dp4a_ss(b1.x, x1.x, ib);
+      ia = dp4a_ss(a1.y, x1.y, ia); ib = dp4a_ss(b1.y, x1.y, ib);
+      ia = dp4a_ss(a1.z, x1.z, ia); ib = dp4a_ss(b1.z, x1.z, ib);
+      ia = dp4a_ss(a1.w, x1.w, ia); ib = dp4a_ss(b1.w, x1.w, ib);
+      const float xsc = xs[c * p.gpr + g];
+      TA[c * tstride + g] = fmul(fmul(i2f_rn(ia), ga), xsc);
+      if (TB) TB[c * tstride + g] = fmul(fmul(i2f_rn(ib), gb), xsc);
+    }
+  }
+};
+
+// The int4 weights as in FmtI4Q8 (t = nibble ^ 8, weight t - 8; low nibble =
+// even column): the staging splits each column's group into its even and odd
+// bytes (16 + 16) and keeps 8 * sum(x) per (column, group), after xs.
+struct FmtI4Q8Cols : StageXCols {
+  static constexpr bool kScales = true;
+  static constexpr Fold kFold = Fold::Serial;
+  static constexpr bool kFix = false;
+  static constexpr bool kTwoPairs = false;
+  static constexpr bool kCols = true;
+  static __device__ __forceinline__ const int* sums8(const GemvParams& p, const uint8_t* xsm) {
+    return reinterpret_cast<const int*>(xsm + xs_off(p) + p.gpr * p.ncol * 4);
+  }
+  static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
+    copy_bytes(xsm + xs_off(p), reinterpret_cast<const uint8_t*>(p.xs), p.gpr * p.ncol * 4, tid,
+               nthr);
+    int* s8 = const_cast<int*>(sums8(p, xsm));
+    const uint8_t* xq = static_cast<const uint8_t*>(p.x);
+    for (int u = tid; u < p.gpr * p.ncol; u += nthr) {  // u = c * gpr + g
+      const uint4* src = reinterpret_cast<const uint4*>(xq + u * 32);
+      const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+      const uint32_t X[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint32_t E[4], O[4];
+      int sx = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        E[j] = prmt(X[2 * j], X[2 * j + 1], 0x6420u);
+        O[j] = prmt(X[2 * j], X[2 * j + 1], 0x7531u);
+        sx = dp4a_us(0x01010101u, X[2 * j], sx);
+        sx = dp4a_us(0x01010101u, X[2 * j + 1], sx);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(xsm + u * 32);
+      dst[0] = make_uint4(E[0], E[1], E[2], E[3]);
+      dst[1] = make_uint4(O[0], O[1], O[2], O[3]);
+      s8[u] = 8 * sx;
+    }
+  }
+  __device__ __forceinline__ void termcols2(const GemvParams& p, const uint8_t* xsm,
+                                            const uint8_t* wA, const uint8_t* wB, const float* sA,
+                                            const float* sB, int g, float* TA, float* TB,
+                                            int tstride) {
+    const uint4 a = *reinterpret_cast<const uint4*>(wA + g * 16);
+    const uint4 b = *reinterpret_cast<const uint4*>(wB + g * 16);
+    const uint32_t A[4] = {a.x, a.y, a.z, a.w}, B[4] = {b.x, b.y, b.z, b.w};
+    uint32_t alo[4], ahi[4], blo[4], bhi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      alo[j] = (A[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
+      ahi[j] = ((A[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+      blo[j] = (B[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
+      bhi[j] = ((B[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+    }
+    const float ga = sA[g], gb = sB[g];
+    const float* xs = xscales(p, xsm);
+    const int* s8 = sums8(p, xsm);
+#pragma unroll 2
+    for (int c = 0; c < p.ncol; ++c) {
+      const int u = c * p.gpr + g;
+      const uint4* px = reinterpret_cast<const uint4*>(xsm + u * 32);
+      const uint4 e = px[0], o = px[1];
+      int ia = -s8[u], ib = ia;
+      ia = dp4a_us(alo[0], e.x, ia); ib = dp4a_us(blo[0], e.x, ib);
+      ia = dp4a_us(ahi[0], o.x, ia); ib = dp4a_us(bhi[0], o.x, ib);
+      ia = dp4a_us(alo[1], e.y, ia); ib = dp4a_us(blo[1], e.y, ib);
+      ia = dp4a_us(ahi[1], o.y, ia); ib = dp4a_us(bhi[1], o.y, ib);
+      ia = dp4a_us(alo[2], e.z, ia); ib = dp4a_us(blo[2], e.z, ib);
+      ia = dp4a_us(ahi[2], o.z, ia); ib = dp4a_us(bhi[2], o.z, ib);
+      ia = dp4a_us(alo[3], e.w, ia); ib = dp4a_us(blo[3], e.w, ib);
+      ia = dp4a_us(ahi[3], o.w, ia); ib = dp4a_us(bhi[3], o.w, ib);
+      const float xsc = xs[u];
+      TA[c * tstride + g] = fmul(fmul(i2f_rn(ia), ga), xsc);
+      if (TB) TB[c * tstride + g] = fmul(fmul(i2f_rn(ib), gb), xsc);
+    }
+  }
+};
+
 // ggml Q8_0 activation blocks staged as qs (k bytes) + decoded d (bpr floats),
 // the once-per-call decode of simd/dequant.nim:1171-1175.
 struct StageXBlocks {

@@ -36,6 +36,8 @@ struct FmtQ8;
 struct FmtI4Q8;
 struct FmtQ8_0Q8;
 struct FmtQ4_0Q8;
+struct FmtQ8Cols;
+struct FmtI4Q8Cols;
 
 template <class Fmt>
 int launch_gemv(GemvParams p, cudaStream_t st);

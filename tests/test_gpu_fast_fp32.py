@@ -218,3 +218,38 @@ def test_mode_switch_and_host_forms():
     y = np.zeros(M, F)
     L.dequantGemvQ4_0(blk, K // 32, x, y)
     assert_close(y, O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
+
+
+@pytest.mark.parametrize("M,K", [(8, 256), (149, 1024), (1500, 2048), (18944, 256),
+                                 (20000, 4096)])
+def test_fast_q4_0_row_tile_shapes(M, K):
+    """Row counts from a few rows per CTA to full tiles with a ragged last
+    tile, and 8..128 blocks per row; results are identical run to run."""
+    x = acts(40 + M, K)
+    w = weights(40 + M, M * K)
+    blk = O.quantizeQ4_0(w).reshape(-1)
+    bd, xd = to_dev(blk, x)
+    y = dev_y(M)
+    L.dequantGemvQ4_0(bd, K // 32, xd, y)
+    first = to_host(y).copy()
+    assert_close(first, O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
+    L.dequantGemvQ4_0(bd, K // 32, xd, y)
+    assert bits_equal(to_host(y), first)  # run to run identical
+
+
+def test_fast_q4_0_several_sequential_groups_in_a_row():
+    """Finite groups at or above 2^100 take the sequential path; several of
+    them in one row, spread over the row's K-chunks, add up deterministically."""
+    M, K = 300, 4096
+    x = acts(15, K)
+    for j in (1, 9, 10, 63, 64, 127):
+        x[32 * j + 3] = F(3e30 * (1 if j % 2 else -1))
+    w = weights(15, M * K)
+    blk = O.quantizeQ4_0(w).reshape(-1)
+    bd, xd = to_dev(blk, x)
+    y = dev_y(M)
+    L.dequantGemvQ4_0(bd, K // 32, xd, y)
+    first = to_host(y).copy()
+    assert_close(first, O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
+    L.dequantGemvQ4_0(bd, K // 32, xd, y)
+    assert bits_equal(to_host(y), first)

@@ -365,6 +365,29 @@ def test_gemm_q8_tensor_core_shapes(M, K, n):
     assert_bits(to_host(y), want)
 
 
+@pytest.mark.parametrize("M,K,n", [(1, 32, 1), (37, 512, 2), (300, 256, 3), (149, 4096, 7),
+                                   (4100, 1024, 8), (333, 512, 9), (150, 2048, 16),
+                                   (64, 512, 17), (97, 11008, 8)])
+def test_gemm_few_columns_q8_and_i4q8(M, K, n):
+    """Up to 16 columns with 32-wide groups run as the GEMV skeleton's column
+    formats (ragged row tiles, one to sixteen columns, K = 11008 as in the
+    Llama down projection); 17 columns take the wide-GEMM kernels."""
+    w = weights(M + n, M * K)
+    x = acts(M + n, K * n)
+    wq, wd = O.quantizeQ8_0Split(w)
+    xq, xd = O.quantizeQ8_0Split(x)
+    d = to_dev(wq, wd, xq, xd)
+    y = dev_y(M * n)
+    L.dequantGemmQ8(*d[:2], 32, *d[2:], n, y)
+    assert_bits(to_host(y), O.dequantGemmQ8(wq, wd, 32, xq, xd, n))
+    s4 = O.calibrateSymmetric(w, 32, 7.0)
+    p4 = O.packInt4(O.quantize(w, s4, 32, "i4"))
+    d4 = to_dev(p4, s4)
+    y4 = dev_y(M * n)
+    L.dequantGemmI4Q8(*d4, 32, *d[2:], n, y4)
+    assert_bits(to_host(y4), O.dequantGemmI4Q8(p4, s4, 32, xq, xd, n))
+
+
 def test_gemm_column_equals_gemv_on_device():
     """test_sdot.nim:243-282 on the device: every GEMM column is the GEMV."""
     M, K, n = 129, 512, 5
