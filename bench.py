@@ -42,6 +42,10 @@ FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 
 M1, K1 = 11008, 4096   # config 1
+# config 4: one Llama-7B layer is q, k, v, o (4096 x 4096) and gate, up
+# (11008 x 4096) over the 4096-vector, stored as one 38400-row matrix, plus
+# down (4096 x 11008) over the 11008-vector; packed int4, group 32.
+CAT_ROWS, DOWN_ROWS, DOWN_K, LAYERS = 4 * 4096 + 2 * 11008, 4096, 11008, 32
 
 
 def cfg1_bytes(M=M1, K=K1) -> int:
@@ -138,6 +142,70 @@ class Cfg1Workload:
 
     def step(self, i):
         self.L.dequantGemvQ4_0(self.w[i % self.ncopies], self.bpr, self.x, self.y)
+
+
+def cfg4_bytes_per_layer() -> int:
+    """Weight bytes (int4 codes + fp32 group scales) of one layer, all GPUs."""
+    return (CAT_ROWS * (K1 // 2 + K1 // 32 * 4) + DOWN_ROWS * (DOWN_K // 2 + DOWN_K // 32 * 4))
+
+
+class Cfg4Workload:
+    """Config 4: 32 Llama-7B layers of packed-int4 weights, this rank's rows.
+
+    Each rank holds rows [r * rows / P, (r + 1) * rows / P) of the concatenated
+    matrix and of down (P divides both).  A step is one decode sweep: per
+    layer, quantize the 4096-vector to Q8_0 on the GPU, dequantGemvI4Q8 over
+    the concatenated matrix, quantize the 11008-vector, dequantGemvI4Q8 over
+    down; with P > 1 the layer's outputs are then all-gathered once.  The
+    layer's output buffer is rank-major -- rank r's [concatenated slice | down
+    slice] -- so the gather is one call over 42496 / P floats per rank."""
+
+    def __init__(self, torch, L, world, rank, layers=LAYERS):
+        assert CAT_ROWS % world == 0 and DOWN_ROWS % world == 0
+        self.torch, self.L, self.world, self.rank, self.layers = torch, L, world, rank, layers
+        self.rc, self.rd = CAT_ROWS // world, DOWN_ROWS // world
+        self.per = self.rc + self.rd
+        g = torch.Generator(device="cuda")
+        self.wc, self.sc, self.wd, self.sd = [], [], [], []
+        for layer in range(layers):
+            for rows, k, W, S, part in ((self.rc, K1, self.wc, self.sc, 0),
+                                        (self.rd, DOWN_K, self.wd, self.sd, 1)):
+                g.manual_seed(4000 + layer + 100 * part + 1000 * rank)
+                w = torch.randn(rows * k, generator=g, device="cuda", dtype=torch.float32) * 0.02
+                sc = torch.empty(rows * k // 32, dtype=torch.float32, device="cuda")
+                L.calibrateSymmetric(w, 32, 7.0, sc)
+                pk = torch.empty(rows * k // 2, dtype=torch.uint8, device="cuda")
+                L.quantizeI4Packed(w, sc, 32, pk)
+                del w
+                W.append(pk)
+                S.append(sc)
+        g.manual_seed(4000 + 1_000_000)
+        self.x = torch.randn(layers, K1, generator=g, device="cuda", dtype=torch.float32)
+        self.xd = torch.randn(layers, DOWN_K, generator=g, device="cuda", dtype=torch.float32)
+        self.xq = torch.empty(K1, dtype=torch.int8, device="cuda")
+        self.xs = torch.empty(K1 // 32, dtype=torch.float32, device="cuda")
+        self.dq = torch.empty(DOWN_K, dtype=torch.int8, device="cuda")
+        self.ds = torch.empty(DOWN_K // 32, dtype=torch.float32, device="cuda")
+        self.y = torch.empty(layers, world * self.per, dtype=torch.float32, device="cuda")
+        torch.cuda.empty_cache()
+
+    def layer(self, pool, layer):
+        L = self.L
+        yl = self.y[layer]
+        off = self.rank * self.per
+        L.quantizeQ8_0Split(self.x[layer], self.xq, self.xs)
+        L.dequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.xq, self.xs,
+                          yl[off:off + self.rc])
+        L.quantizeQ8_0Split(self.xd[layer], self.dq, self.ds)
+        L.dequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.dq, self.ds,
+                          yl[off + self.rc:off + self.per])
+        if pool is not None:
+            from nim_lowprec_b200 import parallel as P
+            pool.call("lp_pool_gather_rows", yl.data_ptr(), self.world * self.per, 1, P._stream())
+
+    def step(self, pool, i):
+        for layer in range(self.layers):
+            self.layer(pool, layer)
 
 
 def graph_time(torch, step, K, W, barrier, chunk=500):
@@ -272,9 +340,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-formats", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="launch each hot kernel once (for ncu), no timing")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        import torch
+
+        import nim_lowprec_b200 as L
+        for name in profile_kernels(torch, L):
+            print("launched:", name, flush=True)
+        return 0
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -359,6 +436,25 @@ def main():
     e_ms = float(t.item())
     e2e_value = world * e2e_steps * cfg1_bytes() / (e_ms / 1e3) / 1e9
 
+    # config 4 (every rank): the 32-layer int4 decode sweep, pooled for N > 1
+    cfg4 = None
+    if not args.no_formats:
+        wl4 = Cfg4Workload(torch, L, world, rank)
+        st4 = 20
+        ms4, g5 = graph_time(torch, lambda i: wl4.step(pool, i), st4, 3, barrier, chunk=st4)
+        del g5
+        t = torch.tensor([ms4], device="cuda")
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sweep_ms = float(t.item()) / st4
+        gbs = LAYERS * cfg4_bytes_per_layer() / (sweep_ms / 1e3) / 1e9
+        cfg4 = {"GB/s": round(gbs, 1), "frac_per_gpu": round(gbs / world / peak, 3),
+                "ms_per_sweep": round(sweep_ms, 4), "layers": LAYERS,
+                "weight_bytes_per_sweep": LAYERS * cfg4_bytes_per_layer(),
+                "launches_per_layer": 4, "gather_per_layer": world > 1}
+        del wl4
+        torch.cuda.empty_cache()
+
     formats = None
     if not args.no_formats and world == 1:
         formats = per_format(torch, L, barrier)
@@ -409,8 +505,90 @@ def main():
     }
     if formats:
         line["formats"] = formats
+    if cfg4:
+        line["config4_llama7b_i4q8_sweep"] = cfg4
     print(json.dumps(line), flush=True)
     return 0
+
+
+PROFILE_KERNELS = "gemv_kernel|k_gemm_tc|k_quantize_q8_0"
+
+
+def profile_kernels(torch, L):
+    """One launch of every hot kernel, for an ncu capture of exactly these
+    launches (`-k regex:` PROFILE_KERNELS `-c 12`).  Inputs are prepared
+    with other kernels (torch RNG, the weight encoders), and each workload is
+    freed before the next, so a capture holds a few hundred MB at most."""
+    g = torch.Generator(device="cuda")
+    sync = torch.cuda.synchronize
+    done = []
+
+    def rnd(n, seed, scale=1.0):
+        g.manual_seed(seed)
+        return torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * scale
+
+    def i8(n, seed):
+        g.manual_seed(seed)
+        return torch.randint(-127, 128, (n,), dtype=torch.int8, device="cuda", generator=g)
+
+    def scales(n, seed):
+        g.manual_seed(seed)
+        return torch.rand(n, generator=g, device="cuda", dtype=torch.float32) * 1e-3
+
+    def run(name, fn):
+        sync()
+        fn()
+        sync()
+        done.append(name)
+
+    M = K = 4096
+    wq, wd = i8(M * K, 0), scales(M * K // 32, 0)
+    xq, xs, y = i8(K, 1), scales(K // 32, 1), torch.empty(M, device="cuda")
+    run("config0 dequantGemvQ8 4096x4096", lambda: L.dequantGemvQ8(wq, wd, 32, xq, xs, y))
+    for B in (8, 64, 512):
+        xqB, xsB = i8(K * B, 2 + B), scales(K * B // 32, 2 + B)
+        yB = torch.empty(M * B, device="cuda")
+        run(f"config3 dequantGemmQ8 B={B}",
+            lambda: L.dequantGemmQ8(wq, wd, 32, xqB, xsB, B, yB))
+        del xqB, xsB, yB
+    del wq, wd, xq, xs, y
+    torch.cuda.empty_cache()
+
+    w = rnd(M1 * K1, 1, 0.02)
+    blocks = torch.empty(M1 * K1 // 32 * 18, dtype=torch.uint8, device="cuda")
+    L.quantizeQ4_0Batch(w, blocks)
+    del w
+    x, y = rnd(K1, 1_000_001), torch.empty(M1, device="cuda")
+    run("config1 dequantGemvQ4_0 block-float", lambda: L.dequantGemvQ4_0(blocks, K1 // 32, x, y))
+    with L.fp32_mode("exact"):
+        run("config1 dequantGemvQ4_0 exact", lambda: L.dequantGemvQ4_0(blocks, K1 // 32, x, y))
+    del blocks, x, y
+    torch.cuda.empty_cache()
+
+    M2 = 14336
+    w = rnd(M2 * K1, 2, 0.02)
+    sc = torch.empty(M2 * K1 // 32, dtype=torch.float32, device="cuda")
+    L.calibrateMX(w, 32, 2, sc)
+    pk = torch.empty(M2 * K1 // 2, dtype=torch.uint8, device="cuda")
+    L.quantizeF4Packed(w, sc, 32, pk)
+    del w
+    x, y = rnd(K1, 1_000_002), torch.empty(M2, device="cuda")
+    run("config2 dequantGemvF4 block-float", lambda: L.dequantGemvF4(pk, sc, 32, x, y))
+    del sc, pk, x, y
+    torch.cuda.empty_cache()
+
+    n = 16_777_216
+    xb = rnd(n, 5)
+    qs = torch.empty(n, dtype=torch.int8, device="cuda")
+    d = torch.empty(n // 32, dtype=torch.float32, device="cuda")
+    run("quantizeQ8_0 K=16777216", lambda: L.quantizeQ8_0Split(xb, qs, d))
+    del xb, qs, d
+    torch.cuda.empty_cache()
+
+    wl4 = Cfg4Workload(torch, L, 1, 0, layers=1)
+    run("config4 layer 0: quantizeQ8_0 (4096), dequantGemvI4Q8 38400x4096, "
+        "quantizeQ8_0 (11008), dequantGemvI4Q8 4096x11008", lambda: wl4.layer(None, 0))
+    return done
 
 
 def per_format(torch, L, barrier, steps=5000):
@@ -474,6 +652,8 @@ def per_format(torch, L, barrier, steps=5000):
     wd = torch.empty(M * K // 32, dtype=torch.float32, device="cuda")
     L.quantizeQ8_0Split(w, wq, wd)
     del w
+    R = -(-3 * L2_BYTES // (M * K + M * K // 8)) + 1
+    copies = [(wq, wd)] + [(wq.clone(), wd.clone()) for _ in range(R - 1)]
     for B in (8, 64, 512):
         x = rnd(K * B, 1_000_003)
         xq = torch.empty(K * B, dtype=torch.int8, device="cuda")
@@ -481,11 +661,15 @@ def per_format(torch, L, barrier, steps=5000):
         L.quantizeQ8_0Split(x, xq, xs)
         y = torch.empty(M * B, dtype=torch.float32, device="cuda")
         st = 200 if B == 512 else 1000
-        ms, gr = graph_time(torch, lambda i: L.dequantGemmQ8(wq, wd, 32, xq, xs, B, y), st, 3, barrier)
+        ms, gr = graph_time(torch, lambda i: L.dequantGemmQ8(*copies[i % R], 32, xq, xs, B, y), st, 3,
+                            barrier)
         del gr
         us = ms / st * 1e3
         tops = 2 * M * K * B / (us / 1e6) / 1e12
-        out[f"config3_gemm_q8_B{B}"] = {"TOPS": round(tops, 2), "us": round(us, 2)}
+        out[f"config3_gemm_q8_B{B}"] = {"TOPS": round(tops, 2), "us": round(us, 2),
+                                        "path": "GEMV-skeleton columns (CUDA-core dp4a)" if B <= 16
+                                        else "tcgen05 kind::i8"}
+    del copies
     return out
 
 
