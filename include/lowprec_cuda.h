@@ -266,6 +266,14 @@ int lp_pool_init(lp_pool_t *pool, const uint8_t *id128, int nranks, int rank, in
 /* Leave and free the pool; NULL is accepted (shutdown is idempotent). */
 int lp_pool_destroy(lp_pool_t pool);
 int lp_pool_size(lp_pool_t pool, int *nranks, int *rank);
+/* The gather's transport (no counterpart in the reference).  By default a pool
+ * whose ranks each have their own GPU maps every rank's exchange buffer over
+ * NVLink (CUDA IPC, set up by lp_pool_init) and gathers with one kernel of
+ * peer stores and bounded completion counters; enable = 0 selects the NCCL
+ * group instead.  Every rank must make the same choice before its next gather.
+ * LP_ERR_UNSUPPORTED: the exchange could not be mapped on every rank. */
+int lp_pool_set_p2p(lp_pool_t pool, int enable);
+int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
 /* Gather every rank's row slice of y (m rows of per_row floats) in place. */
 int lp_pool_gather_rows(lp_pool_t pool, float *y, int64_t m, int64_t per_row, lp_stream_t stream);
 

@@ -77,6 +77,8 @@ SIGNATURES = {
     "lp_pool_destroy": "p",
     "lp_pool_size": "ppp",
     "lp_pool_gather_rows": "ppnnp",
+    "lp_pool_set_p2p": "pi",
+    "lp_pool_get_p2p": "pp",
     "lp_pool_dequant_gemv": "ppnpnnpnpnp",
     "lp_pool_dequant_gemv_i4": "ppnpnnpnpnp",
     "lp_pool_dequant_gemv_f4": "ppnpnnpnpnp",

@@ -135,7 +135,9 @@ int lp_device_error(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LP_ERR_CUDA;
   unsigned int e = lp::take_error_gemv();
   const unsigned int e2 = lp::take_error_gemm_tc();
+  const unsigned int e3 = lp::take_error_pool();
   if (!e) e = e2;
+  if (!e) e = e3;
   return static_cast<int>(e);
 }
 

@@ -64,6 +64,7 @@ int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, co
 // error words of the translation units whose kernels wait (read + clear)
 unsigned int take_error_gemv();
 unsigned int take_error_gemm_tc();
+unsigned int take_error_pool();
 
 // Records the CUDA error text for lp_last_error_detail() and maps to a status.
 void note_cuda_error(cudaError_t e);

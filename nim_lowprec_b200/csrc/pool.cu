@@ -10,20 +10,46 @@
 // with one NCCL group of per-rank broadcasts (an all-gather with unequal
 // counts), in place in y, on the caller's stream.
 //
+// The gather has two forms.  By default every rank also maps every other
+// rank's exchange buffer (CUDA IPC over NVLink; the handles travel over the
+// pool's own NCCL communicator at creation): one small kernel stores this
+// rank's slice into every peer's buffer, each value with the gather's number
+// in the same 8-byte word, and reads the peers' slices out of its own buffer
+// as their words arrive (bounded waits).  That is one launch
+// of a few microseconds where an NCCL call costs ~12 us of latency.  The NCCL
+// group is the fallback (lp_pool_set_p2p(pool, 0), outputs larger than the
+// exchange buffer, or a box where the mapping is not possible on every rank).
+//
 // NCCL is loaded at pool creation (dlopen), so the library itself loads and
 // runs on machines without NCCL; only the pool calls report LP_ERR_NCCL.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 
+#include "lp_device.cuh"
 #include "lp_internal.h"
+
+namespace {
+constexpr int kMaxP2pRanks = 8;
+constexpr int64_t kXchgFloats = int64_t{1} << 20;  // floats per parity (4 MB)
+constexpr int64_t kXchgBytes = 2 * kXchgFloats * 8;  // two halves of 8-byte words
+struct PeerBufs {
+  uint8_t* p[kMaxP2pRanks];
+};
+}  // namespace
 
 struct lp_pool {
   ncclComm_t comm;
   int nranks, rank, device;
+  int p2p;         // 1: gathers through the exchange buffers
+  int p2p_ready;   // the exchange was mapped on every rank at creation
+  uint8_t* xbuf;   // this rank's exchange buffer: two halves of 8-byte words
+  uint32_t* state; // [0] gathers finished, [1] CTAs finished in the current one
+  PeerBufs peers;  // every rank's exchange buffer as mapped here
 };
 
 namespace {
@@ -37,6 +63,8 @@ struct NcclApi {
   ncclResult_t (*group_end)() = nullptr;
   ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 
@@ -54,10 +82,11 @@ const NcclApi& nccl() {
     LP_SYM(group_start, "ncclGroupStart");
     LP_SYM(group_end, "ncclGroupEnd");
     LP_SYM(broadcast, "ncclBroadcast");
+    LP_SYM(all_gather, "ncclAllGather");
     LP_SYM(error_string, "ncclGetErrorString");
 #undef LP_SYM
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.group_start &&
-             api.group_end && api.broadcast && api.error_string;
+             api.group_end && api.broadcast && api.all_gather && api.error_string;
   });
   return api;
 }
@@ -70,14 +99,101 @@ int nccl_status(ncclResult_t r) {
 
 inline cudaStream_t S(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
 
-void rows_of(int64_t m, int nranks, int rank, int64_t* b, int64_t* e) {
+__host__ __device__ inline void rows_of(int64_t m, int nranks, int rank, int64_t* b, int64_t* e) {
   const int64_t per = m / nranks;
   *b = per * rank;
   *e = (rank == nranks - 1) ? m : *b + per;
 }
 
+// ------------------------------------------------- NVLink exchange gather
+// Every value crosses as one naturally aligned 8-byte store of (gather number
+// << 32 | value bits), which lands whole; the receiver polls each of its words
+// until the word carries this gather's number.  No fences or counters: a
+// system-scope fence costs microseconds here.
+__device__ __forceinline__ void st_word(uint64_t* a, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// Gather number e (1, 2, ...) uses exchange half e & 1, so a rank one gather
+// ahead writes the other half while its peers still read this one (two ahead
+// is impossible: finishing a gather needs every peer's words of that gather,
+// and a peer sends them only after finishing the previous one).  e is kept on
+// the device (state[0]) so CUDA-graph replays count too; all ranks make the
+// same gathers, so they agree on it.  Waits are bounded (error word on
+// timeout).
+__global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t per_row,
+                                                   int nranks, int rank, PeerBufs peers,
+                                                   uint32_t* state) {
+  __shared__ uint32_t s_e;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int64_t C = gridDim.x;
+  if (tid == 0) s_e = reinterpret_cast<volatile uint32_t*>(state)[0] + 1u;
+  __syncthreads();
+  const uint32_t e = s_e;
+  const uint64_t tag = static_cast<uint64_t>(e) << 32;
+  const int64_t half = (e & 1u) * kXchgFloats;
+  int64_t b, en;
+  rows_of(m, nranks, rank, &b, &en);
+  const int64_t off = b * per_row, len = (en - b) * per_row;
+  const int64_t chunk = (len + C - 1) / C;
+  const int64_t lo = min(len, blockIdx.x * chunk), hi = min(len, lo + chunk);
+  for (int64_t i = lo + tid; i < hi; i += nthr) {
+    const uint64_t w = tag | __float_as_uint(y[off + i]);
+    for (int q = 0; q < nranks; ++q)
+      if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
+  }
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(peers.p[rank]) + half;
+  bool ok = true;
+  const uint64_t t0 = lp::global_ns();
+  for (int q = 0; q < nranks && ok; ++q) {
+    if (q == rank) continue;
+    int64_t qb, qe;
+    rows_of(m, nranks, q, &qb, &qe);
+    const int64_t qo = qb * per_row, ql = (qe - qb) * per_row;
+    const int64_t qc = (ql + C - 1) / C;
+    const int64_t qlo = min(ql, blockIdx.x * qc), qhi = min(ql, qlo + qc);
+    for (int64_t i = qlo + tid; i < qhi && ok; i += nthr) {
+      uint64_t w = ld_word(mine + qo + i);
+      for (uint32_t n = 1; (w >> 32) != e; ++n) {
+        if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
+          lp::raise_error(LP_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        w = ld_word(mine + qo + i);
+      }
+      if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w));
+    }
+  }
+  // the last CTA to finish publishes e as the finished gather count
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(state + 1, 1u) == static_cast<uint32_t>(C) - 1) {
+      state[1] = 0;
+      __threadfence();
+      atomicExch(state, e);
+    }
+  }
+}
+
+int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st) {
+  const int64_t total = m * per_row;
+  const int64_t per_rank = (total + p->nranks - 1) / p->nranks;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(16, (per_rank + 2047) / 2048)));
+  k_gather_p2p<<<grid, 256, 0, st>>>(y, m, per_row, p->nranks, p->rank, p->peers, p->state);
+  return lp::cuda_status(cudaGetLastError());
+}
+
 // y[0, m*per_row) from every rank's slice of rows.
 int gather(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st) {
+  if (p->nranks == 1 || m == 0) return LP_OK;
+  if (p->p2p && m * per_row <= kXchgFloats) return gather_p2p(p, y, m, per_row, st);
   const NcclApi& api = nccl();
   int r = nccl_status(api.group_start());
   if (r) return r;
@@ -95,7 +211,108 @@ int gather(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st) {
   return first ? first : r;
 }
 
+// Maps every rank's exchange buffer into this process.  All ranks take part
+// (two NCCL all-gathers); the exchange is used only when every rank mapped
+// every peer and every rank has its own GPU.
+void setup_p2p(lp_pool* p) {
+  p->p2p = p->p2p_ready = 0;
+  p->xbuf = nullptr;
+  p->state = nullptr;
+  std::memset(&p->peers, 0, sizeof(p->peers));
+  if (p->nranks < 2) return;
+  const NcclApi& api = nccl();
+  struct Card {
+    cudaIpcMemHandle_t h;
+    char bus[32];
+    int ok;
+  };
+  Card mine;
+  std::memset(&mine, 0, sizeof(mine));
+  bool ok = p->nranks <= kMaxP2pRanks;
+  ok = ok && cudaMalloc(&p->xbuf, kXchgBytes) == cudaSuccess;
+  ok = ok && cudaMemset(p->xbuf, 0, kXchgBytes) == cudaSuccess;
+  ok = ok && cudaMalloc(&p->state, 4 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaMemset(p->state, 0, 4 * sizeof(uint32_t)) == cudaSuccess;
+  ok = ok && cudaIpcGetMemHandle(&mine.h, p->xbuf) == cudaSuccess;
+  ok = ok && cudaDeviceGetPCIBusId(mine.bus, sizeof(mine.bus), p->device) == cudaSuccess;
+  mine.ok = ok ? 1 : 0;
+  cudaGetLastError();
+  // every rank reaches both all-gathers, whatever happened above
+  Card* dev = nullptr;
+  Card* all = new Card[p->nranks];
+  cudaStream_t st = nullptr;
+  bool xok = cudaMalloc(&dev, sizeof(Card) * (p->nranks + 1)) == cudaSuccess &&
+             cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+             cudaMemcpy(dev + p->nranks, &mine, sizeof(Card), cudaMemcpyHostToDevice) == cudaSuccess;
+  xok = xok && api.all_gather(dev + p->nranks, dev, sizeof(Card), ncclChar, p->comm, st) == ncclSuccess;
+  xok = xok && cudaStreamSynchronize(st) == cudaSuccess &&
+        cudaMemcpy(all, dev, sizeof(Card) * p->nranks, cudaMemcpyDeviceToHost) == cudaSuccess;
+  bool mapped = xok;
+  for (int q = 0; q < p->nranks && mapped; ++q) {
+    mapped = all[q].ok != 0;
+    for (int r = 0; r < q && mapped; ++r) mapped = std::strcmp(all[q].bus, all[r].bus) != 0;
+  }
+  for (int q = 0; q < p->nranks && mapped; ++q) {
+    if (q == p->rank) {
+      p->peers.p[q] = p->xbuf;
+      continue;
+    }
+    void* ptr = nullptr;
+    mapped = cudaIpcOpenMemHandle(&ptr, all[q].h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    p->peers.p[q] = static_cast<uint8_t*>(ptr);
+  }
+  cudaGetLastError();
+  // agree: the exchange is on only if every rank mapped every peer
+  int agree = mapped ? 1 : 0;
+  int* dflag = nullptr;
+  bool aok = xok && cudaMalloc(&dflag, sizeof(int) * (p->nranks + 1)) == cudaSuccess &&
+             cudaMemcpy(dflag + p->nranks, &agree, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+             api.all_gather(dflag + p->nranks, dflag, sizeof(int), ncclChar, p->comm, st) == ncclSuccess &&
+             cudaStreamSynchronize(st) == cudaSuccess;
+  int all_ok = aok ? 1 : 0;
+  if (aok) {
+    int* flags = new int[p->nranks];
+    if (cudaMemcpy(flags, dflag, sizeof(int) * p->nranks, cudaMemcpyDeviceToHost) != cudaSuccess)
+      all_ok = 0;
+    for (int q = 0; q < p->nranks && all_ok; ++q) all_ok = flags[q] != 0;
+    delete[] flags;
+  }
+  if (dflag) cudaFree(dflag);
+  if (dev) cudaFree(dev);
+  if (st) cudaStreamDestroy(st);
+  delete[] all;
+  cudaGetLastError();
+  p->p2p = all_ok;
+  p->p2p_ready = all_ok;
+}
+
+void teardown_p2p(lp_pool* p) {
+  cudaDeviceSynchronize();
+  for (int q = 0; q < kMaxP2pRanks; ++q)
+    if (p->peers.p[q] && q != p->rank) cudaIpcCloseMemHandle(p->peers.p[q]);
+  if (p->xbuf) cudaFree(p->xbuf);
+  if (p->state) cudaFree(p->state);
+  std::memset(&p->peers, 0, sizeof(p->peers));
+  p->xbuf = nullptr;
+  p->state = nullptr;
+  p->p2p = p->p2p_ready = 0;
+  cudaGetLastError();
+}
+
 }  // namespace
+
+namespace lp {
+// The error word of this translation unit (see lp_device.cuh).
+unsigned int take_error_pool() {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return LP_ERR_CUDA;
+  if (v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_device_error, &z, sizeof(z));
+  }
+  return v;
+}
+}  // namespace lp
 
 extern "C" {
 
@@ -131,12 +348,16 @@ int lp_pool_init(lp_pool_t* pool, const uint8_t* id, int nranks, int rank, int d
   if (r) return r;
   ncclUniqueId u;
   std::memcpy(u.internal, id, NCCL_UNIQUE_ID_BYTES);
-  lp_pool* p = new lp_pool{nullptr, nranks, rank, device};
+  lp_pool* p = new lp_pool{};
+  p->nranks = nranks;
+  p->rank = rank;
+  p->device = device;
   r = nccl_status(api.comm_init_rank(&p->comm, nranks, u, rank));
   if (r) {
     delete p;
     return r;
   }
+  setup_p2p(p);
   *pool = p;
   return LP_OK;
 }
@@ -144,6 +365,8 @@ int lp_pool_init(lp_pool_t* pool, const uint8_t* id, int nranks, int rank, int d
 int lp_pool_destroy(lp_pool_t pool) {
   if (!pool) return LP_OK;  // idempotent, like shutdown (parallel.nim:153-167)
   int r = LP_OK;
+  cudaSetDevice(pool->device);
+  teardown_p2p(pool);
   if (pool->comm) r = nccl_status(nccl().comm_destroy(pool->comm));
   delete pool;
   return r;
@@ -153,6 +376,23 @@ int lp_pool_size(lp_pool_t pool, int* nranks, int* rank) {
   if (!pool || !nranks || !rank) return LP_ERR_ARG;
   *nranks = pool->nranks;
   *rank = pool->rank;
+  return LP_OK;
+}
+
+int lp_pool_set_p2p(lp_pool_t pool, int enable) {
+  if (!pool) return LP_ERR_ARG;
+  if (!enable) {
+    pool->p2p = 0;
+    return LP_OK;
+  }
+  if (!pool->p2p_ready) return LP_ERR_UNSUPPORTED;
+  pool->p2p = 1;
+  return LP_OK;
+}
+
+int lp_pool_get_p2p(lp_pool_t pool, int* enabled) {
+  if (!pool || !enabled) return LP_ERR_ARG;
+  *enabled = pool->p2p;
   return LP_OK;
 }
 

@@ -63,6 +63,64 @@ __global__ void k_quantize_q8_0(const float* __restrict__ src, int64_t nblocks,
   }
 }
 
+// The same encoder, bandwidth-shaped: 8 lanes per block, a float4 per lane,
+// two blocks per thread per pass (two loads in flight); the block max meets
+// by three shuffles inside the 8-lane group.  fmaxf ignores NaN like the
+// reference's strict `>` scan.  It waits for the previous kernel in the
+// stream before reading or writing anything (it is launched with
+// programmatic stream serialization, so its launch overlaps that kernel's
+// tail) and does not release its own dependents early: its output may be the
+// next GEMV's weights.
+__device__ __forceinline__ void q8_block4(const float4 v, int sub, int lane, int64_t b, bool valid,
+                                          uint8_t* blocks, int8_t* qs, float* dsplit) {
+  const unsigned gm = 0xFFu << (lane & 24);  // this block's 8 lanes
+  float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  a = fmaxf(a, __shfl_xor_sync(gm, a, 1, 8));
+  a = fmaxf(a, __shfl_xor_sync(gm, a, 2, 8));
+  a = fmaxf(a, __shfl_xor_sync(gm, a, 4, 8));
+  if (!valid) return;
+  const float d = __fdiv_rn(a, 127.0f);
+  const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  const float e[4] = {v.x, v.y, v.z, v.w};
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float r = roundf(__fmul_rn(e[i], id));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    word |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * i);
+  }
+  const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+  if (blocks) {
+    unsigned short* blk = reinterpret_cast<unsigned short*>(blocks + b * 34);
+    blk[1 + 2 * sub] = static_cast<unsigned short>(word & 0xFFFFu);
+    blk[2 + 2 * sub] = static_cast<unsigned short>(word >> 16);
+    if (sub == 0) blk[0] = dh;
+  }
+  if (qs) reinterpret_cast<uint32_t*>(qs + b * 32)[sub] = word;
+  if (dsplit && sub == 0) dsplit[b] = h2f(dh);
+}
+
+__global__ void __launch_bounds__(128) k_quantize_q8_0_v4(const float* __restrict__ src,
+                                                          int64_t nblocks, uint8_t* blocks,
+                                                          int8_t* qs, float* dsplit) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const int64_t groups = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 3);
+  const int64_t first = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 3;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the loop bound is uniform over the warp (whole passes), so the 8-lane
+  // shuffles always see all of their lanes
+  const int64_t warp0 = first - (lane >> 3);
+  for (int64_t p = 0; warp0 + p * 2 * groups < nblocks; ++p) {
+    const int64_t b1 = first + p * 2 * groups, b2 = b1 + groups;
+    const bool v1 = b1 < nblocks, v2 = b2 < nblocks;
+    const float4 x1 = v1 ? __ldg(reinterpret_cast<const float4*>(src + b1 * 32) + sub) : z;
+    const float4 x2 = v2 ? __ldg(reinterpret_cast<const float4*>(src + b2 * 32) + sub) : z;
+    q8_block4(x1, sub, lane, b1, v1, blocks, qs, dsplit);
+    q8_block4(x2, sub, lane, b2, v2, blocks, qs, dsplit);
+  }
+}
+
 // ggml.nim:77-97: vmax = the first element of largest magnitude (strict >
 // scan from 0), d = vmax / -8, q = clamp(int(round(x*id)) + 8, 0, 15).
 __global__ void k_quantize_q4_0(const float* __restrict__ src, int64_t nblocks,
@@ -242,8 +300,23 @@ int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* q
                          cudaStream_t st) {
   const int64_t nb = n / 32;
   if (nb == 0) return LP_OK;
-  k_quantize_q8_0<<<grid_for(nb * 32, kThreads), kThreads, 0, st>>>(src, nb, blocks, qs, d);
-  return cuda_status(cudaGetLastError());
+  const bool aligned = (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(qs) & 3) == 0 &&
+                       (reinterpret_cast<uintptr_t>(blocks) & 1) == 0;
+  if (!aligned) {
+    k_quantize_q8_0<<<grid_for(nb * 32, kThreads), kThreads, 0, st>>>(src, nb, blocks, qs, d);
+    return cuda_status(cudaGetLastError());
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid_for(nb * 4, 128)));
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k_quantize_q8_0_v4, src, nb, blocks, qs, d));
 }
 
 int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStream_t st) {

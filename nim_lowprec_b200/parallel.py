@@ -133,6 +133,19 @@ class NcclPool:
     def call(self, name: str, *args):
         N.check(getattr(N.lib(), name)(self._h, *args), name)
 
+    @property
+    def p2p(self) -> bool:
+        """True when gathers use the NVLink exchange buffers (the default when
+        every rank has its own GPU), False for the NCCL group."""
+        v = ctypes.c_int(0)
+        N.check(N.lib().lp_pool_get_p2p(self._h, ctypes.byref(v)), "lp_pool_get_p2p")
+        return bool(v.value)
+
+    @p2p.setter
+    def p2p(self, enable: bool) -> None:
+        # every rank must switch before its next gather
+        N.check(N.lib().lp_pool_set_p2p(self._h, 1 if enable else 0), "lp_pool_set_p2p")
+
     def shutdown(self):
         if self._h:
             N.check(N.lib().lp_pool_destroy(self._h), "lp_pool_destroy")

@@ -88,6 +88,41 @@ def _rank_main(rank, world, port, q):
             y = torch.full((M * n,), float("nan"), device="cuda")
             P.parDequantGemmQ8(pool, wq, wd, 32, xq, xd, n, y)
             same(f"gemm/{i}", y, ref)
+        # the library pool gathers over NVLink by default (one GPU per rank);
+        # both transports, back-to-back gathers (alternating exchange halves)
+        # and CUDA-graph replays give the single-GPU bits
+        npool = pools[1]
+        if not npool.p2p:
+            bad.append("p2p exchange not enabled")
+        refs = []
+        for j in range(n):
+            r_ = torch.empty(M, device="cuda")
+            L.dequantGemvQ8(wq, wd, 32, xq[j * K:(j + 1) * K], xd[j * K // 32:(j + 1) * K // 32], r_)
+            refs.append(r_)
+        for mode in (True, False, True):
+            npool.p2p = mode
+            for j in range(n):
+                y = torch.full((M,), float("nan"), device="cuda")
+                P.parDequantGemvQ8(npool, wq, wd, 32, xq[j * K:(j + 1) * K],
+                                   xd[j * K // 32:(j + 1) * K // 32], y)
+                same(f"q8-col{j}-p2p{int(mode)}", y, refs[j])
+        ys = [torch.full((M,), float("nan"), device="cuda") for _ in range(n)]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for j in range(n):
+                    P.parDequantGemvQ8(npool, wq, wd, 32, xq[j * K:(j + 1) * K],
+                                       xd[j * K // 32:(j + 1) * K // 32], ys[j])
+        torch.cuda.current_stream().wait_stream(s)
+        for rep in range(3):
+            for yy in ys:
+                yy.fill_(float("nan"))
+            g.replay()
+            for j in range(n):
+                same(f"graph{rep}-col{j}", ys[j], refs[j])
+        del g
         pools[1].shutdown()
         from nim_lowprec_b200 import _native as N
         if N.device_error() != 0:
