@@ -58,9 +58,16 @@ struct SmemLimits {
 
 }  // namespace
 
+thread_local const PushCtx* g_push = nullptr;
+thread_local int64_t g_push_off = 0;
+thread_local bool g_pushed = false;
+
 template <class Fmt>
 int launch_gemv(GemvParams p, cudaStream_t st) {
-  if (p.m == 0) return LP_OK;
+  if (p.m == 0) {
+    g_pushed = g_push != nullptr;  // an empty slice has nothing to send
+    return LP_OK;
+  }
   if (p.gpr == 0)  // no groups: every row is the empty fold, 0.0
     return cuda_status(cudaMemsetAsync(p.y, 0, static_cast<size_t>(p.m) * sizeof(float), st));
   const DeviceInfo& di = device_info();
@@ -149,6 +156,11 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
   // Only GEMV kernels release their dependents early, and a GEMV writes
   // nothing but y, which never aliases another GEMV's weights, so the early
   // weight stream cannot read memory still being written.
+  if (g_push) {
+    p.push = g_push;
+    p.push_off = g_push_off;
+    g_pushed = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(32 * (kNcw + 2));

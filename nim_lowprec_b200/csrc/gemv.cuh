@@ -36,6 +36,7 @@
 #include <type_traits>
 
 #include "lp_device.cuh"
+#include "lp_internal.h"
 
 namespace lp {
 
@@ -64,7 +65,36 @@ struct GemvParams {
   int stage_w_bytes, stage_s_bytes;
   float neg_zero;     // -0.0f, passed at run time (see mul2_rn)
   int ncol;           // activation columns (the small-n GEMM formats); else unused
+  const PushCtx* push;  // pooled call: also store every output into the other ranks
+  int64_t push_off;     // this slice's first element in the whole y
 };
+
+// The pooled form's stores: out value v of y element idx (of this slice) goes
+// to every other rank's exchange buffer as one 8-byte word tagged with the
+// gather number (the receiver polls the word's tag).
+struct PushTag {
+  uint64_t tag = 0;
+  int64_t half = 0;
+};
+__device__ __forceinline__ PushTag push_tag(const GemvParams& p) {
+  PushTag t;
+  if (p.push) {
+    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(p.push->state) + 1u;
+    t.tag = static_cast<uint64_t>(e) << 32;
+    t.half = (e & 1u) * kXchgWords;
+  }
+  return t;
+}
+__device__ __forceinline__ void push_out(const GemvParams& p, const PushTag& t, int64_t idx,
+                                         float v) {
+  const uint64_t w = t.tag | __float_as_uint(v);
+  const int nr = p.push->nranks, me = p.push->rank;
+  for (int q = 0; q < nr; ++q) {
+    if (q == me) continue;
+    uint64_t* a = reinterpret_cast<uint64_t*>(p.push->peers[q]) + t.half + p.push_off + idx;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+  }
+}
 
 // Formats with a column dimension (kCols) compute, per (row, group), one term
 // for each of p.ncol activation columns.  The skeleton treats (row r, column
@@ -150,7 +180,8 @@ __device__ __forceinline__ float fold_row(const float* T, int gpr) {
 // power of two with L * rows <= 32; each lane sums 4-term slices of the row
 // (four 16-byte loads in flight), then the L partial sums meet by shuffles.
 __device__ __forceinline__ void tree_fold(const float* T, int tstride, int rows, int gpr,
-                                          float* y, int lane) {
+                                          float* y, int lane, const GemvParams& p,
+                                          const PushTag& pt, int64_t y0) {
   int lg = 5;
   while (lg > 0 && (rows << lg) > 32) --lg;
   const int L = 1 << lg;
@@ -182,7 +213,10 @@ __device__ __forceinline__ void tree_fold(const float* T, int tstride, int rows,
   }
   float s = fadd(fadd(s0, s1), fadd(s2, s3));
   for (int o = L >> 1; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(0xffffffffu, s, o));
-  if (r < rows && sub == 0) y[r] = s;
+  if (r < rows && sub == 0) {
+    y[r] = s;
+    if (p.push) push_out(p, pt, y0 + r, s);
+  }
 }
 
 // Unordered fold, first stage, in a consumer warp whose 32 lanes hold 32
@@ -290,6 +324,13 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- folder
+    // a pooled call's gather number is final once the previous kernel in the
+    // stream (the previous gather) has completed
+    PushTag pt;
+    if (p.push) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      pt = push_tag(p);
+    }
     if constexpr (Fmt::kFold == Fold::Tree) {
       for (int t = 0; t < ntiles; ++t) {
         const int slot = t % p.ring;
@@ -297,7 +338,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         if (s_abort) break;
         const int r0 = row_begin + t * p.rt;
         const int rows = min(p.rt, row_end - r0);
-        tree_fold(terms + slot * p.rt * p.tstride, p.tstride, rows, p.tcols, p.y + r0, lane);
+        tree_fold(terms + slot * p.rt * p.tstride, p.tstride, rows, p.tcols, p.y + r0, lane, p, pt,
+                  r0);
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
       }
@@ -310,9 +352,12 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         const int r0 = row_begin + t * p.rt;
         const int nv = min(p.rt, row_end - r0) * p.ncol;
         const float* T = terms + slot * p.rt * p.ncol * p.tstride;
-        for (int v = lane; v < nv; v += 32)
-          p.y[static_cast<int64_t>(r0) * p.ncol + v] =
-              fold_row<Fmt::kFold>(T + v * p.tstride, p.gpr);
+        for (int v = lane; v < nv; v += 32) {
+          const int64_t idx = static_cast<int64_t>(r0) * p.ncol + v;
+          const float val = fold_row<Fmt::kFold>(T + v * p.tstride, p.gpr);
+          p.y[idx] = val;
+          if (p.push) push_out(p, pt, idx, val);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[slot]);
       }
@@ -332,9 +377,12 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
         if (ti < nt) {
           const int t = t0 + ti;
           const int r0 = row_begin + t * p.rt;
-          if (r < min(p.rt, row_end - r0) * vr)
-            p.y[static_cast<int64_t>(r0) * vr + r] =
-                fold_row<Fmt::kFold>(terms + ((t % p.ring) * vt + r) * p.tstride, p.gpr);
+          if (r < min(p.rt, row_end - r0) * vr) {
+            const int64_t idx = static_cast<int64_t>(r0) * vr + r;
+            const float val = fold_row<Fmt::kFold>(terms + ((t % p.ring) * vt + r) * p.tstride, p.gpr);
+            p.y[idx] = val;
+            if (p.push) push_out(p, pt, idx, val);
+          }
         }
         __syncwarp();
         if (lane == 0)

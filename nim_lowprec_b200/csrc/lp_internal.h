@@ -22,6 +22,24 @@ struct DeviceInfo {
 const DeviceInfo& device_info();
 
 struct GemvParams;
+
+// LpPool over NVLink: each rank's exchange buffer holds two halves of
+// kXchgWords 8-byte words (value bits | gather number << 32), mapped into
+// every rank.  A pooled GEMV given a PushCtx stores its outputs straight into
+// every other rank's buffer from its fold (pool.cu then only receives).
+constexpr int kMaxPushRanks = 8;
+constexpr int64_t kXchgWords = int64_t{1} << 20;
+struct PushCtx {
+  uint8_t* peers[kMaxPushRanks];  // every rank's exchange buffer as mapped here
+  uint32_t* state;                // this rank's finished-gather count (state[0])
+  int nranks, rank;
+};
+// Set by the pool around its local call (this thread only): the device copy of
+// the context and the slice's offset in y; launch_gemv reports in g_pushed
+// whether its kernel takes the push.
+extern thread_local const PushCtx* g_push;
+extern thread_local int64_t g_push_off;
+extern thread_local bool g_pushed;
 struct FmtI8;
 struct FmtI4;
 struct FmtF4;

@@ -34,8 +34,8 @@
 #include "lp_internal.h"
 
 namespace {
-constexpr int kMaxP2pRanks = 8;
-constexpr int64_t kXchgFloats = int64_t{1} << 20;  // floats per parity (4 MB)
+constexpr int kMaxP2pRanks = lp::kMaxPushRanks;
+constexpr int64_t kXchgFloats = lp::kXchgWords;      // values per half
 constexpr int64_t kXchgBytes = 2 * kXchgFloats * 8;  // two halves of 8-byte words
 struct PeerBufs {
   uint8_t* p[kMaxP2pRanks];
@@ -50,6 +50,7 @@ struct lp_pool {
   uint8_t* xbuf;   // this rank's exchange buffer: two halves of 8-byte words
   uint32_t* state; // [0] gathers finished, [1] CTAs finished in the current one
   PeerBufs peers;  // every rank's exchange buffer as mapped here
+  lp::PushCtx* push;  // device copy of peers/state for the GEMVs' own stores
 };
 
 namespace {
@@ -126,12 +127,21 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 // the device (state[0]) so CUDA-graph replays count too; all ranks make the
 // same gathers, so they agree on it.  Waits are bounded (error word on
 // timeout).
+// send == 0: this rank's words were already stored by the GEMV that made
+// its slice (the fused pooled form); only receive.  The kernel is launched
+// with programmatic stream serialization: a receiving-only grid touches
+// neither this rank's slice nor anything the GEMV before it writes, so it
+// starts polling while that GEMV still runs; a sending grid first waits for
+// the GEMV's slice.  A gather never releases its dependents early, so every
+// kernel after it in the stream starts after it has finished -- in
+// particular the next gather finds this gather's count final.
 __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t per_row,
                                                    int nranks, int rank, PeerBufs peers,
-                                                   uint32_t* state) {
+                                                   uint32_t* state, int send) {
   __shared__ uint32_t s_e;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t C = gridDim.x;
+  if (send) asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) s_e = reinterpret_cast<volatile uint32_t*>(state)[0] + 1u;
   __syncthreads();
   const uint32_t e = s_e;
@@ -142,7 +152,7 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
   const int64_t off = b * per_row, len = (en - b) * per_row;
   const int64_t chunk = (len + C - 1) / C;
   const int64_t lo = min(len, blockIdx.x * chunk), hi = min(len, lo + chunk);
-  for (int64_t i = lo + tid; i < hi; i += nthr) {
+  for (int64_t i = lo + tid; send && i < hi; i += nthr) {
     const uint64_t w = tag | __float_as_uint(y[off + i]);
     for (int q = 0; q < nranks; ++q)
       if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
@@ -165,6 +175,7 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
           ok = false;
           break;
         }
+        __nanosleep(64);  // leave the issue slots to the GEMV on this SM
         w = ld_word(mine + qo + i);
       }
       if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w));
@@ -182,18 +193,27 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
   }
 }
 
-int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st) {
+int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {
   const int64_t total = m * per_row;
   const int64_t per_rank = (total + p->nranks - 1) / p->nranks;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(16, (per_rank + 2047) / 2048)));
-  k_gather_p2p<<<grid, 256, 0, st>>>(y, m, per_row, p->nranks, p->rank, p->peers, p->state);
-  return lp::cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, m, per_row, p->nranks, p->rank,
+                                            p->peers, p->state, send));
 }
 
 // y[0, m*per_row) from every rank's slice of rows.
 int gather(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st) {
   if (p->nranks == 1 || m == 0) return LP_OK;
-  if (p->p2p && m * per_row <= kXchgFloats) return gather_p2p(p, y, m, per_row, st);
+  if (p->p2p && m * per_row <= kXchgFloats) return gather_p2p(p, y, m, per_row, st, 1);
   const NcclApi& api = nccl();
   int r = nccl_status(api.group_start());
   if (r) return r;
@@ -218,6 +238,7 @@ void setup_p2p(lp_pool* p) {
   p->p2p = p->p2p_ready = 0;
   p->xbuf = nullptr;
   p->state = nullptr;
+  p->push = nullptr;
   std::memset(&p->peers, 0, sizeof(p->peers));
   if (p->nranks < 2) return;
   const NcclApi& api = nccl();
@@ -282,6 +303,20 @@ void setup_p2p(lp_pool* p) {
   if (st) cudaStreamDestroy(st);
   delete[] all;
   cudaGetLastError();
+  if (all_ok) {
+    lp::PushCtx h;
+    std::memset(&h, 0, sizeof(h));
+    for (int q = 0; q < p->nranks; ++q) h.peers[q] = p->peers.p[q];
+    h.state = p->state;
+    h.nranks = p->nranks;
+    h.rank = p->rank;
+    if (cudaMalloc(&p->push, sizeof(h)) != cudaSuccess ||
+        cudaMemcpy(p->push, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) {
+      if (p->push) cudaFree(p->push);
+      p->push = nullptr;
+    }
+    cudaGetLastError();
+  }
   p->p2p = all_ok;
   p->p2p_ready = all_ok;
 }
@@ -292,6 +327,8 @@ void teardown_p2p(lp_pool* p) {
     if (p->peers.p[q] && q != p->rank) cudaIpcCloseMemHandle(p->peers.p[q]);
   if (p->xbuf) cudaFree(p->xbuf);
   if (p->state) cudaFree(p->state);
+  if (p->push) cudaFree(p->push);
+  p->push = nullptr;
   std::memset(&p->peers, 0, sizeof(p->peers));
   p->xbuf = nullptr;
   p->state = nullptr;
@@ -417,10 +454,23 @@ int lp_pool_gather_rows(lp_pool_t pool, float* y, int64_t m, int64_t per_row, lp
   int64_t b_, e_;                                                     \
   rows_of(m_, pool->nranks, pool->rank, &b_, &e_);                    \
   float* yl_ = y + b_ * (per_row);                                    \
-  const int64_t yl_len_ = (e_ - b_) * (per_row);
+  const int64_t yl_len_ = (e_ - b_) * (per_row);                      \
+  const bool fuse_ = pool->p2p && pool->push && m_ * (per_row) <= kXchgFloats; \
+  lp::g_push = fuse_ ? pool->push : nullptr;                          \
+  lp::g_push_off = b_ * (per_row);                                    \
+  lp::g_pushed = false;
 
+// The local GEMV stored its outputs into the other ranks already (fused
+// form): only receive.  Otherwise (a kernel without the push, or no
+// exchange) the whole gather.  The choice depends on shapes only, so every
+// rank makes the same one.
 #define LP_POOL_POST(per_row)                                         \
+  const bool pushed_ = lp::g_pushed;                                  \
+  lp::g_push = nullptr;                                               \
+  lp::g_pushed = false;                                               \
   if (r_) return r_;                                                  \
+  if (pushed_ && pool->nranks > 1)                                    \
+    return gather_p2p(pool, y, m_, per_row, S(stream), 0);            \
   return gather(pool, y, m_, per_row, S(stream));
 
 int lp_pool_dequant_gemv(lp_pool_t pool, const int8_t* wq, int64_t wq_len, const float* scales,
