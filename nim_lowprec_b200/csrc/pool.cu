@@ -167,18 +167,29 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
     const int64_t qo = qb * per_row, ql = (qe - qb) * per_row;
     const int64_t qc = (ql + C - 1) / C;
     const int64_t qlo = min(ql, blockIdx.x * qc), qhi = min(ql, qlo + qc);
-    for (int64_t i = qlo + tid; i < qhi && ok; i += nthr) {
-      uint64_t w = ld_word(mine + qo + i);
-      for (uint32_t n = 1; (w >> 32) != e; ++n) {
-        if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
-          lp::raise_error(LP_ERR_TIMEOUT);
-          ok = false;
-          break;
-        }
-        __nanosleep(64);  // leave the issue slots to the GEMV on this SM
-        w = ld_word(mine + qo + i);
+    // eight words in flight per thread, then wait on any that is not there yet
+    for (int64_t i0 = qlo + tid; i0 < qhi && ok; i0 += 8 * nthr) {
+      uint64_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t i = i0 + k * nthr;
+        w[k] = i < qhi ? ld_word(mine + qo + i) : 0;
       }
-      if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int64_t i = i0 + k * nthr;
+        if (i >= qhi || !ok) continue;
+        for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
+          if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
+            lp::raise_error(LP_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          __nanosleep(64);  // leave the issue slots to the GEMV on this SM
+          w[k] = ld_word(mine + qo + i);
+        }
+        if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w[k]));
+      }
     }
   }
   // the last CTA to finish publishes e as the finished gather count
@@ -196,7 +207,10 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
 int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {
   const int64_t total = m * per_row;
   const int64_t per_rank = (total + p->nranks - 1) / p->nranks;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(16, (per_rank + 2047) / 2048)));
+  // CTAs enough for ~1024 received words each, at most 64 (all resident at
+  // once on 148 SMs: a sending CTA waits only after its own stores)
+  const int64_t recv = total - per_rank;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(64, (recv + 1023) / 1024)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(256);
