@@ -220,6 +220,15 @@ int lph_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row, 
                           int64_t x_len, float *y, int64_t y_len);
 int lph_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
                           int64_t x_len, float *y, int64_t y_len);
+/* dequantGemvQ4_0 host form that allocates nothing: inputs and output are
+ * staged in one static 32 MiB device array instead of the per-thread
+ * workspace of lph_dequant_gemv_q4_0 (same arguments, same results).  No
+ * counterpart in the reference.  LP_ERR_UNSUPPORTED when the staged bytes
+ * (18 per block + 4 per x and y element, each rounded up to 256) exceed
+ * 32 MiB.  The array is shared process-wide: overlapping calls race and must
+ * be serialised by the caller. */
+int lph_dequant_gemv_q4_0_static(const void *w, int64_t w_len, int64_t blocks_per_row,
+                                 const float *x, int64_t x_len, float *y, int64_t y_len);
 int lph_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
                         int64_t w_scales_len, int64_t group_size, const int8_t *xq,
                         int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,

@@ -60,6 +60,7 @@ SIGNATURES = {
     "lph_dequant_gemv_f4": "pnpnnpnpn",
     "lph_dequant_gemv_q8_0": "pnnpnpn",
     "lph_dequant_gemv_q4_0": "pnnpnpn",
+    "lph_dequant_gemv_q4_0_static": "pnnpnpn",
     "lph_dequant_gemv_q8": "pnpnnpnpnpn",
     "lph_dequant_gemv_i4q8": "pnpnnpnpnpn",
     "lph_dequant_gemv_q8_0q8": "pnnpnpn",
