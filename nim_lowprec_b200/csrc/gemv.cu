@@ -22,6 +22,7 @@ namespace {
 
 constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
 constexpr int kMaxStages = 12;
+constexpr int kTileBytes = 64 * 1024;  // weights + scales of one tile, at most
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
@@ -103,7 +104,7 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     // Tile height: about two (row pair, group) units per consumer thread, in
     // whole row pairs, at most 32 rows and 40 KB of weights + scales.
     int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
-    rt = std::min(rt, std::max(2, (40 * 1024) / std::max(row_total, 1)));
+    rt = std::min(rt, std::max(2, (kTileBytes) / std::max(row_total, 1)));
     rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
     p.rt = std::max(1, rt & ~1);
   }

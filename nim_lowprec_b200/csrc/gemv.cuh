@@ -399,14 +399,20 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     Fmt::stage_x(xsm, p, ct, NC);
     asm volatile("bar.sync 1, %0;" ::"r"(NC) : "memory");
     Fmt f;
-    // Unit q = pair * gpr + g walks q = ct, ct + NC, ...; stepped without a
-    // division per unit.  When NC is a multiple of gpr (dg == 0) a thread
-    // keeps one group for the whole launch and takes two row pairs per step,
-    // two independent straight-line term2 calls the compiler interleaves.
+    // Unit q = pair * gpr + g.  When gpr <= NC a thread keeps one group for
+    // the whole launch (activations in registers) and takes two row pairs per
+    // step, two independent straight-line term2 calls the compiler
+    // interleaves; longer rows walk q = ct, ct + NC, ... without a division
+    // per unit.
     const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
     const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
+    // Whenever a row's groups fit the consumers (gpr <= NC) a thread keeps
+    // one group for the whole launch; when NC is not a multiple of gpr the
+    // threads past the last whole multiple have no unit.
+    const bool fixed = dpr >= 1;
+    const bool idle = fixed && ct >= dpr * p.gpr;
     if constexpr (!ColsOf<Fmt>::value)
-      if (dg == 0) f.prepare(p, xsm, g0);
+      if (fixed && !idle) f.prepare(p, xsm, g0);
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % p.stages;
       const int tb = t % p.ring;
@@ -430,9 +436,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
                       S + rb * p.gpr, g, T + ra * p.ncol * p.tstride,
                       ra + 1 < rows ? T + (ra + 1) * p.ncol * p.tstride : nullptr, p.tstride);
         }
-      } else if (dg == 0) {
+      } else if (fixed) {
         const int g = g0;
-        int pr = pr0;
+        int pr = idle ? npairs : pr0;
         for (; Fmt::kTwoPairs && pr + dpr < npairs; pr += 2 * dpr) {
           const int ra = 2 * pr, rc = 2 * (pr + dpr);
           const int rb = min(ra + 1, rows - 1), rd = min(rc + 1, rows - 1);
