@@ -645,6 +645,20 @@ def per_format(torch, L, barrier, steps=5000):
         out[key] = {"GB/s": round(v, 1), "frac": round(v / peak, 3), "us": round(ms / steps * 1e3, 2)}
     del copies
 
+    # the Q8_0 activation quantizer at the README's size (K = 16,777,216):
+    # 4 bytes in, 34/32 bytes out per element
+    n = 16_777_216
+    xb = [rnd(n, 5 + c) for c in range(3)]  # 3 x 67 MB inputs rotate: more than L2
+    qs = torch.empty(n, dtype=torch.int8, device="cuda")
+    d = torch.empty(n // 32, dtype=torch.float32, device="cuda")
+    ms, gr = graph_time(torch, lambda i: L.quantizeQ8_0Split(xb[i % 3], qs, d), 200, 3, barrier)
+    del gr
+    nb = 4 * n + n + 4 * (n // 32)
+    v = nb / (ms / 200 / 1e3) / 1e9
+    out["quantizeQ8_0_16M"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3),
+                               "us": round(ms / 200 * 1e3, 2)}
+    del xb, qs, d
+
     # config 3: dequantGemmQ8 4096^2 x B
     M = K = 4096
     w = rnd(M * K, 3, 0.02)
