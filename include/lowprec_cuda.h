@@ -205,6 +205,14 @@ int lp_dequantize_q8_0_batch(const void *blocks, int64_t blocks_len, float *dst,
 int lp_dequantize_q4_0_batch(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
                              lp_stream_t stream);
 
+/* dequantizeQ4_K / dequantizeQ6_K: 256-element k-quant super-blocks -> fp32
+ * (blocks_len in super-blocks of 144 / 210 bytes; dst_len = 256 * blocks_len).
+ * Replace ggml.nim:136-161 and :163-213. */
+int lp_dequantize_q4_k(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
+                       lp_stream_t stream);
+int lp_dequantize_q6_k(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
+                       lp_stream_t stream);
+
 /* ======================= host-pointer drop-in forms ==================== */
 /* Same arguments and meaning as the lp_* forms above, HOST pointers, no
  * stream; blocking. */

@@ -55,6 +55,8 @@ SIGNATURES = {
     "lp_quantize_f4_packed": "pnpnnpnp",
     "lp_dequantize_q8_0_batch": "pnpnp",
     "lp_dequantize_q4_0_batch": "pnpnp",
+    "lp_dequantize_q4_k": "pnpnp",
+    "lp_dequantize_q6_k": "pnpnp",
     "lph_dequant_gemv": "pnpnnpnpn",
     "lph_dequant_gemv_i4": "pnpnnpnpn",
     "lph_dequant_gemv_f4": "pnpnnpnpn",

@@ -412,6 +412,24 @@ int lp_dequantize_q4_0_batch(const void* blocks, int64_t blocks_len, float* dst,
                                       S(stream));
 }
 
+int lp_dequantize_q4_k(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
+                       lp_stream_t stream) {
+  LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 256);
+  if (bad(blocks, blocks_len) || bad(dst, dst_len)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_kquant(static_cast<const uint8_t*>(blocks), blocks_len, 0, dst,
+                                      S(stream));
+}
+
+int lp_dequantize_q6_k(const void* blocks, int64_t blocks_len, float* dst, int64_t dst_len,
+                       lp_stream_t stream) {
+  LP_REQUIRE(blocks_len >= 0 && dst_len == blocks_len * 256);
+  if (bad(blocks, blocks_len) || bad(dst, dst_len)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_kquant(static_cast<const uint8_t*>(blocks), blocks_len, 1, dst,
+                                      S(stream));
+}
+
 }  // extern "C"
 
 // ================================================== host-staging forms ==

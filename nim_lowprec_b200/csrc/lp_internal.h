@@ -72,6 +72,8 @@ int launch_quantize_packed(const float* x, int64_t n, const float* scales, int64
                            uint8_t* packed, cudaStream_t st);
 int launch_dequantize_blocks(const uint8_t* blocks, int64_t nblocks, int q4, float* dst,
                              cudaStream_t st);
+int launch_dequantize_kquant(const uint8_t* blocks, int64_t nblocks, int q6, float* dst,
+                             cudaStream_t st);
 
 // GEMM (gemm_tc.cu: tcgen05, LP_ERR_UNSUPPORTED outside its shapes; gemm.cu: CUDA cores)
 int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* xq,

@@ -294,7 +294,67 @@ __global__ void k_dequantize_blocks(const uint8_t* __restrict__ blocks, int64_t 
   }
 }
 
+// ggml.nim:136-161 (dequantizeQ4_K): one thread per output element of the
+// 256-element super-block (d, dmin, 12 bytes of 6-bit sub-scales/mins, 128
+// bytes of nibbles).  Element 64c + 32h + l is nibble h of qs byte 32c + l
+// with sub-block 2c + h: fl(fl(d * sc) * q) - fl(dmin * m).
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& m) {
+  if (j < 4) {
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+__global__ void k_dequantize_q4_k(const uint8_t* __restrict__ blocks, int64_t nblocks,
+                                  float* __restrict__ dst) {
+  const int64_t n = nblocks * 256;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (i >> 8) * 144;
+    const int e = static_cast<int>(i & 255), c = e >> 6, h = (e >> 5) & 1, l = e & 31;
+    const float d = h2f(static_cast<uint32_t>(blk[0]) | (static_cast<uint32_t>(blk[1]) << 8));
+    const float dmin = h2f(static_cast<uint32_t>(blk[2]) | (static_cast<uint32_t>(blk[3]) << 8));
+    int sc, m;
+    scale_min_k4(2 * c + h, blk + 4, sc, m);
+    const uint32_t b = blk[16 + 32 * c + l];
+    const int q = static_cast<int>(h ? (b >> 4) : (b & 15u));
+    dst[i] = __fsub_rn(__fmul_rn(__fmul_rn(d, i2f_rn(sc)), i2f_rn(q)), __fmul_rn(dmin, i2f_rn(m)));
+  }
+}
+
+// ggml.nim:163-213 (dequantizeQ6_K): ql[128] low four bits, qh[64] high two
+// bits, int8 scales[16], d (f16) last.  Element 128h + 32k + l takes
+// fl(fl(d * scale[8h + l/16 + 2k]) * (q - 32)).
+__global__ void k_dequantize_q6_k(const uint8_t* __restrict__ blocks, int64_t nblocks,
+                                  float* __restrict__ dst) {
+  const int64_t n = nblocks * 256;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (i >> 8) * 210;
+    const int e = static_cast<int>(i & 255), h = e >> 7, k = (e >> 5) & 3, l = e & 31;
+    const uint32_t lo = blk[64 * h + l + ((k & 1) ? 32 : 0)];
+    const uint32_t hi = blk[128 + 32 * h + l];
+    const int q = static_cast<int>(((k & 2) ? (lo >> 4) : (lo & 15u)) | (((hi >> (2 * k)) & 3u) << 4)) - 32;
+    const int scale = static_cast<int8_t>(blk[192 + 8 * h + (l >> 4) + 2 * k]);
+    const float d = h2f(static_cast<uint32_t>(blk[208]) | (static_cast<uint32_t>(blk[209]) << 8));
+    dst[i] = __fmul_rn(__fmul_rn(d, i2f_rn(scale)), i2f_rn(q));
+  }
+}
+
 }  // namespace
+
+int launch_dequantize_kquant(const uint8_t* blocks, int64_t nblocks, int q6, float* dst,
+                             cudaStream_t st) {
+  if (nblocks == 0) return LP_OK;
+  if (q6)
+    k_dequantize_q6_k<<<grid_for(nblocks * 256, kThreads), kThreads, 0, st>>>(blocks, nblocks, dst);
+  else
+    k_dequantize_q4_k<<<grid_for(nblocks * 256, kThreads), kThreads, 0, st>>>(blocks, nblocks, dst);
+  return cuda_status(cudaGetLastError());
+}
 
 int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* qs, float* d,
                          cudaStream_t st) {

@@ -20,7 +20,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import _native as N
-from .ggml import Q4_0_BYTES, Q8_0_BYTES
+from .ggml import Q4_0_BYTES, Q4_K_BYTES, Q6_K_BYTES, Q8_0_BYTES
 
 try:  # torch is optional for the host path
     import torch
@@ -330,3 +330,17 @@ def dequantizeQ4_0Batch(blocks, dst):
     N.check(N.lib().lp_dequantize_q4_0_batch(_ptr(blocks), _blocks(blocks, Q4_0_BYTES),
                                              _ptr(dst), _numel(dst), _stream()),
             "dequantize_q4_0_batch")
+
+
+def dequantizeQ4_K(blocks, dst):
+    """dequantizeQ4_K (ggml.nim:136-161): 256-element super-blocks, device."""
+    _dev_only("dequantizeQ4_K", blocks, dst)
+    N.check(N.lib().lp_dequantize_q4_k(_ptr(blocks), _blocks(blocks, Q4_K_BYTES), _ptr(dst),
+                                       _numel(dst), _stream()), "dequantize_q4_k")
+
+
+def dequantizeQ6_K(blocks, dst):
+    """dequantizeQ6_K (ggml.nim:163-213): 256-element super-blocks, device."""
+    _dev_only("dequantizeQ6_K", blocks, dst)
+    N.check(N.lib().lp_dequantize_q6_k(_ptr(blocks), _blocks(blocks, Q6_K_BYTES), _ptr(dst),
+                                       _numel(dst), _stream()), "dequantize_q6_k")

@@ -75,7 +75,8 @@ def lib():
         for nm in ("lpo_quantize_q8_0", "lpo_quantize_q4_0"):
             getattr(L, nm).argtypes = [vp, i64, vp]
         L.lpo_quantize_q8_0_split.argtypes = [vp, i64, vp, vp]
-        for nm in ("lpo_dequantize_q8_0", "lpo_dequantize_q4_0"):
+        for nm in ("lpo_dequantize_q8_0", "lpo_dequantize_q4_0", "lpo_dequantize_q4_k",
+                   "lpo_dequantize_q6_k"):
             getattr(L, nm).argtypes = [vp, i64, vp]
         L.lpo_pool_init.restype = vp
         L.lpo_pool_init.argtypes = [ctypes.c_int]
@@ -210,6 +211,26 @@ def dequantizeQ4_0(blocks) -> np.ndarray:
     blocks = _c(blocks, np.uint8).reshape(-1, Q4_0_BYTES)
     out = np.empty(blocks.shape[0] * QK, np.float32)
     lib().lpo_dequantize_q4_0(_p(blocks), blocks.shape[0], _p(out))
+    return out
+
+
+QK_K = 256
+Q4_K_BYTES, Q6_K_BYTES = 144, 210
+
+
+def dequantizeQ4_K(blocks) -> np.ndarray:
+    """dequantizeQ4_K (ggml.nim:136-161)."""
+    blocks = _c(blocks, np.uint8).reshape(-1, Q4_K_BYTES)
+    out = np.empty(blocks.shape[0] * QK_K, np.float32)
+    lib().lpo_dequantize_q4_k(_p(blocks), blocks.shape[0], _p(out))
+    return out
+
+
+def dequantizeQ6_K(blocks) -> np.ndarray:
+    """dequantizeQ6_K (ggml.nim:163-213)."""
+    blocks = _c(blocks, np.uint8).reshape(-1, Q6_K_BYTES)
+    out = np.empty(blocks.shape[0] * QK_K, np.float32)
+    lib().lpo_dequantize_q6_k(_p(blocks), blocks.shape[0], _p(out))
     return out
 
 

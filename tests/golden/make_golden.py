@@ -83,8 +83,7 @@ def main():
     gen.emit_ggml_schemes()
     gen.emit_mx_schemes()
     # keep only the fixtures this repository tests against
-    for name in ("ref_ggml_q4_k_bytes.bin", "ref_ggml_q4_k_dq.bin", "ref_ggml_q6_k_bytes.bin",
-                 "ref_ggml_q6_k_dq.bin", "ref_mx_f6e2m3_dq.bin", "ref_mx_f6e3m2_dq.bin"):
+    for name in ("ref_mx_f6e2m3_dq.bin", "ref_mx_f6e3m2_dq.bin"):
         p = os.path.join(HERE, name)
         if os.path.exists(p):
             os.remove(p)

@@ -74,6 +74,31 @@ def test_dequantize_blocks_match_gguf_golden(fmt):
     assert np.array_equal(to_host(out).view(np.uint32), want)
 
 
+@pytest.mark.parametrize("fmt", ["q4_k", "q6_k"])
+def test_dequantize_kquants_match_gguf_golden_and_oracle(fmt):
+    """The k-quant super-blocks: gguf-py's goldens, then 4099 random
+    super-blocks (every byte random except finite f16 d / dmin) vs the oracle."""
+    bb, fn, ofn = ((144, L.dequantizeQ4_K, O.dequantizeQ4_K) if fmt == "q4_k"
+                   else (210, L.dequantizeQ6_K, O.dequantizeQ6_K))
+    raw = np.fromfile(os.path.join(G, f"ref_ggml_{fmt}_bytes.bin"), np.uint8)
+    want = np.fromfile(os.path.join(G, f"ref_ggml_{fmt}_dq.bin"), np.uint32)
+    (rd,) = to_dev(raw)
+    out = torch.empty(want.size, dtype=torch.float32, device="cuda")
+    fn(rd, out)
+    assert np.array_equal(to_host(out).view(np.uint32), want)
+    rng = np.random.default_rng(17)
+    nb = 4099
+    blk = rng.integers(0, 256, size=(nb, bb), dtype=np.uint16).astype(np.uint8)
+    dpos = [0, 2] if fmt == "q4_k" else [208]
+    for p_ in dpos:
+        blk[:, p_:p_ + 2] = (rng.standard_normal(nb) * 0.1).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    raw = blk.reshape(-1)
+    (rd,) = to_dev(raw)
+    out = torch.empty(nb * 256, dtype=torch.float32, device="cuda")
+    fn(rd, out)
+    assert bits_equal(to_host(out), ofn(raw))
+
+
 def test_quantize_q8_0_random_and_edges_vs_oracle():
     rng = np.random.default_rng(3)
     x = (rng.standard_normal(32 * 4099) * 3).astype(F)

@@ -43,6 +43,18 @@ def test_ggml_dequant_of_gguf_bytes_bit_exact(fmt):
     assert np.array_equal(dq.view(np.uint32), want)
 
 
+@pytest.mark.parametrize("fmt", ["q4_k", "q6_k"])
+def test_kquant_dequant_of_gguf_bytes_bit_exact(fmt):
+    """dequantizeQ4_K / Q6_K (ggml.nim:136-213) against gguf-py's dequantization
+    of valid random super-blocks with finite d / dmin (gen_reference.py:175-195;
+    test_scheme_conformance.nim's k-quant checks)."""
+    raw = rd(f"ref_ggml_{fmt}_bytes.bin", np.uint8)
+    want = rd(f"ref_ggml_{fmt}_dq.bin", np.uint32)
+    dq = O.dequantizeQ4_K(raw) if fmt == "q4_k" else O.dequantizeQ6_K(raw)
+    assert dq.size == want.size == raw.size // (144 if fmt == "q4_k" else 210) * 256
+    assert np.array_equal(dq.view(np.uint32), want)
+
+
 def test_golden_input_has_the_edge_blocks():
     x = rd("ref_scheme_input.bin", np.float32)
     assert np.all(x[100:132] == 0)                       # the all-zero block
