@@ -511,12 +511,12 @@ def main():
     return 0
 
 
-PROFILE_KERNELS = "gemv_kernel|k_gemm_tc|k_quantize_q8_0"
+PROFILE_KERNELS = "gemv_kernel|k_gemm_tc|k_quantize_q8_0|k_dequantize_q4_k|k_dequantize_q6_k"
 
 
 def profile_kernels(torch, L):
     """One launch of every hot kernel, for an ncu capture of exactly these
-    launches (`-k regex:` PROFILE_KERNELS `-c 12`).  Inputs are prepared
+    launches (`-k regex:` PROFILE_KERNELS `-c 14`).  Inputs are prepared
     with other kernels (torch RNG, the weight encoders), and each workload is
     freed before the next, so a capture holds a few hundred MB at most."""
     g = torch.Generator(device="cuda")
@@ -588,6 +588,21 @@ def profile_kernels(torch, L):
     wl4 = Cfg4Workload(torch, L, 1, 0, layers=1)
     run("config4 layer 0: quantizeQ8_0 (4096), dequantGemvI4Q8 38400x4096, "
         "quantizeQ8_0 (11008), dequantGemvI4Q8 4096x11008", lambda: wl4.layer(None, 0))
+    del wl4
+    torch.cuda.empty_cache()
+
+    # k-quant super-block dequantization, 65536 super-blocks (16.7 M values)
+    nb = 65536
+    for bb, fn, name in ((144, L.dequantizeQ4_K, "Q4_K"), (210, L.dequantizeQ6_K, "Q6_K")):
+        g.manual_seed(7)
+        raw = torch.randint(0, 256, (nb, bb), dtype=torch.uint8, device="cuda", generator=g)
+        dpos = (0, 2) if bb == 144 else (208,)
+        for p_ in dpos:  # finite f16 scales
+            raw[:, p_:p_ + 2] = (torch.randn(nb, device="cuda", generator=g) * 0.1).half() \
+                .view(torch.uint8).view(nb, 2)
+        out = torch.empty(nb * 256, device="cuda")
+        run(f"dequantize{name} 65536 super-blocks", lambda: fn(raw.view(-1), out))
+        del raw, out
     return done
 
 
@@ -658,6 +673,25 @@ def per_format(torch, L, barrier, steps=5000):
     out["quantizeQ8_0_16M"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3),
                                "us": round(ms / 200 * 1e3, 2)}
     del xb, qs, d
+
+    # k-quant super-block dequantization (GGUF ingestion), 65536 super-blocks
+    nbk = 65536
+    outs = [torch.empty(nbk * 256, device="cuda") for _ in range(3)]  # 3 x 67 MB: more than L2
+    for bb, fn, name in ((144, L.dequantizeQ4_K, "Q4_K"), (210, L.dequantizeQ6_K, "Q6_K")):
+        g.manual_seed(7)
+        raw = torch.randint(0, 256, (nbk, bb), dtype=torch.uint8, device="cuda", generator=g)
+        for p_ in ((0, 2) if bb == 144 else (208,)):
+            raw[:, p_:p_ + 2] = (torch.randn(nbk, device="cuda", generator=g) * 0.1).half() \
+                .view(torch.uint8).view(nbk, 2)
+        flat = raw.view(-1)
+        ms, gr = graph_time(torch, lambda i: fn(flat, outs[i % 3]), 300, 3, barrier)
+        del gr
+        nbytes = nbk * bb + nbk * 256 * 4
+        v = nbytes / (ms / 300 / 1e3) / 1e9
+        out[f"dequantize{name}_65536"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3),
+                                          "us": round(ms / 300 * 1e3, 2)}
+        del raw, flat
+    del outs
 
     # config 3: dequantGemmQ8 4096^2 x B
     M = K = 4096

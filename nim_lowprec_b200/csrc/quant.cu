@@ -294,10 +294,22 @@ __global__ void k_dequantize_blocks(const uint8_t* __restrict__ blocks, int64_t 
   }
 }
 
-// ggml.nim:136-161 (dequantizeQ4_K): one thread per output element of the
-// 256-element super-block (d, dmin, 12 bytes of 6-bit sub-scales/mins, 128
-// bytes of nibbles).  Element 64c + 32h + l is nibble h of qs byte 32c + l
-// with sub-block 2c + h: fl(fl(d * sc) * q) - fl(dmin * m).
+// ggml.nim:136-161 (dequantizeQ4_K).  256-element super-block: d, dmin,
+// 12 bytes of 6-bit sub-scales/mins, 128 bytes of nibbles; element
+// 64c + 32h + l is nibble h of qs byte 32c + l with sub-block 2c + h:
+// fl(fl(d * sc) * q) - fl(dmin * m).  A thread takes 8 consecutive elements
+// (one sub-block, one 8-byte load of codes, two float4 stores).
+template <bool kVec>
+__device__ __forceinline__ void store8(float* o, const float (&v)[8]) {
+  if (kVec) {
+    reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = v[i];
+  }
+}
+
 __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& m) {
   if (j < 4) {
     sc = q[j] & 63;
@@ -308,39 +320,68 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, i
   }
 }
 
+// kVec: blocks and dst 16-byte aligned (vector code loads and stores)
+template <bool kVec>
 __global__ void k_dequantize_q4_k(const uint8_t* __restrict__ blocks, int64_t nblocks,
                                   float* __restrict__ dst) {
-  const int64_t n = nblocks * 256;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint8_t* blk = blocks + (i >> 8) * 144;
-    const int e = static_cast<int>(i & 255), c = e >> 6, h = (e >> 5) & 1, l = e & 31;
+  const int64_t n8 = nblocks * 32;  // 8-element pieces
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n8;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (t >> 5) * 144;
+    const int e0 = static_cast<int>(t & 31) * 8, c = e0 >> 6, h = (e0 >> 5) & 1, l0 = e0 & 31;
     const float d = h2f(static_cast<uint32_t>(blk[0]) | (static_cast<uint32_t>(blk[1]) << 8));
     const float dmin = h2f(static_cast<uint32_t>(blk[2]) | (static_cast<uint32_t>(blk[3]) << 8));
     int sc, m;
     scale_min_k4(2 * c + h, blk + 4, sc, m);
-    const uint32_t b = blk[16 + 32 * c + l];
-    const int q = static_cast<int>(h ? (b >> 4) : (b & 15u));
-    dst[i] = __fsub_rn(__fmul_rn(__fmul_rn(d, i2f_rn(sc)), i2f_rn(q)), __fmul_rn(dmin, i2f_rn(m)));
+    const float d1 = __fmul_rn(d, i2f_rn(sc)), mm = __fmul_rn(dmin, i2f_rn(m));
+    uint32_t wv[2];
+    if (kVec) {
+      const uint2 w = *reinterpret_cast<const uint2*>(blk + 16 + 32 * c + l0);  // 8-byte aligned
+      wv[0] = w.x;
+      wv[1] = w.y;
+    } else {
+      const uint8_t* qb = blk + 16 + 32 * c + l0;
+      wv[0] = qb[0] | (qb[1] << 8) | (qb[2] << 16) | (static_cast<uint32_t>(qb[3]) << 24);
+      wv[1] = qb[4] | (qb[5] << 8) | (qb[6] << 16) | (static_cast<uint32_t>(qb[7]) << 24);
+    }
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t b = (wv[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+      const int q = static_cast<int>(h ? (b >> 4) : (b & 15u));
+      v[i] = __fsub_rn(__fmul_rn(d1, i2f_rn(q)), mm);
+    }
+    store8<kVec>(dst + t * 8, v);
   }
 }
 
 // ggml.nim:163-213 (dequantizeQ6_K): ql[128] low four bits, qh[64] high two
 // bits, int8 scales[16], d (f16) last.  Element 128h + 32k + l takes
-// fl(fl(d * scale[8h + l/16 + 2k]) * (q - 32)).
+// fl(fl(d * scale[8h + l/16 + 2k]) * (q - 32)); a thread takes 8 consecutive
+// elements (one scale; the 210-byte blocks are only 2-byte aligned, so the
+// codes come as bytes).
+template <bool kVec>
 __global__ void k_dequantize_q6_k(const uint8_t* __restrict__ blocks, int64_t nblocks,
                                   float* __restrict__ dst) {
-  const int64_t n = nblocks * 256;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint8_t* blk = blocks + (i >> 8) * 210;
-    const int e = static_cast<int>(i & 255), h = e >> 7, k = (e >> 5) & 3, l = e & 31;
-    const uint32_t lo = blk[64 * h + l + ((k & 1) ? 32 : 0)];
-    const uint32_t hi = blk[128 + 32 * h + l];
-    const int q = static_cast<int>(((k & 2) ? (lo >> 4) : (lo & 15u)) | (((hi >> (2 * k)) & 3u) << 4)) - 32;
-    const int scale = static_cast<int8_t>(blk[192 + 8 * h + (l >> 4) + 2 * k]);
+  const int64_t n8 = nblocks * 32;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n8;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* blk = blocks + (t >> 5) * 210;
+    const int e0 = static_cast<int>(t & 31) * 8, h = e0 >> 7, k = (e0 >> 5) & 3, l0 = e0 & 31;
+    const uint8_t* ql = blk + 64 * h + l0 + ((k & 1) ? 32 : 0);
+    const uint8_t* qh = blk + 128 + 32 * h + l0;
+    const int scale = static_cast<int8_t>(blk[192 + 8 * h + (l0 >> 4) + 2 * k]);
     const float d = h2f(static_cast<uint32_t>(blk[208]) | (static_cast<uint32_t>(blk[209]) << 8));
-    dst[i] = __fmul_rn(__fmul_rn(d, i2f_rn(scale)), i2f_rn(q));
+    const float ds = __fmul_rn(d, i2f_rn(scale));
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = ql[i], hi = qh[i];
+      const int q =
+          static_cast<int>(((k & 2) ? (lo >> 4) : (lo & 15u)) | (((hi >> (2 * k)) & 3u) << 4)) - 32;
+      v[i] = __fmul_rn(ds, i2f_rn(q));
+    }
+    store8<kVec>(dst + t * 8, v);
   }
 }
 
@@ -349,10 +390,16 @@ __global__ void k_dequantize_q6_k(const uint8_t* __restrict__ blocks, int64_t nb
 int launch_dequantize_kquant(const uint8_t* blocks, int64_t nblocks, int q6, float* dst,
                              cudaStream_t st) {
   if (nblocks == 0) return LP_OK;
-  if (q6)
-    k_dequantize_q6_k<<<grid_for(nblocks * 256, kThreads), kThreads, 0, st>>>(blocks, nblocks, dst);
-  else
-    k_dequantize_q4_k<<<grid_for(nblocks * 256, kThreads), kThreads, 0, st>>>(blocks, nblocks, dst);
+  // vector stores (and Q4_K's 8-byte code loads) need 16-byte alignment
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(blocks)) & 15) == 0;
+  const int grid = grid_for(nblocks * 32, kThreads);
+  if (q6) {
+    if (vec) k_dequantize_q6_k<true><<<grid, kThreads, 0, st>>>(blocks, nblocks, dst);
+    else k_dequantize_q6_k<false><<<grid, kThreads, 0, st>>>(blocks, nblocks, dst);
+  } else {
+    if (vec) k_dequantize_q4_k<true><<<grid, kThreads, 0, st>>>(blocks, nblocks, dst);
+    else k_dequantize_q4_k<false><<<grid, kThreads, 0, st>>>(blocks, nblocks, dst);
+  }
   return cuda_status(cudaGetLastError());
 }
 

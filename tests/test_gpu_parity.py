@@ -96,7 +96,14 @@ def test_dequantize_kquants_match_gguf_golden_and_oracle(fmt):
     (rd,) = to_dev(raw)
     out = torch.empty(nb * 256, dtype=torch.float32, device="cuda")
     fn(rd, out)
-    assert bits_equal(to_host(out), ofn(raw))
+    want = ofn(raw)
+    assert bits_equal(to_host(out), want)
+    # unaligned blocks and output (element-wise loads and stores)
+    rd2 = torch.zeros(raw.size + 1, dtype=torch.uint8, device="cuda")
+    rd2[1:].copy_(rd)
+    out2 = torch.full((nb * 256 + 1,), float("nan"), dtype=torch.float32, device="cuda")
+    fn(rd2[1:], out2[1:])
+    assert bits_equal(to_host(out2[1:]), want)
 
 
 def test_quantize_q8_0_random_and_edges_vs_oracle():
