@@ -213,6 +213,17 @@ int lp_dequantize_q4_k(const void *blocks, int64_t blocks_len, float *dst, int64
 int lp_dequantize_q6_k(const void *blocks, int64_t blocks_len, float *dst, int64_t dst_len,
                        lp_stream_t stream);
 
+/* quantizeNVFP4 / dequantizeNVFP4: e2m1 codes (one byte per element) in
+ * 16-element blocks, one e4m3 decode scale per block, one fp32 global decode
+ * scale (written to *global_decode_scale, a device float; the reference
+ * returns it).  x_len a multiple of 16.  Replace nvfp4.nim:39-78 and :80-92. */
+int lp_quantize_nvfp4(const float *x, int64_t x_len, uint8_t *codes, int64_t codes_len,
+                      uint8_t *block_scales, int64_t scales_len, float *global_decode_scale,
+                      lp_stream_t stream);
+int lp_dequantize_nvfp4(const uint8_t *codes, int64_t codes_len, const uint8_t *block_scales,
+                        int64_t scales_len, float global_decode_scale, float *dst,
+                        int64_t dst_len, lp_stream_t stream);
+
 /* ======================= host-pointer drop-in forms ==================== */
 /* Same arguments and meaning as the lp_* forms above, HOST pointers, no
  * stream; blocking. */

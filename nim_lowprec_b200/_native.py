@@ -57,6 +57,8 @@ SIGNATURES = {
     "lp_dequantize_q4_0_batch": "pnpnp",
     "lp_dequantize_q4_k": "pnpnp",
     "lp_dequantize_q6_k": "pnpnp",
+    "lp_quantize_nvfp4": "pnpnpnpp",
+    "lp_dequantize_nvfp4": "pnpnfpnp",
     "lph_dequant_gemv": "pnpnnpnpn",
     "lph_dequant_gemv_i4": "pnpnnpnpn",
     "lph_dequant_gemv_f4": "pnpnnpnpn",

@@ -430,6 +430,28 @@ int lp_dequantize_q6_k(const void* blocks, int64_t blocks_len, float* dst, int64
                                       S(stream));
 }
 
+int lp_quantize_nvfp4(const float* x, int64_t x_len, uint8_t* codes, int64_t codes_len,
+                      uint8_t* block_scales, int64_t scales_len, float* global_decode_scale,
+                      lp_stream_t stream) {
+  LP_REQUIRE(x_len >= 0 && x_len % 16 == 0 && codes_len == x_len && scales_len == x_len / 16);
+  if (bad(x, x_len) || bad(codes, codes_len) || bad(block_scales, scales_len) ||
+      !global_decode_scale)
+    return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_quantize_nvfp4(x, x_len, codes, block_scales, global_decode_scale, S(stream));
+}
+
+int lp_dequantize_nvfp4(const uint8_t* codes, int64_t codes_len, const uint8_t* block_scales,
+                        int64_t scales_len, float global_decode_scale, float* dst,
+                        int64_t dst_len, lp_stream_t stream) {
+  LP_REQUIRE(dst_len == codes_len && scales_len * 16 == codes_len && codes_len >= 0);
+  if (bad(codes, codes_len) || bad(block_scales, scales_len) || bad(dst, dst_len))
+    return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_nvfp4(codes, block_scales, global_decode_scale, codes_len, dst,
+                                     S(stream));
+}
+
 }  // extern "C"
 
 // ================================================== host-staging forms ==

@@ -74,6 +74,10 @@ int launch_dequantize_blocks(const uint8_t* blocks, int64_t nblocks, int q4, flo
                              cudaStream_t st);
 int launch_dequantize_kquant(const uint8_t* blocks, int64_t nblocks, int q6, float* dst,
                              cudaStream_t st);
+int launch_quantize_nvfp4(const float* x, int64_t n, uint8_t* codes, uint8_t* scales,
+                          float* gds_out, cudaStream_t st);
+int launch_dequantize_nvfp4(const uint8_t* codes, const uint8_t* scales, float gds, int64_t n,
+                            float* dst, cudaStream_t st);
 
 // GEMM (gemm_tc.cu: tcgen05, LP_ERR_UNSUPPORTED outside its shapes; gemm.cu: CUDA cores)
 int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* xq,

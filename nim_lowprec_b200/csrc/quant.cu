@@ -247,6 +247,110 @@ __device__ __forceinline__ uint32_t to_e2m1(float f) {
   return code == 0 ? sign : (sign | static_cast<uint32_t>(code));
 }
 
+// ------------------------------------------------------------ NVFP4 ---
+// nvfp4.nim:39-92 (TransformerEngine NVFP4QuantizerRef, 1D path): e2m1
+// codes in 16-element blocks, one e4m3 decode scale per block, one fp32
+// global decode scale per tensor.
+
+// e4m3fn code of a finite a in [0, 448] (float8.nim:78-112): round to
+// nearest even on the e4m3 grid, subnormal step 2^-9.  (The scheme clamps
+// its block scales into this range before encoding.)
+__device__ __forceinline__ uint32_t e4m3_code(float a) {
+  if (a < 0.015625f) return static_cast<uint32_t>(__float2int_rn(a * 512.0f));  // exact scaling
+  const uint32_t bits = __float_as_uint(a);
+  int ex = static_cast<int>((bits >> 23) & 255u) - 127;
+  const uint32_t f = bits & 0x7FFFFFu;
+  uint32_t q = f >> 20;
+  const uint32_t rem = f & 0xFFFFFu;
+  if (rem > 0x80000u || (rem == 0x80000u && (q & 1u))) ++q;
+  if (q == 8u) {
+    q = 0;
+    ++ex;
+  }
+  const uint32_t code = (static_cast<uint32_t>(ex + 7) << 3) | q;
+  return code > 0x7Eu ? 0x7Eu : code;
+}
+__device__ __forceinline__ float e4m3_value(uint32_t u) {
+  const uint32_t ef = (u >> 3) & 15u, mf = u & 7u;
+  const float mag = ef ? __uint_as_float(((ef + 120u) << 23) | (mf << 20))
+                       : static_cast<float>(mf) * 0.001953125f;
+  return (u & 0x80u) ? -mag : mag;
+}
+
+// Pass 1: the tensor's largest |x| (NaN never wins, like the strict > scan)
+// as non-negative float bits, max-combined into *amax (zeroed beforehand).
+__global__ void k_nvfp4_amax(const float* __restrict__ x, int64_t n, uint32_t* amax) {
+  uint32_t m = 0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float a = fabsf(x[i]);
+    if (a == a) m = max(m, __float_as_uint(a));
+  }
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && m) atomicMax(amax, m);
+}
+
+__device__ __forceinline__ void nvfp4_globals(float gamax, float& ges, float& gds) {
+  const float F32MAX = 3.4028234663852886e38f;
+  ges = fminf(__fdiv_rn(2688.0f, gamax), F32MAX);  // 448 * 6
+  if (ges == 0.0f) ges = 1.0f;
+  gds = __fdiv_rn(1.0f, ges);
+}
+
+// Pass 2: one thread per 16-element block.
+__global__ void k_nvfp4_encode(const float* __restrict__ x, int64_t nblocks,
+                               const uint32_t* amax, uint8_t* __restrict__ codes,
+                               uint8_t* __restrict__ scales) {
+  const float F32MAX = 3.4028234663852886e38f;
+  float ges, gds;
+  nvfp4_globals(__uint_as_float(*amax), ges, gds);
+  const float mult = __fmul_rn(ges, __fdiv_rn(1.0f, 6.0f));
+  for (int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; b < nblocks;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = x[b * 16 + i];
+    float vmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = fabsf(v[i]);
+      if (a > vmax) vmax = a;
+    }
+    float ds = fminf(__fmul_rn(vmax, mult), F32MAX);
+    ds = fminf(fmaxf(ds, -448.0f), 448.0f);
+    const uint32_t ds8 = e4m3_code(ds);
+    scales[b] = static_cast<uint8_t>(ds8);
+    const float es = fminf(__fdiv_rn(1.0f, __fmul_rn(e4m3_value(ds8), gds)), F32MAX);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float sc = __fmul_rn(v[i], es);
+      if (sc < -6.0f) sc = -6.0f;  // NaN passes through, as in the reference's clamp
+      if (sc > 6.0f) sc = 6.0f;
+      codes[b * 16 + i] = static_cast<uint8_t>(sc == 0.0f ? 0u : to_e2m1(sc));
+    }
+  }
+}
+
+// Pass 3: the global decode scale replaces the amax in place.
+__global__ void k_nvfp4_finish(float* gds_out) {
+  float ges, gds;
+  nvfp4_globals(*gds_out, ges, gds);
+  *gds_out = gds;
+}
+
+// dequantizeNVFP4 (nvfp4.nim:80-92): (value(code) * value(scale)) * gds.
+__global__ void k_nvfp4_dequant(const uint8_t* __restrict__ codes,
+                                const uint8_t* __restrict__ scales, float gds, int64_t n,
+                                float* __restrict__ dst) {
+  const float lut[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t c = codes[i];
+    const float q = (c & 8u) ? -lut[c & 7u] : lut[c & 7u];
+    dst[i] = __fmul_rn(__fmul_rn(q, e4m3_value(scales[i >> 4])), gds);
+  }
+}
+
 // quantize[T] (quant.nim:48-60, value = x/scale + 0.0) + pack two per byte,
 // low nibble = even index (intx.nim:83-94, mxfloat.nim:138-149).
 __global__ void k_quantize_packed(const float* __restrict__ x, int64_t n,
@@ -386,6 +490,26 @@ __global__ void k_dequantize_q6_k(const uint8_t* __restrict__ blocks, int64_t nb
 }
 
 }  // namespace
+
+int launch_quantize_nvfp4(const float* x, int64_t n, uint8_t* codes, uint8_t* scales,
+                          float* gds_out, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(gds_out, 0, sizeof(float), st);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (n > 0) {
+    k_nvfp4_amax<<<grid_for(n, kThreads), kThreads, 0, st>>>(x, n, reinterpret_cast<uint32_t*>(gds_out));
+    k_nvfp4_encode<<<grid_for(n / 16, kThreads), kThreads, 0, st>>>(
+        x, n / 16, reinterpret_cast<const uint32_t*>(gds_out), codes, scales);
+  }
+  k_nvfp4_finish<<<1, 1, 0, st>>>(gds_out);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_dequantize_nvfp4(const uint8_t* codes, const uint8_t* scales, float gds, int64_t n,
+                            float* dst, cudaStream_t st) {
+  if (n == 0) return LP_OK;
+  k_nvfp4_dequant<<<grid_for(n, kThreads), kThreads, 0, st>>>(codes, scales, gds, n, dst);
+  return cuda_status(cudaGetLastError());
+}
 
 int launch_dequantize_kquant(const uint8_t* blocks, int64_t nblocks, int q6, float* dst,
                              cudaStream_t st) {

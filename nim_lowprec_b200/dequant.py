@@ -344,3 +344,23 @@ def dequantizeQ6_K(blocks, dst):
     _dev_only("dequantizeQ6_K", blocks, dst)
     N.check(N.lib().lp_dequantize_q6_k(_ptr(blocks), _blocks(blocks, Q6_K_BYTES), _ptr(dst),
                                        _numel(dst), _stream()), "dequantize_q6_k")
+
+
+
+def quantizeNVFP4(x, codes, blockScales, globalDecodeScale):
+    """quantizeNVFP4 (nvfp4.nim:39-78), device: e2m1 codes (uint8 per element),
+    e4m3 block scales (uint8 per 16 elements); the global decode scale the
+    reference returns is written to the 1-element device tensor
+    `globalDecodeScale`."""
+    _dev_only("quantizeNVFP4", x, codes, blockScales, globalDecodeScale)
+    N.check(N.lib().lp_quantize_nvfp4(_ptr(x), _numel(x), _ptr(codes), _numel(codes),
+                                      _ptr(blockScales), _numel(blockScales),
+                                      _ptr(globalDecodeScale), _stream()), "quantize_nvfp4")
+
+
+def dequantizeNVFP4(codes, blockScales, globalDecodeScale, dst):
+    """dequantizeNVFP4 (nvfp4.nim:80-92), device; globalDecodeScale is a float."""
+    _dev_only("dequantizeNVFP4", codes, blockScales, dst)
+    N.check(N.lib().lp_dequantize_nvfp4(_ptr(codes), _numel(codes), _ptr(blockScales),
+                                        _numel(blockScales), float(globalDecodeScale),
+                                        _ptr(dst), _numel(dst), _stream()), "dequantize_nvfp4")

@@ -78,6 +78,13 @@ def lib():
         for nm in ("lpo_dequantize_q8_0", "lpo_dequantize_q4_0", "lpo_dequantize_q4_k",
                    "lpo_dequantize_q6_k"):
             getattr(L, nm).argtypes = [vp, i64, vp]
+        L.lpo_to_f8e4m3.restype = ctypes.c_uint8
+        L.lpo_to_f8e4m3.argtypes = [f32]
+        L.lpo_f8e4m3_to_f32.restype = f32
+        L.lpo_f8e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        L.lpo_quantize_nvfp4.restype = f32
+        L.lpo_quantize_nvfp4.argtypes = [vp, i64, vp, vp]
+        L.lpo_dequantize_nvfp4.argtypes = [vp, vp, f32, i64, vp]
         L.lpo_pool_init.restype = vp
         L.lpo_pool_init.argtypes = [ctypes.c_int]
         L.lpo_pool_shutdown.argtypes = [vp]
@@ -231,6 +238,29 @@ def dequantizeQ6_K(blocks) -> np.ndarray:
     blocks = _c(blocks, np.uint8).reshape(-1, Q6_K_BYTES)
     out = np.empty(blocks.shape[0] * QK_K, np.float32)
     lib().lpo_dequantize_q6_k(_p(blocks), blocks.shape[0], _p(out))
+    return out
+
+
+NVFP4_BLOCK = 16
+
+
+def quantizeNVFP4(x):
+    """quantizeNVFP4 (nvfp4.nim:39-78): (codes u8 per element, e4m3 block
+    scales u8 per 16 elements, global decode scale)."""
+    x = _c(x, np.float32).reshape(-1)
+    assert x.size % NVFP4_BLOCK == 0
+    codes = np.empty(x.size, np.uint8)
+    scales = np.empty(x.size // NVFP4_BLOCK, np.uint8)
+    gds = lib().lpo_quantize_nvfp4(_p(x), x.size, _p(codes), _p(scales))
+    return codes, scales, np.float32(gds)
+
+
+def dequantizeNVFP4(codes, scales, gds) -> np.ndarray:
+    """dequantizeNVFP4 (nvfp4.nim:80-92)."""
+    codes = _c(codes, np.uint8).reshape(-1)
+    scales = _c(scales, np.uint8).reshape(-1)
+    out = np.empty(codes.size, np.float32)
+    lib().lpo_dequantize_nvfp4(_p(codes), _p(scales), float(gds), codes.size, _p(out))
     return out
 
 

@@ -82,6 +82,7 @@ def main():
     gen = load_reference_generator(ref_root)
     gen.emit_ggml_schemes()
     gen.emit_mx_schemes()
+    gen.emit_nvfp4()
     # keep only the fixtures this repository tests against
     for name in ("ref_mx_f6e2m3_dq.bin", "ref_mx_f6e3m2_dq.bin"):
         p = os.path.join(HERE, name)

@@ -106,6 +106,47 @@ def test_dequantize_kquants_match_gguf_golden_and_oracle(fmt):
     assert bits_equal(to_host(out2[1:]), want)
 
 
+def _nvfp4_on_device(x):
+    (xd,) = to_dev(x)
+    codes = torch.empty(x.size, dtype=torch.uint8, device="cuda")
+    scales = torch.empty(x.size // 16, dtype=torch.uint8, device="cuda")
+    gds = torch.empty(1, dtype=torch.float32, device="cuda")
+    L.quantizeNVFP4(xd, codes, scales, gds)
+    return codes, scales, gds
+
+
+def test_nvfp4_matches_the_te_golden_and_oracle():
+    """quantizeNVFP4 / dequantizeNVFP4 (nvfp4.nim:39-92) on the device: the TE
+    golden, then random tensors with zero, huge-range, inf and NaN entries vs
+    the oracle."""
+    x = np.fromfile(os.path.join(G, "ref_nvfp4_input.bin"), np.float32)
+    raw = np.fromfile(os.path.join(G, "ref_nvfp4_out.bin"), np.uint8)
+    nb = x.size // 16
+    codes, scales, gds = _nvfp4_on_device(x)
+    assert to_host(gds)[0] == raw[:4].view("<f4")[0]
+    assert np.array_equal(to_host(scales), raw[4:4 + nb])
+    assert np.array_equal(to_host(codes), raw[4 + nb:])
+    rng = np.random.default_rng(23)
+    for case in range(4):
+        x = (rng.standard_normal(16 * 4099) * 3).astype(F)
+        x = (x.reshape(-1, 16) * (F(2.0) ** rng.integers(-30, 30, size=(4099, 1)).astype(F))).reshape(-1)
+        if case >= 1:
+            x[16 * 3:16 * 4] = 0.0
+            x[100] = -0.0
+        if case >= 2:
+            x[5000] = np.nan
+        if case == 3:
+            x[777] = np.inf
+        codes, scales, gds = _nvfp4_on_device(x)
+        oc, os_, og = O.quantizeNVFP4(x)
+        assert bits_equal(to_host(gds), np.array([og], F))
+        assert np.array_equal(to_host(scales), os_)
+        assert np.array_equal(to_host(codes), oc)
+        out = torch.empty(x.size, dtype=torch.float32, device="cuda")
+        L.dequantizeNVFP4(codes, scales, float(og), out)
+        assert bits_equal(to_host(out), O.dequantizeNVFP4(oc, os_, og))
+
+
 def test_quantize_q8_0_random_and_edges_vs_oracle():
     rng = np.random.default_rng(3)
     x = (rng.standard_normal(32 * 4099) * 3).astype(F)

@@ -55,6 +55,40 @@ def test_kquant_dequant_of_gguf_bytes_bit_exact(fmt):
     assert np.array_equal(dq.view(np.uint32), want)
 
 
+def test_nvfp4_scheme_matches_the_te_golden():
+    """quantizeNVFP4 (nvfp4.nim:39-78) against the numpy transcription of
+    TransformerEngine's NVFP4QuantizerRef (gen_reference.py:237-294): global
+    decode scale, e4m3 block scales and e2m1 codes, bit for bit."""
+    x = rd("ref_nvfp4_input.bin", np.float32)
+    raw = rd("ref_nvfp4_out.bin", np.uint8)
+    nb = x.size // 16
+    codes, scales, gds = O.quantizeNVFP4(x)
+    assert gds == raw[:4].view("<f4")[0]
+    assert np.array_equal(scales, raw[4:4 + nb])
+    assert np.array_equal(codes, raw[4 + nb:])
+    dq = O.dequantizeNVFP4(codes, scales, gds)
+    lut = np.array([O.lib().lpo_f4e2m1_to_f32(c) for c in range(16)], np.float32)
+    e4 = np.array([O.lib().lpo_f8e4m3_to_f32(c) for c in range(256)], np.float32)
+    want = (lut[codes] * np.repeat(e4[scales], 16)).astype(np.float32) * np.float32(gds)
+    assert np.array_equal(dq.view(np.uint32), want.astype(np.float32).view(np.uint32))
+
+
+def test_e4m3_codec_round_trip_and_rounding():
+    """e4m3fn (float8.nim:28-112): every finite code decodes and re-encodes to
+    itself; midpoints between neighbours round to the even code."""
+    for c in range(256):
+        if (c & 0x7F) == 0x7F:
+            continue  # NaN
+        v = O.lib().lpo_f8e4m3_to_f32(c)
+        assert O.lib().lpo_to_f8e4m3(v) == (c if v != 0 or c == 0 else c)
+    for c in range(0, 0x7E):
+        a, b = O.lib().lpo_f8e4m3_to_f32(c), O.lib().lpo_f8e4m3_to_f32(c + 1)
+        mid = np.float32((np.float64(a) + np.float64(b)) / 2)
+        if np.float64(mid) == (np.float64(a) + np.float64(b)) / 2:
+            assert O.lib().lpo_to_f8e4m3(float(mid)) == (c if c % 2 == 0 else c + 1)
+    assert O.lib().lpo_to_f8e4m3(460.0) == 0x7E and O.lib().lpo_to_f8e4m3(465.0) == 0x7F
+
+
 def test_golden_input_has_the_edge_blocks():
     x = rd("ref_scheme_input.bin", np.float32)
     assert np.all(x[100:132] == 0)                       # the all-zero block
