@@ -14,8 +14,9 @@ graph replays bracketed by CUDA events on the launching stream.
 
 N > 1 (torchrun, one process per GPU): weak scaling of the LpPool form -- each
 rank owns 11008 contiguous rows of an (N*11008) x 4096 matrix, runs the same
-GEMV on them and all-gathers the output vector over NCCL every step, so every
-rank ends the step holding the whole y.
+GEMV on them and gathers the output vector every step (the pool's NVLink
+transport: peer stores from the GEMV itself), so every rank ends the step
+holding the whole y.
 
 `--impl reference` times the reference's algorithm on the host cores (the C
 restatement in oracle/, pooled over every core like LpPool) on the same
@@ -511,12 +512,13 @@ def main():
     return 0
 
 
-PROFILE_KERNELS = "gemv_kernel|k_gemm_tc|k_quantize_q8_0|k_dequantize_q4_k|k_dequantize_q6_k"
+PROFILE_KERNELS = ("gemv_kernel|k_gemm_tc|k_quantize_q8_0|k_dequantize_q4_k|k_dequantize_q6_k"
+                   "|k_dequantize_batch")
 
 
 def profile_kernels(torch, L):
     """One launch of every hot kernel, for an ncu capture of exactly these
-    launches (`-k regex:` PROFILE_KERNELS `-c 14`).  Inputs are prepared
+    launches (`-k regex:` PROFILE_KERNELS `-c 15`).  Inputs are prepared
     with other kernels (torch RNG, the weight encoders), and each workload is
     freed before the next, so a capture holds a few hundred MB at most."""
     g = torch.Generator(device="cuda")
@@ -603,6 +605,12 @@ def profile_kernels(torch, L):
         out = torch.empty(nb * 256, device="cuda")
         run(f"dequantize{name} 65536 super-blocks", lambda: fn(raw.view(-1), out))
         del raw, out
+
+    # dequantizeBatch, int8 per group of 128, 16,000,000 values
+    q, sc = i8(16_000_000, 8), scales(125_000, 8)
+    out = torch.empty(16_000_000, device="cuda")
+    run("dequantizeBatch 16000000 group 128", lambda: L.dequantizeBatch(q, sc, 128, out))
+    del q, sc, out
     return done
 
 
@@ -692,6 +700,22 @@ def per_format(torch, L, barrier, steps=5000):
                                           "us": round(ms / 300 * 1e3, 2)}
         del raw, flat
     del outs
+
+    # dequantizeBatch, int8 per group of 128 over 16,000,000 values (the shape of
+    # the reference's elementwise-dequant benchmark, bench_dequant.nim:13-14)
+    n, gsz = 16_000_000, 128
+    qb = [torch.randint(-128, 128, (n,), dtype=torch.int8, device="cuda", generator=g)
+          for _ in range(3)]
+    scb = torch.rand(n // gsz, device="cuda", generator=g) * 0.1
+    dst = [torch.empty(n, device="cuda") for _ in range(3)]  # 3 x 80 MB: more than L2
+    ms, gr = graph_time(torch, lambda i: L.dequantizeBatch(qb[i % 3], scb, gsz, dst[i % 3]),
+                        300, 3, barrier)
+    del gr
+    nbytes = n + 4 * n + 4 * (n // gsz)
+    v = nbytes / (ms / 300 / 1e3) / 1e9
+    out["dequantizeBatch_16M_g128"] = {"GB/s": round(v, 1), "frac": round(v / peak, 3),
+                                       "us": round(ms / 300 * 1e3, 2)}
+    del qb, scb, dst
 
     # config 3: dequantGemmQ8 4096^2 x B
     M = K = 4096

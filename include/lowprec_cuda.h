@@ -174,6 +174,16 @@ int lp_quantize_q8_0_split(const float *src, int64_t src_len, int8_t *qs, int64_
 int lp_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
                       int64_t group_size, int8_t *dst, int64_t dst_len, lp_stream_t stream);
 
+/* dequantizeBatch: dst = (f32(q) - zero_points[g]) * scales[g], g = i div
+ * group_size (group_size <= 0: per tensor), for int8-backed I8 and I4 values
+ * stored one per byte.  zero_points_len = 0 is the symmetric case (QParams
+ * with an empty zeroPoint); otherwise it covers every group.  Replaces
+ * simd/dequant.nim:159-206 (proc dequantizeBatch*, both instantiations) and
+ * its scalar fall-through quant.nim:62-74 (proc dequantize*). */
+int lp_dequantize_batch(const int8_t *q, int64_t q_len, const float *scales, int64_t scales_len,
+                        const float *zero_points, int64_t zero_points_len, int64_t group_size,
+                        float *dst, int64_t dst_len, lp_stream_t stream);
+
 /* calibrateSymmetric: scale = absmax/qmax per group (1.0 for a zero group,
  * ragged last group, group_size <= 0 = per tensor).
  * Replaces quant.nim:95-110 (proc calibrateSymmetric*). */
@@ -272,6 +282,9 @@ int lph_quantize_q8_0_batch(const float *src, int64_t src_len, void *blocks, int
 int lph_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len);
 int lph_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
                        int64_t group_size, int8_t *dst, int64_t dst_len);
+int lph_dequantize_batch(const int8_t *q, int64_t q_len, const float *scales, int64_t scales_len,
+                         const float *zero_points, int64_t zero_points_len, int64_t group_size,
+                         float *dst, int64_t dst_len);
 
 /* ======================= LpPool: row-sharded forms across GPUs ======== *
  * One process (rank) per GPU of a box.  Rank r owns the rows
@@ -296,8 +309,10 @@ int lp_pool_destroy(lp_pool_t pool);
 int lp_pool_size(lp_pool_t pool, int *nranks, int *rank);
 /* The gather's transport (no counterpart in the reference).  By default a pool
  * whose ranks each have their own GPU maps every rank's exchange buffer over
- * NVLink (CUDA IPC, set up by lp_pool_init) and gathers with one kernel of
- * peer stores and bounded completion counters; enable = 0 selects the NCCL
+ * NVLink (CUDA IPC, set up by lp_pool_init) and gathers with 8-byte peer
+ * stores that carry the gather's sequence number beside each float (pooled
+ * GEMVs store their rows from the GEMV itself), read back with bounded
+ * polls; enable = 0 selects the NCCL
  * group instead.  Every rank must make the same choice before its next gather.
  * LP_ERR_UNSUPPORTED: the exchange could not be mapped on every rank. */
 int lp_pool_set_p2p(lp_pool_t pool, int enable);

@@ -10,8 +10,9 @@ from . import _native
 from .dequant import (  # noqa: F401
     calibrateMX, calibrateSymmetric, dequantGemmI4Q8, dequantGemmQ8, dequantGemv,
     dequantGemvF4, dequantGemvI4, dequantGemvI4Q8, dequantGemvQ4_0, dequantGemvQ4_0Q8,
-    dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantizeQ4_0Batch, dequantizeQ4_K,
-    dequantizeQ6_K, dequantizeQ8_0Batch, dequantizeNVFP4, quantizeBatch, quantizeNVFP4, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0,
+    dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantizeBatch, dequantizeQ4_0Batch,
+    dequantizeQ4_K, dequantizeQ6_K, dequantizeQ8_0Batch, dequantizeNVFP4, quantizeBatch,
+    quantizeNVFP4, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0,
     quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split, fp32_mode,
     fp32Mode, setFp32Mode)
 from .ggml import QK, QK_K, BlockQ4_0, BlockQ4_K, BlockQ6_K, BlockQ8_0  # noqa: F401

@@ -49,6 +49,7 @@ SIGNATURES = {
     "lp_quantize_q4_0_batch": "pnpnp",
     "lp_quantize_q8_0_split": "pnpnpnp",
     "lp_quantize_batch": "pnpnnpnp",
+    "lp_dequantize_batch": "pnpnpnnpnp",
     "lp_calibrate_symmetric": "pnnfpnp",
     "lp_calibrate_mx": "pnnipnp",
     "lp_quantize_i4_packed": "pnpnnpnp",
@@ -74,6 +75,7 @@ SIGNATURES = {
     "lph_quantize_q8_0_batch": "pnpn",
     "lph_quantize_q4_0_batch": "pnpn",
     "lph_quantize_batch": "pnpnnpn",
+    "lph_dequantize_batch": "pnpnpnnpn",
     "lp_set_fp32_mode": "i",
     "lp_get_fp32_mode": "",
     "lp_pool_rows": "niipp",

@@ -353,6 +353,20 @@ int lp_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_
                                    S(stream));
 }
 
+int lp_dequantize_batch(const int8_t* q, int64_t q_len, const float* scales, int64_t scales_len,
+                        const float* zero_points, int64_t zero_points_len, int64_t group_size,
+                        float* dst, int64_t dst_len, lp_stream_t stream) {
+  const int64_t groups = q_len ? num_groups(q_len, group_size) : 0;
+  LP_REQUIRE(q_len >= 0 && q_len == dst_len && scales_len >= groups);
+  LP_REQUIRE(zero_points_len == 0 || zero_points_len >= groups);
+  if (bad(q, q_len) || bad(scales, scales_len) || bad(dst, dst_len) ||
+      bad(zero_points, zero_points_len))
+    return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_dequantize_batch(q, q_len, scales, zero_points_len ? zero_points : nullptr,
+                                     group_size > 0 ? group_size : 0, dst, S(stream));
+}
+
 int lp_calibrate_symmetric(const float* x, int64_t x_len, int64_t group_size, float qmax,
                            float* scales, int64_t scales_len, lp_stream_t stream) {
   LP_REQUIRE(x_len >= 0);
@@ -661,6 +675,22 @@ int lph_quantize_batch(const float* x, int64_t x_len, const float* scales, int64
   st = lp_quantize_batch(static_cast<const float*>(sx.dev), x_len,
                          static_cast<const float*>(ss.dev), scales_len, group_size,
                          static_cast<int8_t*>(sd.dev), dst_len, t_stage.stream);
+  return stage_out(dst, sd, st);
+}
+
+int lph_dequantize_batch(const int8_t* q, int64_t q_len, const float* scales, int64_t scales_len,
+                         const float* zero_points, int64_t zero_points_len, int64_t group_size,
+                         float* dst, int64_t dst_len) {
+  Seg sq{q, nb<int8_t>(q_len)}, ss{scales, nb<float>(scales_len)},
+      sz{zero_points, nb<float>(zero_points_len)}, sd{nullptr, nb<float>(dst_len)};
+  LPH_PRECHECK(lp_dequantize_batch(q, q_len, scales, scales_len, zero_points, zero_points_len,
+                                   group_size, dst, dst_len, nullptr));
+  int st = stage_in({&sq, &ss, &sz, &sd});
+  if (st != LP_OK) return st;
+  st = lp_dequantize_batch(static_cast<const int8_t*>(sq.dev), q_len,
+                           static_cast<const float*>(ss.dev), scales_len,
+                           static_cast<const float*>(sz.dev), zero_points_len, group_size,
+                           static_cast<float*>(sd.dev), dst_len, t_stage.stream);
   return stage_out(dst, sd, st);
 }
 

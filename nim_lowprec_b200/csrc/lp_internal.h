@@ -66,6 +66,8 @@ int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* q
 int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStream_t st);
 int launch_quantize_batch(const float* x, int64_t n, const float* scales, int64_t gs,
                           int8_t* dst, cudaStream_t st);
+int launch_dequantize_batch(const int8_t* q, int64_t n, const float* scales, const float* zp,
+                            int64_t gs, float* dst, cudaStream_t st);
 int launch_calibrate(const float* x, int64_t n, int64_t gs, float qmax, int mx_emax, int mx,
                      float* scales, int64_t nscales, cudaStream_t st);
 int launch_quantize_packed(const float* x, int64_t n, const float* scales, int64_t gs, int f4,

@@ -489,6 +489,57 @@ __global__ void k_dequantize_q6_k(const uint8_t* __restrict__ blocks, int64_t nb
   }
 }
 
+// dequantizeBatch (simd/dequant.nim:159-206; scalar quant.nim:62-74):
+// dst = fl(fl(f32(q) - zp[g]) * scale[g]), g = i div gs, zp = 0 when absent
+// (f32(q) - 0 == f32(q), so the symmetric form is the same arithmetic).  A
+// thread takes 16 consecutive values: one 16-byte load, four 16-byte stores
+// when kVec (q and dst 16-byte aligned), and walks the group boundaries
+// inside its run.  gs > 0 here (per tensor: gs = n).
+template <bool kVec>
+__global__ void k_dequantize_batch(const int8_t* __restrict__ q, int64_t n,
+                                   const float* __restrict__ scales,
+                                   const float* __restrict__ zp, int64_t gs,
+                                   float* __restrict__ dst) {
+  const int64_t n16 = (n + 15) / 16;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n16;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i0 = t * 16;
+    const int cnt = n - i0 < 16 ? static_cast<int>(n - i0) : 16;
+    int8_t v[16];
+    if (kVec && cnt == 16) {
+      const int4 w = *reinterpret_cast<const int4*>(q + i0);
+      memcpy(v, &w, 16);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = j < cnt ? q[i0 + j] : 0;
+    }
+    int64_t g = i0 / gs, r = i0 - g * gs;
+    float sc = scales[g], z = zp ? zp[g] : 0.0f;
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (r == gs && i0 + j < n) {
+        ++g;
+        r = 0;
+        sc = scales[g];
+        z = zp ? zp[g] : 0.0f;
+      }
+      o[j] = __fmul_rn(__fsub_rn(static_cast<float>(v[j]), z), sc);
+      ++r;
+    }
+    float* out = dst + i0;
+    if (kVec && cnt == 16) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(out + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < cnt) out[j] = o[j];
+    }
+  }
+}
+
 }  // namespace
 
 int launch_quantize_nvfp4(const float* x, int64_t n, uint8_t* codes, uint8_t* scales,
@@ -501,6 +552,18 @@ int launch_quantize_nvfp4(const float* x, int64_t n, uint8_t* codes, uint8_t* sc
         x, n / 16, reinterpret_cast<const uint32_t*>(gds_out), codes, scales);
   }
   k_nvfp4_finish<<<1, 1, 0, st>>>(gds_out);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_dequantize_batch(const int8_t* q, int64_t n, const float* scales, const float* zp,
+                            int64_t gs, float* dst, cudaStream_t st) {
+  if (n == 0) return LP_OK;
+  if (gs <= 0 || gs > n) gs = n;
+  const int grid = grid_for((n + 15) / 16, kThreads);
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0)
+    k_dequantize_batch<true><<<grid, kThreads, 0, st>>>(q, n, scales, zp, gs, dst);
+  else
+    k_dequantize_batch<false><<<grid, kThreads, 0, st>>>(q, n, scales, zp, gs, dst);
   return cuda_status(cudaGetLastError());
 }
 

@@ -272,6 +272,20 @@ def quantizeBatch(x, scales, groupSize, dst):
           int(groupSize), _ptr(dst), _numel(dst))
 
 
+def dequantizeBatch(q, scales, groupSize, dst, zeroPoint=None):
+    """simd/dequant.nim:159-206 (and its scalar fall-through quant.nim:62-74):
+    dst = (f32(q) - zeroPoint[g]) * scale[g] for I8 or I4 values held one per
+    int8; ``zeroPoint`` None (or empty) is the symmetric case, groupSize <= 0
+    per tensor."""
+    mode = _mode(q, scales, dst, zeroPoint)
+    _check_dtype(q, np.int8, "q"); _check_dtype(scales, np.float32, "scales")
+    _check_dtype(dst, np.float32, "dst")
+    if zeroPoint is not None:
+        _check_dtype(zeroPoint, np.float32, "zeroPoint")
+    _call(mode, "dequantize_batch", _ptr(q), _numel(q), _ptr(scales), _numel(scales),
+          _ptr(zeroPoint), _numel(zeroPoint), int(groupSize), _ptr(dst), _numel(dst))
+
+
 def _dev_only(name, *arrs):
     if _mode(*arrs) != "dev":
         raise TypeError(f"{name} takes torch CUDA tensors")

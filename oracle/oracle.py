@@ -70,6 +70,7 @@ def lib():
         L.lpo_calibrate_mx.argtypes = [vp, i64, i64, ctypes.c_int, vp]
         L.lpo_quantize.argtypes = [vp, i64, vp, i64, ctypes.c_int, vp]
         L.lpo_quantize_batch.argtypes = [vp, i64, vp, i64, vp]
+        L.lpo_dequantize_batch.argtypes = [vp, i64, vp, vp, i64, vp]
         L.lpo_pack_int4.argtypes = [vp, i64, vp]
         L.lpo_pack_f4.argtypes = [vp, i64, vp]
         for nm in ("lpo_quantize_q8_0", "lpo_quantize_q4_0"):
@@ -163,6 +164,19 @@ def quantizeBatch(x, scales, groupSize: int) -> np.ndarray:
     scales = _c(scales, np.float32)
     out = np.empty(x.size, np.int8)
     lib().lpo_quantize_batch(_p(x), x.size, _p(scales), groupSize, _p(out))
+    return out
+
+
+def dequantizeBatch(q, scales, groupSize: int, zeroPoint=None) -> np.ndarray:
+    """(f32(q) - zeroPoint[g]) * scale[g] for int8-backed I8 / I4 values
+    (simd/dequant.nim:159-206 = quant.nim:62-74); ``groupSize <= 0`` is per
+    tensor, ``zeroPoint`` None is symmetric."""
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    zp = None if zeroPoint is None else _c(zeroPoint, np.float32)
+    out = np.empty(q.size, np.float32)
+    lib().lpo_dequantize_batch(_p(q), q.size, _p(scales), None if zp is None else _p(zp),
+                               groupSize, _p(out))
     return out
 
 

@@ -197,6 +197,45 @@ def test_quantize_batch_and_calibrate_vs_oracle(n, gs):
     assert np.array_equal(qh, O.quantizeBatch(x, sc_o, gs))
 
 
+@pytest.mark.parametrize("n,gs,asym,off", [
+    (1000, 0, False, 0), (1000, 64, False, 0), (512, 32, False, 0),  # test_quant_simd.nim:33-64
+    (4_000_003, 128, False, 0), (4_000_003, 128, True, 0), (16_000_000, 128, False, 0),
+    (333, 7, True, 0), (97, 1, False, 0), (1001, 64, True, 3), (1001, 24, False, 1), (0, 32, False, 0)])
+def test_dequantize_batch_vs_oracle(n, gs, asym, off):
+    """dequantizeBatch (simd/dequant.nim:159-206): device and host forms equal
+    the oracle bit for bit -- symmetric and zero-point, per tensor and per
+    group (groups shorter than a thread's 16-value run included), ragged
+    tails, and pointers off the 16-byte vector alignment."""
+    rng = np.random.default_rng(n + gs)
+    q = rng.integers(-128, 128, n, dtype=np.int8)
+    ng = (n + gs - 1) // gs if gs > 0 else 1
+    sc = (rng.random(ng, dtype=np.float32) * F(0.1) + F(1e-3)).astype(F)
+    sc[::5] = -sc[::5]
+    zp = (rng.random(ng, dtype=np.float32) * F(40.0) - F(20.0)).astype(F) if asym else None
+    want = O.dequantizeBatch(q, sc, gs, zp)
+    qb = torch.zeros(n + off, dtype=torch.int8, device="cuda")
+    qb[off:] = torch.from_numpy(q).cuda()
+    out = torch.full((n + off,), float("nan"), dtype=torch.float32, device="cuda")
+    sc_d = to_dev(sc)[0]
+    zp_d = to_dev(zp)[0] if asym else None
+    L.dequantizeBatch(qb[off:], sc_d, gs, out[off:], zp_d)
+    assert_bits(to_host(out[off:]), want)
+    if n <= 5000:
+        host = np.full(n, np.nan, F)
+        L.dequantizeBatch(q, sc, gs, host, zp)
+        assert_bits(host, want)
+
+
+def test_dequantize_batch_rejects_short_scales():
+    q = torch.zeros(100, dtype=torch.int8, device="cuda")
+    y = torch.empty(100, dtype=torch.float32, device="cuda")
+    sc = torch.ones(3, dtype=torch.float32, device="cuda")  # 4 groups of 32 needed
+    with pytest.raises(N.NativeError):
+        L.dequantizeBatch(q, sc, 32, y)
+    with pytest.raises(N.NativeError):
+        L.dequantizeBatch(q, torch.ones(4, dtype=torch.float32, device="cuda"), 32, y, sc)
+
+
 def test_calibrate_mx_and_f4_pack_vs_golden_input():
     x = np.fromfile(os.path.join(G, "ref_mx_input.bin"), np.float32)
     sc_o = O.calibrateMX(x, 32, 2)

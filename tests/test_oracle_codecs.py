@@ -184,6 +184,41 @@ def test_calibrate_symmetric_zero_group_and_ragged_tail():
     assert sc[1] == np.float32(49.0) / np.float32(127.0)
 
 
+def _affine(x, gs, qmin, qmax):
+    """calibrateAsymmetric's (scale, zeroPoint) per group (quant.nim:139-177)."""
+    n = x.size
+    gs = gs if gs > 0 else n
+    sc, zp = [], []
+    for lo in range(0, n, gs):
+        mn, mx = np.float32(x[lo:lo + gs].min()), np.float32(x[lo:lo + gs].max())
+        span = np.float32(mx - mn)
+        s = np.float32(span / np.float32(qmax - qmin)) if span > 0 else np.float32(1.0)
+        sc.append(s)
+        zp.append(np.float32(np.float32(qmin) - np.float32(mn / s)))
+    return np.array(sc, np.float32), np.array(zp, np.float32)
+
+
+@pytest.mark.parametrize("kind,n,gs,qmax", [("i8", 1000, 0, 127.0), ("i8", 1000, 64, 127.0),
+                                            ("i4", 512, 32, 7.0), ("i8", 333, 7, 127.0)])
+def test_dequantize_batch_is_the_scalar_formula(kind, n, gs, qmax):
+    """test_quant_simd.nim:33-64: dequantizeBatch of calibrateSymmetric +
+    quantize output equals the scalar dequantize, f32(q) * scale[i div gs],
+    bit for bit; the asymmetric form is (f32(q) - zeroPoint) * scale."""
+    i = np.arange(n, dtype=np.float32)
+    x = (np.sin(i * np.float32(0.1)) * np.float32(5.0)).astype(np.float32)
+    sc = O.calibrateSymmetric(x, gs, qmax)
+    q = O.quantize(x, sc, gs, kind)
+    g = np.arange(n) // (gs if gs > 0 else max(n, 1))
+    want = (q.astype(np.float32) * sc[g]).astype(np.float32)
+    assert np.array_equal(O.dequantizeBatch(q, sc, gs).view(np.uint32), want.view(np.uint32))
+    sa, za = _affine(x, gs, -128.0, 127.0)
+    qa = np.clip(np.round(x / sa[g] + za[g]), -128, 127).astype(np.int8)
+    want = ((qa.astype(np.float32) - za[g]) * sa[g]).astype(np.float32)
+    got = O.dequantizeBatch(qa, sa, gs, za)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.max(np.abs(got - x)) <= np.max(sa) * 0.5 + 1e-6
+
+
 def test_q8_0_split_matches_blocks():
     rng = np.random.default_rng(0)
     x = rng.standard_normal(4096).astype(np.float32)
