@@ -101,44 +101,58 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
     p.rt = rt > 1 ? rt & ~1 : 1;  // whole row pairs
   } else {
-    // Tile height: about two (row pair, group) units per consumer thread, in
-    // whole row pairs, at most 32 rows and 40 KB of weights + scales.
-    int rt = std::max(2, std::min(32, (4 * NC) / p.gpr));
-    rt = std::min(rt, std::max(2, (kTileBytes) / std::max(row_total, 1)));
-    rt = std::min(rt, (p.m + di.sm_count - 1) / di.sm_count + 1);
-    p.rt = std::max(1, rt & ~1);
+    // Tile height: as few tiles per CTA as the tile cap allows (at most 32
+    // rows -- one folder lane each -- and kTileBytes of weights + scales),
+    // then the CTA's rows spread evenly over them, in whole row pairs.  Each
+    // tile costs the consumers a handoff and a ragged last tile idles most
+    // of them, so fewer, even tiles finish sooner (config 1: 9.6 us with
+    // three tiles of 26 rows, 11.0 us with five of 16).
+    const int cap = std::max(2, std::min(32, kTileBytes / std::max(row_total, 1))) & ~1;
+    const int ctas = std::min(p.m, di.sm_count);
+    const int rpc = (p.m + ctas - 1) / ctas;  // rows of the largest CTA
+    const int nt = (rpc + cap - 1) / cap;
+    const int rt = (((rpc + nt - 1) / nt) + 1) & ~1;
+    p.rt = std::max(2, std::min(rt, cap));
   }
   p.tstride = round_up(p.gpr, 32) + 4;
-  // Ordered folds take fb tiles (<= 32 rows) per pass over a ring of two
-  // passes; the unordered fold goes tile by tile over four slots.
-  p.tcols = p.gpr;
-  p.wred = 0;
-  if (Fmt::kFold == Fold::Tree) {
-    p.fb = 1;
-    p.ring = 4;
-    // consumer warps pre-reduce 32 groups when each warp holds 32 groups of
-    // one row pair for the whole launch
-    if (p.gpr % 32 == 0 && NC % p.gpr == 0) {
-      p.wred = 1;
-      p.tcols = p.gpr / 32;
-    }
-  } else {
-    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / (p.rt * vr)));
-    while (p.fb > 1 && 2 * p.fb * p.rt * vr * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
-    p.ring = 2 * p.fb;
-    if (kCols) {
-      // one tile per fold pass; up to four slots (the consumers run ahead)
+  // Shared memory holds the staged activations, the term ring and at least
+  // two weight stages; where the tile height above leaves room for fewer,
+  // tiles get shorter.
+  int terms_bytes = 0;
+  for (;;) {
+    // Ordered folds take fb tiles (<= 32 rows) per pass over a ring of two
+    // passes; the unordered fold goes tile by tile over four slots.
+    p.tcols = p.gpr;
+    p.wred = 0;
+    if (Fmt::kFold == Fold::Tree) {
       p.fb = 1;
-      p.ring = p.rt * vr * p.tstride * 4 * 4 <= 72 * 1024 ? 4 : 2;
+      p.ring = 4;
+      // consumer warps pre-reduce 32 groups when each warp holds 32 groups of
+      // one row pair for the whole launch
+      if (p.gpr % 32 == 0 && NC % p.gpr == 0) {
+        p.wred = 1;
+        p.tcols = p.gpr / 32;
+      }
+    } else {
+      p.fb = std::max(1, std::min(kMaxRing / 2, 32 / (p.rt * vr)));
+      while (p.fb > 1 && 2 * p.fb * p.rt * vr * p.tstride * 4 > 40 * 1024) p.fb >>= 1;
+      p.ring = 2 * p.fb;
+      if (kCols) {
+        // one tile per fold pass; up to four slots (the consumers run ahead)
+        p.fb = 1;
+        p.ring = p.rt * vr * p.tstride * 4 * 4 <= 72 * 1024 ? 4 : 2;
+      }
     }
+    p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
+    p.stage_w_bytes = round_up(p.rt * p.row_bytes, 128);
+    p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 128) : 0;
+    terms_bytes = round_up(p.ring * p.rt * vr * p.tstride * 4, 128);
+    const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
+    const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
+    p.stages = std::min(kMaxStages, (lim[slot].one - fixed) / per_stage);
+    if (p.stages >= 2 || kCols || p.rt <= 2) break;
+    p.rt -= 2;
   }
-  p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
-  p.stage_w_bytes = round_up(p.rt * p.row_bytes, 128);
-  p.stage_s_bytes = Fmt::kScales ? round_up(p.rt * p.gpr * 4, 128) : 0;
-  const int terms_bytes = round_up(p.ring * p.rt * vr * p.tstride * 4, 128);
-  const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
-  const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
-  p.stages = std::min(kMaxStages, (lim[slot].one - fixed) / per_stage);
   if (p.stages < 2) return LP_ERR_UNSUPPORTED;  // activations too large for shared memory
   // Bulk copies need 16-byte aligned, 16-byte multiple rows of weights and scales.
   const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);

@@ -253,3 +253,22 @@ def test_fast_q4_0_several_sequential_groups_in_a_row():
     assert_close(first, O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
     L.dequantGemvQ4_0(bd, K // 32, xd, y)
     assert bits_equal(to_host(y), first)
+
+
+@pytest.mark.parametrize("xoff,woff", [(1, 0), (0, 2), (3, 18)])
+def test_fast_q4_0_unaligned_pointers(xoff, woff):
+    """Activations off the 16-byte grid (staged with scalar loads) and block
+    arrays only 2-byte aligned (the reference's blocks need no more; their
+    rows are staged with plain loads instead of bulk copies) stay within the
+    fast-mode tolerance."""
+    M, K = 333, 4096
+    x = acts(70 + xoff, K)
+    w = weights(70 + woff, M * K)
+    blk = O.quantizeQ4_0(w).reshape(-1)
+    xb = torch.zeros(K + xoff, dtype=torch.float32, device="cuda")
+    xb[xoff:] = torch.from_numpy(x).cuda()
+    bb = torch.zeros(blk.size + woff, dtype=torch.uint8, device="cuda")
+    bb[woff:] = torch.from_numpy(blk).cuda()
+    y = dev_y(M)
+    L.dequantGemvQ4_0(bb[woff:], K // 32, xb[xoff:], y)
+    assert_close(to_host(y), O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
