@@ -22,7 +22,12 @@ namespace {
 
 constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
 constexpr int kMaxStages = 12;
-constexpr int kTileBytes = 64 * 1024;  // weights + scales of one tile, at most
+constexpr int kTileBytes = 96 * 1024;  // weights + scales of one tile, at most
+// Weight bytes in flight per CTA, at most (but at least two stages): the
+// copies in flight share the SM's part of the HBM stream, so more of them
+// only delay the first tile the consumers wait for (config 1: two 58 KB
+// stages 9.6 us, three 10.2 us).
+constexpr int kFlightBytes = 128 * 1024;
 
 inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
@@ -106,7 +111,8 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     // then the CTA's rows spread evenly over them, in whole row pairs.  Each
     // tile costs the consumers a handoff and a ragged last tile idles most
     // of them, so fewer, even tiles finish sooner (config 1: 9.6 us with
-    // three tiles of 26 rows, 11.0 us with five of 16).
+    // three tiles of 26 rows, 11.0 us with five of 16; the config-4 int4
+    // matrices 20.6 and 12.2 us with 96 KB tiles, 23.0 and 13.9 with 64 KB).
     const int cap = std::max(2, std::min(32, kTileBytes / std::max(row_total, 1))) & ~1;
     const int ctas = std::min(p.m, di.sm_count);
     const int rpc = (p.m + ctas - 1) / ctas;  // rows of the largest CTA
@@ -132,6 +138,8 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
       if (p.gpr % 32 == 0 && NC % p.gpr == 0) {
         p.wred = 1;
         p.tcols = p.gpr / 32;
+        // a row holds only its tcols partial sums (float4-aligned rows)
+        p.tstride = round_up(p.tcols, 4) + 4;
       }
     } else {
       p.fb = std::max(1, std::min(kMaxRing / 2, 32 / (p.rt * vr)));
@@ -150,6 +158,7 @@ int launch_gemv(GemvParams p, cudaStream_t st) {
     const int fixed = 128 + round_up(p.x_bytes, 128) + terms_bytes + 8 * (2 * kMaxStages + 2 * kMaxRing);
     const int per_stage = p.stage_w_bytes + p.stage_s_bytes;
     p.stages = std::min(kMaxStages, (lim[slot].one - fixed) / per_stage);
+    if (!kCols) p.stages = std::min(p.stages, std::max(2, kFlightBytes / per_stage));
     if (p.stages >= 2 || kCols || p.rt <= 2) break;
     p.rt -= 2;
   }
