@@ -129,19 +129,23 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 // timeout).
 // send == 0: this rank's words were already stored by the GEMV that made
 // its slice (the fused pooled form); only receive.  The kernel is launched
-// with programmatic stream serialization: a receiving-only grid touches
-// neither this rank's slice nor anything the GEMV before it writes, so it
-// starts polling while that GEMV still runs; a sending grid first waits for
-// the GEMV's slice.  A gather never releases its dependents early, so every
-// kernel after it in the stream starts after it has finished -- in
-// particular the next gather finds this gather's count final.
+// with programmatic stream serialization and releases its dependents at
+// once, so the next kernel (typically the next GEMV) can stage its weights
+// while this gather runs; every kernel of this library launched that way
+// waits for its grid dependency before it reads activations or writes
+// outputs.  The gather itself
+// waits for the kernel before it (the GEMV that made this rank's slice) to
+// complete before it reads the gather count: that GEMV had waited for the
+// previous gather in turn, so the count is final, and this gather completes
+// only after its GEMV has.
 __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t per_row,
                                                    int nranks, int rank, PeerBufs peers,
                                                    uint32_t* state, int send) {
   __shared__ uint32_t s_e;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t C = gridDim.x;
-  if (send) asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (tid == 0) s_e = reinterpret_cast<volatile uint32_t*>(state)[0] + 1u;
   __syncthreads();
   const uint32_t e = s_e;
