@@ -272,3 +272,21 @@ def test_fast_q4_0_unaligned_pointers(xoff, woff):
     y = dev_y(M)
     L.dequantGemvQ4_0(bb[woff:], K // 32, xb[xoff:], y)
     assert_close(to_host(y), O.dequantGemvQ4_0(blk, K // 32, x), vals_blocks(blk, K, True), x)
+
+
+def test_fast_fp32_long_rows_fit_two_stages():
+    """K = 14336: the longest tiles the tile cap allows leave shared memory
+    for fewer than two weight stages next to the staged activations and the
+    term ring, so the planner shortens them; Q4_0 and MXFP4 rows of that
+    length still run and stay within tolerance."""
+    M, K = 300, 14336
+    x = acts(80, K)
+    (y, ref, wv), = run_block_formats(M, K, x, 80)[1:]
+    assert_close(y, ref, wv, x)
+    w = weights(81, M * K)
+    sm = O.calibrateMX(w, 32, 2)
+    pf = O.packF4(O.quantize(w, sm, 32, "f4"))
+    a, b, xd = to_dev(pf, sm, x)
+    yd = dev_y(M)
+    L.dequantGemvF4(a, b, 32, xd, yd)
+    assert_close(to_host(yd), O.dequantGemvF4(pf, sm, 32, x), vals_f4(pf, sm, 32, K), x)
