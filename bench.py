@@ -421,13 +421,31 @@ def main():
 
     yh_all = torch.empty(world * M1, dtype=torch.float32).pin_memory() if world > 1 else None
 
-    def e2e_step(i):
-        wl.x.copy_(xh, non_blocking=True)
-        step(i)
-        if pool is not None:
+    if pool is None:
+        # One GPU: x comes in from page-locked memory by the library's copy-in
+        # kernel (one read over the host link, overlapping the previous GEMV;
+        # every CTA stages all of x, so the GEMV reading it in place would
+        # cross it 148 times); the C-ABI call writes y straight into
+        # page-locked host memory (its device address), each value once.
+        from nim_lowprec_b200 import _native as NV
+        xh_dev, yh_dev = NV.host_device_pointer(xh.data_ptr()), NV.host_device_pointer(yh.data_ptr())
+        lib, nblk = NV.lib(), M1 * wl.bpr
+
+        def e2e_step(i):
+            st = torch.cuda.current_stream().cuda_stream
+            NV.check(lib.lp_copy_in(wl.x.data_ptr(), xh_dev, K1 * 4, st), "e2e copy_in")
+            NV.check(lib.lp_dequant_gemv_q4_0(wl.w[i % wl.ncopies].data_ptr(), nblk, wl.bpr,
+                                              wl.x.data_ptr(), K1, yh_dev, M1,
+                                              torch.cuda.current_stream().cuda_stream),
+                     "e2e dequantGemvQ4_0")
+        transfer = ("x: lp_copy_in kernel from page-locked memory; y: written by the GEMV "
+                    "into page-locked host memory")
+    else:
+        def e2e_step(i):
+            wl.x.copy_(xh, non_blocking=True)
+            step(i)
             yh_all.copy_(y_all, non_blocking=True)
-        else:
-            yh.copy_(wl.y, non_blocking=True)
+        transfer = "cudaMemcpyAsync of x in and of the gathered y out, per step"
 
     e2e_steps = min(args.steps, 20000)
     e_ms, g3 = graph_time(torch, e2e_step, e2e_steps, 3, barrier)
@@ -436,6 +454,16 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e_ms = float(t.item())
     e2e_value = world * e2e_steps * cfg1_bytes() / (e_ms / 1e3) / 1e9
+    if pool is None:  # the host-buffer path gives the device path's bits
+        del g3
+        torch.cuda.synchronize()
+        wl.x.copy_(xh)
+        wl.step(0)
+        e2e_step(0)
+        torch.cuda.synchronize()
+        if not torch.equal(yh, wl.y.cpu()):
+            raise SystemExit("e2e: host-buffer GEMV differs from the device-buffer GEMV")
+        g3 = None
 
     # config 4 (every rank): the 32-layer int4 decode sweep, pooled for N > 1
     cfg4 = None
@@ -500,7 +528,7 @@ def main():
                      "peak_kind": f"{peak_kind} hbm_gbs"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": K1 * 4,
-                "d2h_bytes_per_step": world * M1 * 4, "steps": e2e_steps},
+                "d2h_bytes_per_step": world * M1 * 4, "steps": e2e_steps, "transfer": transfer},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }

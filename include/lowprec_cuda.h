@@ -10,7 +10,9 @@
  *
  * Two forms per kernel:
  *   lp_*   DEVICE pointers + a CUDA stream; asynchronous, stream-ordered,
- *          allocates nothing, reentrant across streams.
+ *          allocates nothing, reentrant across streams.  Activations and
+ *          outputs may also be page-locked host memory, passed by the
+ *          address lp_host_device_pointer gives.
  *   lph_*  HOST pointers, blocking: the literal drop-in for the Nim
  *          signature.  Stages through a cached per-thread device workspace,
  *          copies every input host->device, runs, copies the output back.
@@ -60,6 +62,22 @@ const char *lp_last_error_detail(void);
  * kernel of this library recorded on it (LP_OK if none).  Device-side
  * failures never trap; they are reported here. */
 int lp_device_error(void);
+
+/* Device address of page-locked host memory (no counterpart in the reference).
+ * The device forms take any device-accessible pointer; a page-locked host
+ * buffer (cudaHostAlloc / cudaMallocHost / cudaHostRegister, or a pinned
+ * torch tensor) passed by this address is read and written by the kernels
+ * themselves over the host link, with no copy.  LP_ERR_ARG for memory that
+ * is not page-locked or not mapped. */
+int lp_host_device_pointer(const void *host, void **dev);
+
+/* Copy `bytes` from page-locked host memory (src: its lp_host_device_pointer
+ * address) into device memory as a kernel of `stream` (no counterpart in the
+ * reference).  For per-step inputs of a decode loop: the source is read
+ * while the previous kernel in the stream finishes, dst is written after it
+ * has, and a following GEMV starts streaming its weights at once.  src must
+ * not be written by the kernel before it in the stream. */
+int lp_copy_in(void *dst, const void *src, int64_t bytes, lp_stream_t stream);
 
 /* ======================= fp32-activation fused dequant-GEMVs ========== */
 

@@ -49,6 +49,8 @@ SIGNATURES = {
     "lp_quantize_q4_0_batch": "pnpnp",
     "lp_quantize_q8_0_split": "pnpnpnp",
     "lp_quantize_batch": "pnpnnpnp",
+    "lp_host_device_pointer": "pp",
+    "lp_copy_in": "ppnp",
     "lp_dequantize_batch": "pnpnpnnpnp",
     "lp_calibrate_symmetric": "pnnfpnp",
     "lp_calibrate_mx": "pnnipnp",
@@ -159,6 +161,16 @@ def check(status: int, where: str) -> None:
         # the reference asserts its shape preconditions (AssertionDefect)
         raise AssertionError(f"{where}: {status_string(status)}")
     raise NativeError(status, where)
+
+
+def host_device_pointer(host_addr: int) -> int:
+    """Device address of page-locked host memory (e.g. a pinned torch CPU
+    tensor's data_ptr()), for passing activations or outputs that live in
+    host memory straight to a device form; raises NativeError otherwise."""
+    d = ctypes.c_void_p()
+    check(lib().lp_host_device_pointer(ctypes.c_void_p(host_addr), ctypes.byref(d)),
+          "host_device_pointer")
+    return int(d.value)
 
 
 def device_error() -> int:

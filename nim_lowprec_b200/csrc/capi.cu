@@ -141,6 +141,23 @@ int lp_device_error(void) {
   return static_cast<int>(e);
 }
 
+int lp_host_device_pointer(const void* host, void** dev) {
+  if (!host || !dev) return LP_ERR_ARG;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, const_cast<void*>(host), 0) != cudaSuccess || !d) {
+    cudaGetLastError();  // not page-locked here: clear the runtime's error
+    return LP_ERR_ARG;
+  }
+  *dev = d;
+  return LP_OK;
+}
+
+int lp_copy_in(void* dst, const void* src, int64_t bytes, lp_stream_t stream) {
+  if (bytes < 0 || bad(dst, bytes) || bad(src, bytes)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  return lp::launch_copy_in(dst, src, bytes, S(stream));
+}
+
 // ------------------------------------------------ fp32-activation GEMVs
 
 static int gemv_f32_group(int fmt, const void* w, int64_t w_len, const float* scales,

@@ -60,6 +60,9 @@ struct FmtI4Q8Cols;
 template <class Fmt>
 int launch_gemv(GemvParams p, cudaStream_t st);
 
+// per-step inputs from page-locked host memory (transfer.cu)
+int launch_copy_in(void* dst, const void* src, int64_t bytes, cudaStream_t st);
+
 // encoders (quant.cu)
 int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* qs, float* d,
                          cudaStream_t st);

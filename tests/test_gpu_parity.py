@@ -600,3 +600,62 @@ def test_unaligned_device_pointers_take_plain_staging():
     y = dev_y(M)
     L.dequantGemv(big[1:], sd, 32, xd, y)
     assert_bits(to_host(y), O.dequantGemv(q8, s8, 32, x))
+
+
+def test_page_locked_host_buffers_through_the_device_forms():
+    """lp_host_device_pointer: a device form given page-locked host memory for
+    its activations and output reads and writes it in place, with the bits of
+    the device-buffer call (fp32 Q4_0 in both modes, int8 Q8); pageable
+    memory is refused before anything is launched."""
+    M, K = 1000, 4096
+    bpr, gpr = K // 32, K // 32
+    w = weights(90, M * K)
+    x = acts(91, K)
+    blk = O.quantizeQ4_0(w).reshape(-1)
+    (bd,) = to_dev(blk)
+    xd = torch.from_numpy(x).cuda()
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.full((M,), float("nan"), dtype=torch.float32).pin_memory()
+    xp, yp = N.host_device_pointer(xh.data_ptr()), N.host_device_pointer(yh.data_ptr())
+    st = torch.cuda.current_stream().cuda_stream
+    for mode in ("fast", "exact"):
+        with L.fp32_mode(mode):
+            yd = dev_y(M)
+            L.dequantGemvQ4_0(bd, bpr, xd, yd)
+            N.check(N.lib().lp_dequant_gemv_q4_0(bd.data_ptr(), M * bpr, bpr, xp, K, yp, M, st), "q4_0")
+            torch.cuda.synchronize()
+            assert_bits(yh.numpy(), to_host(yd))
+    wq, ws = O.quantizeQ8_0Split(w)
+    xq, xs = O.quantizeQ8_0Split(x)
+    wqd, wsd, xqd, xsd = to_dev(wq, ws, xq, xs)
+    yd = dev_y(M)
+    L.dequantGemvQ8(wqd, wsd, 32, xqd, xsd, yd)
+    xqh, xsh = torch.from_numpy(xq).pin_memory(), torch.from_numpy(xs).pin_memory()
+    yh.fill_(float("nan"))
+    N.check(N.lib().lp_dequant_gemv_q8(wqd.data_ptr(), M * K, wsd.data_ptr(), M * gpr, 32,
+                                       N.host_device_pointer(xqh.data_ptr()), K,
+                                       N.host_device_pointer(xsh.data_ptr()), gpr, yp, M, st), "q8")
+    torch.cuda.synchronize()
+    assert_bits(yh.numpy(), to_host(yd))
+    pageable = np.zeros(16, np.float32)
+    with pytest.raises(N.NativeError):
+        N.host_device_pointer(pageable.ctypes.data)
+
+
+
+@pytest.mark.parametrize("nbytes,soff,doff", [(16384, 0, 0), (44032, 0, 0), (4097, 0, 0),
+                                              (1000, 3, 5), (0, 0, 0)])
+def test_copy_in_from_page_locked_memory(nbytes, soff, doff):
+    """lp_copy_in moves bytes from page-locked host memory into device memory
+    in stream order (16-byte units when both ends and the size allow)."""
+    rng = np.random.default_rng(nbytes)
+    src = torch.from_numpy(rng.integers(0, 256, nbytes + soff, dtype=np.uint8)).pin_memory()
+    dst = torch.zeros(nbytes + doff + 7, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    # (an empty pinned tensor has no storage: zero bytes take a null source)
+    sp = N.host_device_pointer(src.data_ptr()) + soff if nbytes else None
+    N.check(N.lib().lp_copy_in(dst.data_ptr() + doff, sp, nbytes, st), "copy_in")
+    torch.cuda.synchronize()
+    got = dst.cpu().numpy()
+    assert np.array_equal(got[doff:doff + nbytes], src.numpy()[soff:])
+    assert not got[:doff].any() and not got[doff + nbytes:].any()
