@@ -441,11 +441,21 @@ def main():
         transfer = ("x: lp_copy_in kernel from page-locked memory; y: written by the GEMV "
                     "into page-locked host memory")
     else:
+        # N GPUs: x in by the copy-in kernel; the pooled call's y is the
+        # page-locked host vector itself -- the GEMV writes this rank's rows
+        # and the receive kernel the other ranks' rows straight into it.
+        from nim_lowprec_b200 import _native as NV
+        xh_dev = NV.host_device_pointer(xh.data_ptr())
+        yall_dev = NV.host_device_pointer(yh_all.data_ptr())
+        lib, nblk = NV.lib(), M1 * wl.bpr
+
         def e2e_step(i):
-            wl.x.copy_(xh, non_blocking=True)
-            step(i)
-            yh_all.copy_(y_all, non_blocking=True)
-        transfer = "cudaMemcpyAsync of x in and of the gathered y out, per step"
+            st = torch.cuda.current_stream().cuda_stream
+            NV.check(lib.lp_copy_in(wl.x.data_ptr(), xh_dev, K1 * 4, st), "e2e copy_in")
+            pool.call("lp_pool_dequant_gemv_q4_0", wl.w[i % wl.ncopies].data_ptr(), nblk, wl.bpr,
+                      wl.x.data_ptr(), K1, yall_dev, world * M1, st)
+        transfer = ("x: lp_copy_in kernel from page-locked memory; y: the pooled call writes the "
+                    "whole gathered vector into page-locked host memory")
 
     e2e_steps = min(args.steps, 20000)
     e_ms, g3 = graph_time(torch, e2e_step, e2e_steps, 3, barrier)
@@ -454,16 +464,18 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e_ms = float(t.item())
     e2e_value = world * e2e_steps * cfg1_bytes() / (e_ms / 1e3) / 1e9
-    if pool is None:  # the host-buffer path gives the device path's bits
-        del g3
-        torch.cuda.synchronize()
-        wl.x.copy_(xh)
-        wl.step(0)
-        e2e_step(0)
-        torch.cuda.synchronize()
-        if not torch.equal(yh, wl.y.cpu()):
-            raise SystemExit("e2e: host-buffer GEMV differs from the device-buffer GEMV")
-        g3 = None
+    # the host-buffer path gives the device path's bits (every rank, same calls)
+    del g3
+    torch.cuda.synchronize()
+    barrier()
+    wl.x.copy_(xh)
+    step(0)
+    e2e_step(0)
+    torch.cuda.synchronize()
+    got, want = (yh, wl.y) if pool is None else (yh_all, y_all)
+    if not torch.equal(got, want.cpu()):
+        raise SystemExit("e2e: host-buffer GEMV differs from the device-buffer GEMV")
+    g3 = None
 
     # config 4 (every rank): the 32-layer int4 decode sweep, pooled for N > 1
     cfg4 = None
