@@ -440,6 +440,13 @@ def main():
                      "e2e dequantGemvQ4_0")
         transfer = ("x: lp_copy_in kernel from page-locked memory; y: written by the GEMV "
                     "into page-locked host memory")
+    elif not pool.p2p:
+        # the pool's NCCL transport gathers device buffers only
+        def e2e_step(i):
+            wl.x.copy_(xh, non_blocking=True)
+            step(i)
+            yh_all.copy_(y_all, non_blocking=True)
+        transfer = "cudaMemcpyAsync of x in and of the gathered y out, per step"
     else:
         # N GPUs: x in by the copy-in kernel; the pooled call's y is the
         # page-locked host vector itself -- the GEMV writes this rank's rows
