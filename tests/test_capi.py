@@ -91,3 +91,28 @@ def test_python_api_rejects_wrong_dtypes_and_mixed_arrays():
     with pytest.raises(TypeError):
         L.dequantGemvQ8(np.zeros(64, np.int16), np.zeros(2, np.float32), 32,
                         np.zeros(64, np.int8), np.zeros(2, np.float32), np.zeros(1, np.float32))
+
+
+def test_host_buffer_entries_check_their_arguments_before_the_device():
+    """lp_copy_in and lp_host_device_pointer refuse null pointers and negative
+    sizes, and an empty copy is a no-op, all without a CUDA call."""
+    L = N.lib()
+    out = ctypes.c_void_p()
+    assert L.lp_host_device_pointer(NULL, ctypes.byref(out)) == N.LP_ERR_ARG
+    assert L.lp_host_device_pointer(ctypes.c_void_p(16), NULL) == N.LP_ERR_ARG
+    assert L.lp_copy_in(NULL, NULL, 0, NULL) == N.LP_OK
+    assert L.lp_copy_in(NULL, ctypes.c_void_p(16), 64, NULL) == N.LP_ERR_ARG
+    assert L.lp_copy_in(ctypes.c_void_p(16), NULL, 64, NULL) == N.LP_ERR_ARG
+    assert L.lp_copy_in(ctypes.c_void_p(16), ctypes.c_void_p(16), -1, NULL) == N.LP_ERR_ARG
+    with pytest.raises(N.NativeError):
+        N.host_device_pointer(0)
+
+
+def test_dequantize_batch_shape_rules():
+    """dequantizeBatch asserts q.len == dst.len; scales and zero points must
+    cover every group."""
+    L = N.lib()
+    assert L.lp_dequantize_batch(NULL, 64, NULL, 2, NULL, 0, 32, NULL, 63, NULL) == N.LP_ERR_SHAPE
+    assert L.lp_dequantize_batch(NULL, 64, NULL, 1, NULL, 0, 32, NULL, 64, NULL) == N.LP_ERR_SHAPE
+    assert L.lp_dequantize_batch(NULL, 64, NULL, 2, NULL, 1, 32, NULL, 64, NULL) == N.LP_ERR_SHAPE
+    assert L.lp_dequantize_batch(NULL, 0, NULL, 0, NULL, 0, 32, NULL, 0, NULL) == N.LP_OK
