@@ -140,6 +140,21 @@ int lp_dequant_gemv_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const floa
                          int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
                          int64_t y_len, lp_stream_t stream);
 
+/* quantizeQ8_0 of fp32 x followed by dequantGemvQ8 / dequantGemvI4Q8, in one
+ * launch: the GEMV quantizes the activations while it stages them, with the
+ * arithmetic of lp_quantize_q8_0_split, so the results equal the two calls'
+ * bit for bit.  The composition of ggml.nim:60-75 (quantizeQ8_0, =
+ * simd/dequant.nim:1624-1641) with simd/dequant.nim:753-878 / :968-1145; no
+ * single proc of the reference.  group_size must be 32 (the Q8_0 block) and
+ * x_len a multiple of 32. */
+int lp_quantize_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                                int64_t w_scales_len, int64_t group_size, const float *x,
+                                int64_t x_len, float *y, int64_t y_len, lp_stream_t stream);
+int lp_quantize_dequant_gemv_i4q8(const uint8_t *wpacked, int64_t wpacked_len,
+                                  const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                                  const float *x, int64_t x_len, float *y, int64_t y_len,
+                                  lp_stream_t stream);
+
 /* dequantGemvQ8_0Q8: Q8_0 weight blocks x Q8_0 activation blocks.
  * Replaces simd/dequant.nim:1187-1286 (proc dequantGemvQ8_0Q8*). */
 int lp_dequant_gemv_q8_0q8(const void *w, int64_t w_len, int64_t blocks_per_row, const void *xq,

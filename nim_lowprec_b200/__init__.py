@@ -12,7 +12,8 @@ from .dequant import (  # noqa: F401
     dequantGemvF4, dequantGemvI4, dequantGemvI4Q8, dequantGemvQ4_0, dequantGemvQ4_0Q8,
     dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantizeBatch, dequantizeQ4_0Batch,
     dequantizeQ4_K, dequantizeQ6_K, dequantizeQ8_0Batch, dequantizeNVFP4, quantizeBatch,
-    quantizeNVFP4, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0,
+    quantizeNVFP4, quantizeF4Packed, quantizeI4Packed, quantizeQ4_0, quantizeDequantGemvI4Q8,
+    quantizeDequantGemvQ8,
     quantizeQ4_0Batch, quantizeQ8_0, quantizeQ8_0Batch, quantizeQ8_0Split, fp32_mode,
     fp32Mode, setFp32Mode)
 from .ggml import QK, QK_K, BlockQ4_0, BlockQ4_K, BlockQ6_K, BlockQ8_0  # noqa: F401

@@ -50,6 +50,8 @@ SIGNATURES = {
     "lp_quantize_q8_0_split": "pnpnpnp",
     "lp_quantize_batch": "pnpnnpnp",
     "lp_host_device_pointer": "pp",
+    "lp_quantize_dequant_gemv_q8": "pnpnnpnpnp",
+    "lp_quantize_dequant_gemv_i4q8": "pnpnnpnpnp",
     "lp_copy_in": "ppnp",
     "lp_dequantize_batch": "pnpnpnnpnp",
     "lp_calibrate_symmetric": "pnnfpnp",

@@ -246,6 +246,38 @@ static int gemv_q8_group(int i4, const void* w, int64_t w_len, const float* ws, 
   return i4 ? lp::launch_gemv<lp::FmtI4Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8>(p, S(st));
 }
 
+// quantizeQ8_0 (ggml.nim:60-75) of fp32 x, then the Q8-activation GEMV, as
+// one launch; Q8_0 blocks are 32 values, so the weight groups must be too.
+static int gemv_q8_from_f32(int i4, const void* w, int64_t w_len, const float* ws,
+                            int64_t ws_len, int64_t gs, const float* x, int64_t x_len, float* y,
+                            int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len, k = x_len;
+  LP_REQUIRE(gs == 32 && fits(m, k) && k % 32 == 0);
+  const int64_t gpr = k / 32;
+  const int64_t rb = i4 ? k / 2 : k;
+  LP_REQUIRE(w_len == m * rb && ws_len == m * gpr);
+  if (bad(w, w_len) || bad(ws, ws_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  GemvParams p = base(w, ws, x, nullptr, y, m, k, 32, gpr, rb);
+  return i4 ? lp::launch_gemv<lp::FmtI4Q8FromF32>(p, S(st))
+            : lp::launch_gemv<lp::FmtQ8FromF32>(p, S(st));
+}
+
+int lp_quantize_dequant_gemv_q8(const int8_t* wq, int64_t wq_len, const float* w_scales,
+                                int64_t w_scales_len, int64_t group_size, const float* x,
+                                int64_t x_len, float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_q8_from_f32(0, wq, wq_len, w_scales, w_scales_len, group_size, x, x_len, y, y_len,
+                          stream);
+}
+
+int lp_quantize_dequant_gemv_i4q8(const uint8_t* wpacked, int64_t wpacked_len,
+                                  const float* w_scales, int64_t w_scales_len, int64_t group_size,
+                                  const float* x, int64_t x_len, float* y, int64_t y_len,
+                                  lp_stream_t stream) {
+  return gemv_q8_from_f32(1, wpacked, wpacked_len, w_scales, w_scales_len, group_size, x, x_len,
+                          y, y_len, stream);
+}
+
 int lp_dequant_gemv_q8(const int8_t* wq, int64_t wq_len, const float* w_scales,
                        int64_t w_scales_len, int64_t group_size, const int8_t* xq, int64_t xq_len,
                        const float* x_scales, int64_t x_scales_len, float* y, int64_t y_len,

@@ -51,6 +51,8 @@ template <> int x_stage_bytes<FmtQ8>(const GemvParams& p) { return q8_bytes(p); 
 template <> int x_stage_bytes<FmtI4Q8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ8_0Q8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ4_0Q8>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtQ8FromF32>(const GemvParams& p) { return q8_bytes(p); }
+template <> int x_stage_bytes<FmtI4Q8FromF32>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ8Cols>(const GemvParams& p) {
   return round_up(p.k * p.ncol, 16) + 4 * p.gpr * p.ncol;
 }
@@ -210,6 +212,8 @@ template int launch_gemv<FmtQ8_0F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ4_0F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtI4Q8>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ8FromF32>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtI4Q8FromF32>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8_0Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ4_0Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8Cols>(GemvParams, cudaStream_t);

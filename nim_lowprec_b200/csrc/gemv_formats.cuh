@@ -866,6 +866,49 @@ struct StageXQ8 {
   }
 };
 
+// fp32 activations quantized to Q8_0 while they are staged -- the same
+// arithmetic as quantizeQ8_0 (ggml.nim:60-75, k_quantize_q8_0): amax of the
+// 32-value block, d = fl(amax / 127), id = d ? fl(1 / d) : 0, q =
+// clamp(roundf(fl(x * id)), +-127), scale = f32(f16(d)) -- into StageXQ8's
+// layout, so quantizeQ8_0 followed by a Q8-activation GEMV becomes one launch
+// with the two-launch bits.  Eight threads per block, four values each.
+struct StageXQ8FromF32 {
+  static __device__ __noinline__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid,
+                                              int nthr) {
+    const float* x = static_cast<const float*>(p.x);
+    uint32_t* q = reinterpret_cast<uint32_t*>(xsm);
+    float* xs = reinterpret_cast<float*>(xsm + ((p.k + 15) & ~15));
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const int ntask = p.gpr * 8;
+    for (int t0 = tid & ~31; t0 < ntask; t0 += nthr) {
+      const int t = t0 + (tid & 31);
+      const bool valid = t < ntask;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid)
+        v = vec ? __ldg(reinterpret_cast<const float4*>(x) + t)
+                : make_float4(__ldg(x + 4 * t), __ldg(x + 4 * t + 1), __ldg(x + 4 * t + 2),
+                              __ldg(x + 4 * t + 3));
+      float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+      if (!valid) continue;
+      const float d = __fdiv_rn(a, 127.0f);
+      const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+      const float e[4] = {v.x, v.y, v.z, v.w};
+      uint32_t word = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float r = roundf(__fmul_rn(e[i], id));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        word |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * i);
+      }
+      q[t] = word;
+      if ((t & 7) == 0) xs[t >> 3] = h2f(__half_as_ushort(__float2half_rn(d)));
+    }
+  }
+};
+
 // dequantGemvQ8 (simd/dequant.nim:753-878; scalar :868-878).
 struct FmtQ8 : StageXQ8 {
   static constexpr bool kScales = true;
@@ -980,6 +1023,18 @@ struct FmtI4Q8 : StageXQ8 {
       isum += (n >= 8 ? n - 16 : n) * static_cast<int8_t>(xq[kk]);
     }
     return fmul(fmul(i2f_rn(isum), ws), xs);
+  }
+};
+
+// quantizeQ8_0 of fp32 x, then dequantGemvQ8 / dequantGemvI4Q8, in one launch.
+struct FmtQ8FromF32 : FmtQ8 {
+  static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
+    StageXQ8FromF32::stage_x(xsm, p, tid, nthr);
+  }
+};
+struct FmtI4Q8FromF32 : FmtI4Q8 {
+  static __device__ void stage_x(uint8_t* xsm, const GemvParams& p, int tid, int nthr) {
+    StageXQ8FromF32::stage_x(xsm, p, tid, nthr);
   }
 };
 

@@ -50,6 +50,8 @@ struct FmtI4F;
 struct FmtF4F;
 struct FmtQ8_0F;
 struct FmtQ4_0F;
+struct FmtQ8FromF32;
+struct FmtI4Q8FromF32;
 struct FmtQ8;
 struct FmtI4Q8;
 struct FmtQ8_0Q8;

@@ -209,6 +209,28 @@ def dequantGemvI4Q8(wpacked, wScales, groupSize, xq, xScales, y):
     _gemv_q8("dequant_gemv_i4q8", wpacked, wScales, groupSize, xq, xScales, y, np.uint8)
 
 
+def _quantize_gemv_q8(name, w, wScales, groupSize, x, y, wdt):
+    _dev_only(name, w, wScales, x, y)
+    _check_dtype(w, wdt, "w"); _check_dtype(wScales, np.float32, "wScales")
+    _check_dtype(x, np.float32, "x"); _check_dtype(y, np.float32, "y")
+    N.check(getattr(N.lib(), "lp_" + name)(_ptr(w), _numel(w), _ptr(wScales), _numel(wScales),
+                                          int(groupSize), _ptr(x), _numel(x), _ptr(y), _numel(y),
+                                          _stream()), name)
+
+
+def quantizeDequantGemvQ8(wq, wScales, groupSize, x, y):
+    """quantizeQ8_0 of fp32 x (ggml.nim:60-75) then dequantGemvQ8
+    (simd/dequant.nim:753-878) in one launch; the two calls' bits.
+    groupSize must be 32."""
+    _quantize_gemv_q8("quantize_dequant_gemv_q8", wq, wScales, groupSize, x, y, np.int8)
+
+
+def quantizeDequantGemvI4Q8(wpacked, wScales, groupSize, x, y):
+    """quantizeQ8_0 of fp32 x then dequantGemvI4Q8 (simd/dequant.nim:968-1145)
+    in one launch; the two calls' bits.  groupSize must be 32."""
+    _quantize_gemv_q8("quantize_dequant_gemv_i4q8", wpacked, wScales, groupSize, x, y, np.uint8)
+
+
 def dequantGemvQ8_0Q8(w, blocksPerRow, xq, y):
     """simd/dequant.nim:1187-1286: Q8_0 weights x Q8_0 activation blocks."""
     _gemv_blocks("dequant_gemv_q8_0q8", w, Q8_0_BYTES, blocksPerRow, xq, y, xq_blocks=True)

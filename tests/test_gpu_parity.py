@@ -659,3 +659,39 @@ def test_copy_in_from_page_locked_memory(nbytes, soff, doff):
     got = dst.cpu().numpy()
     assert np.array_equal(got[doff:doff + nbytes], src.numpy()[soff:])
     assert not got[:doff].any() and not got[doff + nbytes:].any()
+
+
+@pytest.mark.parametrize("M,K,xoff", [(1, 32, 0), (333, 4096, 0), (4096, 11008, 0),
+                                      (300, 4096, 1), (4800, 4096, 0)])
+def test_quantize_dequant_gemv_is_the_two_calls(M, K, xoff):
+    """quantizeQ8_0 + dequantGemvQ8 / dequantGemvI4Q8 fused into one launch give
+    the bits of the two separate calls and of the oracle -- an all-zero
+    block, a block of large values, ragged row counts and activations off the
+    16-byte grid included."""
+    w = weights(100 + M, M * K)
+    x = acts(101 + M, K)
+    x[:32] = 0.0
+    if K >= 96:
+        x[64:96] *= F(1e4)  # large, with the block's f16 scale still finite
+    gpr = K // 32
+    xq_o, xs_o = O.quantizeQ8_0Split(x)
+    xb = torch.zeros(K + xoff, dtype=torch.float32, device="cuda")
+    xb[xoff:] = torch.from_numpy(x).cuda()
+    xd = xb[xoff:]
+    xq = torch.empty(K, dtype=torch.int8, device="cuda")
+    xs = torch.empty(gpr, dtype=torch.float32, device="cuda")
+    L.quantizeQ8_0Split(xd, xq, xs)
+    wq, ws = O.quantizeQ8_0Split(w)
+    s4 = O.calibrateSymmetric(w, 32, 7.0)
+    p4 = O.packInt4(O.quantize(w, s4, 32, "i4"))
+    for fused, two, ofn, wt, st in (
+            (L.quantizeDequantGemvQ8, L.dequantGemvQ8, O.dequantGemvQ8, wq, ws),
+            (L.quantizeDequantGemvI4Q8, L.dequantGemvI4Q8, O.dequantGemvI4Q8, p4, s4)):
+        wd, sd = to_dev(wt, st)
+        y1, y2 = dev_y(M), dev_y(M)
+        fused(wd, sd, 32, xd, y1)
+        two(wd, sd, 32, xq, xs, y2)
+        assert_bits(to_host(y1), to_host(y2))
+        assert_bits(to_host(y1), ofn(wt, st, 32, xq_o, xs_o))
+    with pytest.raises(AssertionError):
+        L.quantizeDequantGemvQ8(*to_dev(wq, ws), 64, xd, dev_y(M))
