@@ -190,16 +190,25 @@ class Cfg4Workload:
         self.y = torch.empty(layers, world * self.per, dtype=torch.float32, device="cuda")
         torch.cuda.empty_cache()
 
-    def layer(self, pool, layer):
+    def layer(self, pool, layer, fused=True):
+        """fused: each GEMV quantizes its fp32 activations to Q8_0 itself
+        (quantizeDequantGemvI4Q8, two launches per layer); else the separate
+        quantizeQ8_0 launches (four per layer) -- the same bits."""
         L = self.L
         yl = self.y[layer]
         off = self.rank * self.per
-        L.quantizeQ8_0Split(self.x[layer], self.xq, self.xs)
-        L.dequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.xq, self.xs,
-                          yl[off:off + self.rc])
-        L.quantizeQ8_0Split(self.xd[layer], self.dq, self.ds)
-        L.dequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.dq, self.ds,
-                          yl[off + self.rc:off + self.per])
+        if fused:
+            L.quantizeDequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.x[layer],
+                                      yl[off:off + self.rc])
+            L.quantizeDequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.xd[layer],
+                                      yl[off + self.rc:off + self.per])
+        else:
+            L.quantizeQ8_0Split(self.x[layer], self.xq, self.xs)
+            L.dequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.xq, self.xs,
+                              yl[off:off + self.rc])
+            L.quantizeQ8_0Split(self.xd[layer], self.dq, self.ds)
+            L.dequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.dq, self.ds,
+                              yl[off + self.rc:off + self.per])
         if pool is not None:
             from nim_lowprec_b200 import parallel as P
             pool.call("lp_pool_gather_rows", yl.data_ptr(), self.world * self.per, 1, P._stream())
@@ -499,7 +508,7 @@ def main():
         cfg4 = {"GB/s": round(gbs, 1), "frac_per_gpu": round(gbs / world / peak, 3),
                 "ms_per_sweep": round(sweep_ms, 4), "layers": LAYERS,
                 "weight_bytes_per_sweep": LAYERS * cfg4_bytes_per_layer(),
-                "launches_per_layer": 4, "gather_per_layer": world > 1}
+                "launches_per_layer": 2, "gather_per_layer": world > 1}
         del wl4
         torch.cuda.empty_cache()
 
@@ -636,7 +645,7 @@ def profile_kernels(torch, L):
 
     wl4 = Cfg4Workload(torch, L, 1, 0, layers=1)
     run("config4 layer 0: quantizeQ8_0 (4096), dequantGemvI4Q8 38400x4096, "
-        "quantizeQ8_0 (11008), dequantGemvI4Q8 4096x11008", lambda: wl4.layer(None, 0))
+        "quantizeQ8_0 (11008), dequantGemvI4Q8 4096x11008", lambda: wl4.layer(None, 0, fused=False))
     del wl4
     torch.cuda.empty_cache()
 
