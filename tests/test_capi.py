@@ -116,3 +116,15 @@ def test_dequantize_batch_shape_rules():
     assert L.lp_dequantize_batch(NULL, 64, NULL, 1, NULL, 0, 32, NULL, 64, NULL) == N.LP_ERR_SHAPE
     assert L.lp_dequantize_batch(NULL, 64, NULL, 2, NULL, 1, 32, NULL, 64, NULL) == N.LP_ERR_SHAPE
     assert L.lp_dequantize_batch(NULL, 0, NULL, 0, NULL, 0, 32, NULL, 0, NULL) == N.LP_OK
+
+
+def test_quantize_dequant_gemv_shape_rules():
+    """The fused quantizeQ8_0 + GEMV entries need Q8_0-sized groups (32),
+    whole blocks of x, and the weight/scale lengths of the GEMV they fuse."""
+    L = N.lib()
+    for fn, rb in ((L.lp_quantize_dequant_gemv_q8, 64), (L.lp_quantize_dequant_gemv_i4q8, 32)):
+        assert fn(NULL, 2 * rb, NULL, 4, 64, NULL, 64, NULL, 2, NULL) == N.LP_ERR_SHAPE   # gs 64
+        assert fn(NULL, 2 * rb, NULL, 4, 32, NULL, 48, NULL, 2, NULL) == N.LP_ERR_SHAPE   # x 48
+        assert fn(NULL, 2 * rb - 1, NULL, 4, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_SHAPE
+        assert fn(NULL, 2 * rb, NULL, 3, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_SHAPE
+        assert fn(NULL, 2 * rb, NULL, 4, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_ARG     # nulls
