@@ -19,7 +19,7 @@
 ## Types come from the reference modules (I8, BlockQ8_0, BlockQ4_0), which
 ## are layout-compatible with the C ABI (34 / 18-byte blocks).
 
-import nim_lowprec/[intx, ggml]
+import nim_lowprec/[intx, ggml, quant]
 
 const lpLib* {.strdefine.} = "liblowprec_cuda.so"
 
@@ -58,6 +58,11 @@ proc lph_quantize_q8_0_batch(src: pointer, srcLen: int64, blocks: pointer,
     blocksLen: int64): cint {.importc, dynlib: lpLib.}
 proc lph_quantize_q4_0_batch(src: pointer, srcLen: int64, blocks: pointer,
     blocksLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_quantize_batch(x: pointer, xLen: int64, scales: pointer, scalesLen: int64,
+    gs: int64, dst: pointer, dstLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_dequantize_batch(q: pointer, qLen: int64, scales: pointer, scalesLen: int64,
+    zp: pointer, zpLen: int64, gs: int64, dst: pointer, dstLen: int64): cint {.
+    importc, dynlib: lpLib.}
 proc lp_status_string(status: cint): cstring {.importc, dynlib: lpLib.}
 
 template base[T](a: openArray[T]): pointer =
@@ -143,3 +148,27 @@ proc quantizeQ8_0Batch*(src: openArray[float32], blocks: var openArray[BlockQ8_0
 proc quantizeQ4_0Batch*(src: openArray[float32], blocks: var openArray[BlockQ4_0]) =
   check(lph_quantize_q4_0_batch(base(src), src.len, base(blocks), blocks.len),
       "quantizeQ4_0Batch")
+
+# ---- elementwise codecs over QParams (simd/dequant.nim:159-206, 1717-1750) ----
+
+proc groupOf(p: QParams): int64 =
+  ## QParams' group size as the C ABI takes it: 0 for a per-tensor scale.
+  if p.scheme == qPerTensor: 0'i64 else: p.groupSize.int64
+
+proc quantizeBatch*(x: openArray[float32], p: QParams, dst: var openArray[I8]) =
+  ## The symmetric case, as the reference's vector form; QParams with zero
+  ## points are refused (the reference runs its scalar `quantize` for them).
+  if p.zeroPoint.len > 0:
+    raise newException(LowprecCudaError, "quantizeBatch: QParams with zero points")
+  check(lph_quantize_batch(base(x), x.len, base(p.scale), p.scale.len, groupOf(p),
+      base(dst), dst.len), "quantizeBatch")
+
+template defDequantizeBatch(T: untyped) =
+  proc dequantizeBatch*(q: openArray[T], p: QParams, dst: var openArray[float32]) =
+    ## (f32(q) - zeroPoint) * scale per group; symmetric and affine QParams.
+    check(lph_dequantize_batch(base(q), q.len, base(p.scale), p.scale.len,
+        base(p.zeroPoint), p.zeroPoint.len, groupOf(p), base(dst), dst.len),
+        "dequantizeBatch")
+
+defDequantizeBatch(I8)
+defDequantizeBatch(I4)
