@@ -128,3 +128,19 @@ def test_quantize_dequant_gemv_shape_rules():
         assert fn(NULL, 2 * rb - 1, NULL, 4, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_SHAPE
         assert fn(NULL, 2 * rb, NULL, 3, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_SHAPE
         assert fn(NULL, 2 * rb, NULL, 4, 32, NULL, 64, NULL, 2, NULL) == N.LP_ERR_ARG     # nulls
+
+
+def test_nim_shim_binds_only_exported_symbols():
+    """Every C symbol the Nim shim imports (importc, dynlib) is exported by the
+    library with the header's name -- the shim cannot be compiled here."""
+    import os
+    import re
+    shim = os.path.join(os.path.dirname(N.LIB_PATH), "nim", "nim_lowprec_cuda.nim")
+    src = open(shim).read()
+    names = re.findall(r"^proc\s+(lph?_\w+)\s*\(", src, flags=re.M)
+    assert len(names) >= 15
+    L = N.lib()
+    header = open(N.HEADER).read()
+    for name in names:
+        assert hasattr(L, name), name
+        assert re.search(r"\b" + name + r"\s*\(", header), name
