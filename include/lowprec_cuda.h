@@ -49,6 +49,9 @@ extern "C" {
 
 typedef void *lp_stream_t; /* a cudaStream_t; NULL is the legacy default stream */
 
+/* Library utilities (no counterpart in the reference, whose procs assert
+ * and return nothing). */
+
 /* Library version, e.g. 100 for 0.1.0. */
 int lp_version(void);
 
@@ -269,7 +272,8 @@ int lp_dequantize_nvfp4(const uint8_t *codes, int64_t codes_len, const uint8_t *
 
 /* ======================= host-pointer drop-in forms ==================== */
 /* Same arguments and meaning as the lp_* forms above, HOST pointers, no
- * stream; blocking. */
+ * stream; blocking.  Each replaces the same reference proc as its lp_* form
+ * (simd/dequant.nim, ggml.nim), with the Nim signature's host arrays. */
 int lph_dequant_gemv(const int8_t *wq, int64_t wq_len, const float *scales, int64_t scales_len,
                      int64_t group_size, const float *x, int64_t x_len, float *y, int64_t y_len);
 int lph_dequant_gemv_i4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
@@ -350,10 +354,13 @@ int lp_pool_size(lp_pool_t pool, int *nranks, int *rank);
  * LP_ERR_UNSUPPORTED: the exchange could not be mapped on every rank. */
 int lp_pool_set_p2p(lp_pool_t pool, int enable);
 int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
-/* Gather every rank's row slice of y (m rows of per_row floats) in place. */
+/* Gather every rank's row slice of y (m rows of per_row floats) in place:
+ * the output exchange inside the reference's par* procs (parallel.nim:186-474),
+ * on its own. */
 int lp_pool_gather_rows(lp_pool_t pool, float *y, int64_t m, int64_t per_row, lp_stream_t stream);
 
-/* Pooled forms of the GEMVs / GEMMs above (parDequantGemv*, parDequantGemm*). */
+/* Pooled forms of the GEMVs / GEMMs above (parDequantGemv*, parDequantGemm*:
+ * parallel.nim:186-474). */
 int lp_pool_dequant_gemv(lp_pool_t pool, const int8_t *wq, int64_t wq_len, const float *scales,
                          int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
                          float *y, int64_t y_len, lp_stream_t stream);
