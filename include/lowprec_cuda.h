@@ -204,11 +204,15 @@ int lp_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int6
 int lp_quantize_q8_0_split(const float *src, int64_t src_len, int8_t *qs, int64_t qs_len,
                            float *d, int64_t d_len, lp_stream_t stream);
 
-/* quantizeBatch: symmetric int8 encode q = toI8(x / scale) (divide, ties-away,
- * clamp [-128,127]); group_size <= 0 means one per-tensor scale.
- * Replaces simd/dequant.nim:1717-1750 (= quantize[I8], quant.nim:48-60). */
+/* quantizeBatch: int8 encode q = toI8(x / scales[g] + zero_points[g]) (divide,
+ * then add, ties-away round, clamp [-128,127]), g = i div group_size
+ * (group_size <= 0: one per-tensor scale).  zero_points_len = 0 is the
+ * symmetric case (QParams with an empty zeroPoint, + 0.0); otherwise it covers
+ * every group.  Replaces simd/dequant.nim:1717-1750 (proc quantizeBatch*,
+ * whose zero-point case falls through to quantize[I8], quant.nim:48-60). */
 int lp_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
-                      int64_t group_size, int8_t *dst, int64_t dst_len, lp_stream_t stream);
+                      const float *zero_points, int64_t zero_points_len, int64_t group_size,
+                      int8_t *dst, int64_t dst_len, lp_stream_t stream);
 
 /* dequantizeBatch: dst = (f32(q) - zero_points[g]) * scales[g], g = i div
  * group_size (group_size <= 0: per tensor), for int8-backed I8 and I4 values
@@ -286,15 +290,6 @@ int lph_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row, 
                           int64_t x_len, float *y, int64_t y_len);
 int lph_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
                           int64_t x_len, float *y, int64_t y_len);
-/* dequantGemvQ4_0 host form that allocates nothing: inputs and output are
- * staged in one static 32 MiB device array instead of the per-thread
- * workspace of lph_dequant_gemv_q4_0 (same arguments, same results).  No
- * counterpart in the reference.  LP_ERR_UNSUPPORTED when the staged bytes
- * (18 per block + 4 per x and y element, each rounded up to 256) exceed
- * 32 MiB.  The array is shared process-wide: overlapping calls race and must
- * be serialised by the caller. */
-int lph_dequant_gemv_q4_0_static(const void *w, int64_t w_len, int64_t blocks_per_row,
-                                 const float *x, int64_t x_len, float *y, int64_t y_len);
 int lph_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
                         int64_t w_scales_len, int64_t group_size, const int8_t *xq,
                         int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
@@ -318,10 +313,28 @@ int lph_dequant_gemm_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const flo
 int lph_quantize_q8_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len);
 int lph_quantize_q4_0_batch(const float *src, int64_t src_len, void *blocks, int64_t blocks_len);
 int lph_quantize_batch(const float *x, int64_t x_len, const float *scales, int64_t scales_len,
-                       int64_t group_size, int8_t *dst, int64_t dst_len);
+                       const float *zero_points, int64_t zero_points_len, int64_t group_size,
+                       int8_t *dst, int64_t dst_len);
 int lph_dequantize_batch(const int8_t *q, int64_t q_len, const float *scales, int64_t scales_len,
                          const float *zero_points, int64_t zero_points_len, int64_t group_size,
                          float *dst, int64_t dst_len);
+
+/* ======================= host form that allocates nothing ============== */
+/* No counterpart in the reference.  For callers that may not allocate device
+ * memory during a call (real-time callbacks, hosts with a memory budget fixed
+ * at start-up, embeddings that forbid cudaMalloc after initialisation):
+ * dequantGemvQ4_0 with host arrays, like lph_dequant_gemv_q4_0 (same
+ * arguments, same results), but its inputs and output are staged in one
+ * static 32 MiB device array that every GPU loading the library holds until
+ * exit, instead of a workspace grown with cudaMalloc.  No cudaMalloc, cudaFree
+ * or other allocating call is made.  Shape errors return LP_ERR_SHAPE before
+ * anything is copied; LP_ERR_UNSUPPORTED when the staged bytes (18 per block +
+ * 4 per x and y element, each rounded up to 256) exceed 32 MiB.  The first
+ * call on a device looks up the array's address (make it before any stream
+ * capture).  The array is shared process-wide: calls that overlap in time race
+ * on it and must be serialised by the caller. */
+int lph_dequant_gemv_q4_0_static(const void *w, int64_t w_len, int64_t blocks_per_row,
+                                 const float *x, int64_t x_len, float *y, int64_t y_len);
 
 /* ======================= LpPool: row-sharded forms across GPUs ======== *
  * One process (rank) per GPU of a box.  Rank r owns the rows
@@ -396,6 +409,77 @@ int lp_pool_dequant_gemm_i4q8(lp_pool_t pool, const uint8_t *wpacked, int64_t wp
                               const int8_t *xq, int64_t xq_len, const float *x_scales,
                               int64_t x_scales_len, int64_t n, float *y, int64_t y_len,
                               lp_stream_t stream);
+
+/* ======================= LpPool in one process, host arrays ========== *
+ * The reference's LpPool is one process with worker threads over host
+ * arrays.  Here a worker is a host thread bound to one GPU: a pooled call
+ * slices the rows as the reference does (per = rows div n, worker t owns
+ * [per*t, per*t + per), the last one the remainder; parallel.nim:118-124),
+ * each worker runs the host form (lph_*) of its slice on its GPU, and the
+ * slices of y come back into the caller's y.  Results equal the serial call
+ * bit for bit.  Blocking; not safe to call concurrently on one pool
+ * (parallel.nim:85-91). */
+typedef struct lph_pool *lph_pool_t;
+
+/* initPool(threads): a pool of `threads` GPUs (<= 0: every visible GPU;
+ * capped at the number visible), devices 0 .. n-1.  LP_ERR_NO_DEVICE without
+ * a GPU.  Replaces parallel.nim:134-151 (proc initPool*). */
+int lph_pool_init(lph_pool_t *pool, int threads);
+/* shutdown: stop the workers and free the pool; *pool becomes NULL, and a
+ * NULL pool is accepted (idempotent).  Replaces parallel.nim:153-167. */
+int lph_pool_shutdown(lph_pool_t *pool);
+/* threadCount: workers (GPUs) of the pool, 0 for NULL.  Replaces
+ * parallel.nim:169-171. */
+int lph_pool_thread_count(lph_pool_t pool);
+
+/* Pooled forms (serial fallback when the pool has one worker or fewer than
+ * 128 rows, parallel.nim:358-360).  Replace parDequantGemvQ8 /
+ * parDequantGemvI4Q8 (parallel.nim:346-374, pooled overloads) and
+ * parDequantGemmQ8 / parDequantGemmI4Q8 (parallel.nim:420-474). */
+int lph_pool_dequant_gemv_q8(lph_pool_t pool, const int8_t *wq, int64_t wq_len,
+                             const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                             const int8_t *xq, int64_t xq_len, const float *x_scales,
+                             int64_t x_scales_len, float *y, int64_t y_len);
+int lph_pool_dequant_gemv_i4q8(lph_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                               const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                               const int8_t *xq, int64_t xq_len, const float *x_scales,
+                               int64_t x_scales_len, float *y, int64_t y_len);
+int lph_pool_dequant_gemm_q8(lph_pool_t pool, const int8_t *wq, int64_t wq_len,
+                             const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                             const int8_t *xq, int64_t xq_len, const float *x_scales,
+                             int64_t x_scales_len, int64_t n, float *y, int64_t y_len);
+int lph_pool_dequant_gemm_i4q8(lph_pool_t pool, const uint8_t *wpacked, int64_t wpacked_len,
+                               const float *w_scales, int64_t w_scales_len, int64_t group_size,
+                               const int8_t *xq, int64_t xq_len, const float *x_scales,
+                               int64_t x_scales_len, int64_t n, float *y, int64_t y_len);
+
+/* Per-call forms par*(..., threads): shards = min(threads, rows div 64), at
+ * least 1, threads <= 0 meaning every GPU (shardCount, parallel.nim:45-53),
+ * over one pool of every visible GPU made on first use; one shard runs the
+ * serial host form.  Replace parallel.nim:186-418 (parDequantGemv,
+ * parDequantGemvI4, parDequantGemvF4, parDequantGemvQ8_0, parDequantGemvQ4_0,
+ * and the per-call overloads of parDequantGemvQ8 / parDequantGemvI4Q8). */
+int lph_par_dequant_gemv(const int8_t *wq, int64_t wq_len, const float *scales,
+                         int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                         float *y, int64_t y_len, int threads);
+int lph_par_dequant_gemv_i4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                            int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                            float *y, int64_t y_len, int threads);
+int lph_par_dequant_gemv_f4(const uint8_t *wpacked, int64_t wpacked_len, const float *scales,
+                            int64_t scales_len, int64_t group_size, const float *x, int64_t x_len,
+                            float *y, int64_t y_len, int threads);
+int lph_par_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row,
+                              const float *x, int64_t x_len, float *y, int64_t y_len, int threads);
+int lph_par_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row,
+                              const float *x, int64_t x_len, float *y, int64_t y_len, int threads);
+int lph_par_dequant_gemv_q8(const int8_t *wq, int64_t wq_len, const float *w_scales,
+                            int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                            int64_t xq_len, const float *x_scales, int64_t x_scales_len, float *y,
+                            int64_t y_len, int threads);
+int lph_par_dequant_gemv_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                              int64_t w_scales_len, int64_t group_size, const int8_t *xq,
+                              int64_t xq_len, const float *x_scales, int64_t x_scales_len,
+                              float *y, int64_t y_len, int threads);
 
 #ifdef __cplusplus
 }

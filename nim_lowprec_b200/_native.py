@@ -48,7 +48,7 @@ SIGNATURES = {
     "lp_quantize_q8_0_batch": "pnpnp",
     "lp_quantize_q4_0_batch": "pnpnp",
     "lp_quantize_q8_0_split": "pnpnpnp",
-    "lp_quantize_batch": "pnpnnpnp",
+    "lp_quantize_batch": "pnpnpnnpnp",
     "lp_host_device_pointer": "pp",
     "lp_quantize_dequant_gemv_q8": "pnpnnpnpnp",
     "lp_quantize_dequant_gemv_i4q8": "pnpnnpnpnp",
@@ -78,7 +78,7 @@ SIGNATURES = {
     "lph_dequant_gemm_i4q8": "pnpnnpnpnnpn",
     "lph_quantize_q8_0_batch": "pnpn",
     "lph_quantize_q4_0_batch": "pnpn",
-    "lph_quantize_batch": "pnpnnpn",
+    "lph_quantize_batch": "pnpnpnnpn",
     "lph_dequantize_batch": "pnpnpnnpn",
     "lp_set_fp32_mode": "i",
     "lp_get_fp32_mode": "",
@@ -99,6 +99,20 @@ SIGNATURES = {
     "lp_pool_dequant_gemv_i4q8": "ppnpnnpnpnpnp",
     "lp_pool_dequant_gemm_q8": "ppnpnnpnpnnpnp",
     "lp_pool_dequant_gemm_i4q8": "ppnpnnpnpnnpnp",
+    "lph_pool_init": "pi",
+    "lph_pool_shutdown": "p",
+    "lph_pool_thread_count": "p",
+    "lph_pool_dequant_gemv_q8": "ppnpnnpnpnpn",
+    "lph_pool_dequant_gemv_i4q8": "ppnpnnpnpnpn",
+    "lph_pool_dequant_gemm_q8": "ppnpnnpnpnnpn",
+    "lph_pool_dequant_gemm_i4q8": "ppnpnnpnpnnpn",
+    "lph_par_dequant_gemv": "pnpnnpnpni",
+    "lph_par_dequant_gemv_i4": "pnpnnpnpni",
+    "lph_par_dequant_gemv_f4": "pnpnnpnpni",
+    "lph_par_dequant_gemv_q8_0": "pnnpnpni",
+    "lph_par_dequant_gemv_q4_0": "pnnpnpni",
+    "lph_par_dequant_gemv_q8": "pnpnnpnpnpni",
+    "lph_par_dequant_gemv_i4q8": "pnpnnpnpnpni",
 }
 
 

@@ -62,6 +62,14 @@ namespace {
 // checks only, so a bad call fails before any device work or allocation.
 thread_local bool t_validate_only = false;
 
+}  // namespace
+
+namespace lp {
+void set_validate_only(bool on) { t_validate_only = on; }
+}  // namespace lp
+
+namespace {
+
 #define LP_VALIDATED()                   \
   do {                                   \
     if (t_validate_only) return LP_OK;   \
@@ -393,13 +401,18 @@ int lp_quantize_q8_0_split(const float* src, int64_t src_len, int8_t* qs, int64_
 static int64_t num_groups(int64_t n, int64_t gs) { return gs > 0 ? (n + gs - 1) / gs : 1; }
 
 int lp_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
-                      int64_t group_size, int8_t* dst, int64_t dst_len, lp_stream_t stream) {
+                      const float* zero_points, int64_t zero_points_len, int64_t group_size,
+                      int8_t* dst, int64_t dst_len, lp_stream_t stream) {
+  const int64_t groups = x_len ? num_groups(x_len, group_size) : 0;
   LP_REQUIRE(x_len >= 0 && x_len == dst_len);
-  LP_REQUIRE(scales_len >= (x_len ? num_groups(x_len, group_size) : 0));
-  if (bad(x, x_len) || bad(scales, scales_len) || bad(dst, dst_len)) return LP_ERR_ARG;
+  LP_REQUIRE(scales_len >= groups);
+  LP_REQUIRE(zero_points_len == 0 || zero_points_len >= groups);
+  if (bad(x, x_len) || bad(scales, scales_len) || bad(zero_points, zero_points_len) ||
+      bad(dst, dst_len))
+    return LP_ERR_ARG;
   LP_VALIDATED();
-  return lp::launch_quantize_batch(x, x_len, scales, group_size > 0 ? group_size : 0, dst,
-                                   S(stream));
+  return lp::launch_quantize_batch(x, x_len, scales, zero_points_len ? zero_points : nullptr,
+                                   group_size > 0 ? group_size : 0, dst, S(stream));
 }
 
 int lp_dequantize_batch(const int8_t* q, int64_t q_len, const float* scales, int64_t scales_len,
@@ -716,13 +729,17 @@ int lph_quantize_q4_0_batch(const float* src, int64_t src_len, void* blocks, int
 }
 
 int lph_quantize_batch(const float* x, int64_t x_len, const float* scales, int64_t scales_len,
-                       int64_t group_size, int8_t* dst, int64_t dst_len) {
-  Seg sx{x, nb<float>(x_len)}, ss{scales, nb<float>(scales_len)}, sd{nullptr, nb<int8_t>(dst_len)};
-  LPH_PRECHECK(lp_quantize_batch(x, x_len, scales, scales_len, group_size, dst, dst_len, nullptr));
-  int st = stage_in({&sx, &ss, &sd});
+                       const float* zero_points, int64_t zero_points_len, int64_t group_size,
+                       int8_t* dst, int64_t dst_len) {
+  Seg sx{x, nb<float>(x_len)}, ss{scales, nb<float>(scales_len)},
+      sz{zero_points, nb<float>(zero_points_len)}, sd{nullptr, nb<int8_t>(dst_len)};
+  LPH_PRECHECK(lp_quantize_batch(x, x_len, scales, scales_len, zero_points, zero_points_len,
+                                 group_size, dst, dst_len, nullptr));
+  int st = stage_in({&sx, &ss, &sz, &sd});
   if (st != LP_OK) return st;
   st = lp_quantize_batch(static_cast<const float*>(sx.dev), x_len,
-                         static_cast<const float*>(ss.dev), scales_len, group_size,
+                         static_cast<const float*>(ss.dev), scales_len,
+                         static_cast<const float*>(sz.dev), zero_points_len, group_size,
                          static_cast<int8_t*>(sd.dev), dst_len, t_stage.stream);
   return stage_out(dst, sd, st);
 }

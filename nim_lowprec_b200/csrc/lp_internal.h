@@ -69,8 +69,8 @@ int launch_copy_in(void* dst, const void* src, int64_t bytes, cudaStream_t st);
 int launch_quantize_q8_0(const float* src, int64_t n, uint8_t* blocks, int8_t* qs, float* d,
                          cudaStream_t st);
 int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStream_t st);
-int launch_quantize_batch(const float* x, int64_t n, const float* scales, int64_t gs,
-                          int8_t* dst, cudaStream_t st);
+int launch_quantize_batch(const float* x, int64_t n, const float* scales, const float* zp,
+                          int64_t gs, int8_t* dst, cudaStream_t st);
 int launch_dequantize_batch(const int8_t* q, int64_t n, const float* scales, const float* zp,
                             int64_t gs, float* dst, cudaStream_t st);
 int launch_calibrate(const float* x, int64_t n, int64_t gs, float qmax, int mx_emax, int mx,
@@ -96,6 +96,10 @@ int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, co
 unsigned int take_error_gemv();
 unsigned int take_error_gemm_tc();
 unsigned int take_error_pool();
+
+// While on (this thread only), the lp_* entry points run their shape and
+// argument checks and return without launching anything (capi.cu).
+void set_validate_only(bool on);
 
 // Records the CUDA error text for lp_last_error_detail() and maps to a status.
 void note_cuda_error(cudaError_t e);

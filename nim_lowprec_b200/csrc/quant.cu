@@ -159,15 +159,20 @@ __global__ void k_quantize_q4_0(const float* __restrict__ src, int64_t nblocks,
   }
 }
 
-// quant.nim:48-60 (quantizeBatch, simd/dequant.nim:1717-1750):
-// toI8(x / scale): round half away, clamp [-128, 127].
+// quant.nim:48-60 (quantizeBatch, simd/dequant.nim:1717-1750, whose
+// zero-point case falls through to this scalar quantize):
+// toI8(x / scale + zeroPoint): round half away, clamp [-128, 127]; the
+// symmetric case adds 0.0 (zp null).
 __global__ void k_quantize_batch(const float* __restrict__ x, int64_t n,
-                                 const float* __restrict__ scales, int64_t gs,
+                                 const float* __restrict__ scales,
+                                 const float* __restrict__ zp, int64_t gs,
                                  int8_t* __restrict__ dst) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float s = scales[gs > 0 ? i / gs : 0];
-    float r = roundf(__fadd_rn(__fdiv_rn(x[i], s), 0.0f));
+    const int64_t g = gs > 0 ? i / gs : 0;
+    const float s = scales[g];
+    const float z = zp ? zp[g] : 0.0f;
+    float r = roundf(__fadd_rn(__fdiv_rn(x[i], s), z));
     r = fminf(fmaxf(r, -128.0f), 127.0f);
     dst[i] = static_cast<int8_t>(static_cast<int>(r));
   }
@@ -620,10 +625,10 @@ int launch_quantize_q4_0(const float* src, int64_t n, uint8_t* blocks, cudaStrea
   return cuda_status(cudaGetLastError());
 }
 
-int launch_quantize_batch(const float* x, int64_t n, const float* scales, int64_t gs,
-                          int8_t* dst, cudaStream_t st) {
+int launch_quantize_batch(const float* x, int64_t n, const float* scales, const float* zp,
+                          int64_t gs, int8_t* dst, cudaStream_t st) {
   if (n == 0) return LP_OK;
-  k_quantize_batch<<<grid_for(n, kThreads), kThreads, 0, st>>>(x, n, scales, gs, dst);
+  k_quantize_batch<<<grid_for(n, kThreads), kThreads, 0, st>>>(x, n, scales, zp, gs, dst);
   return cuda_status(cudaGetLastError());
 }
 

@@ -284,14 +284,18 @@ quantizeQ8_0 = quantizeQ8_0Batch
 quantizeQ4_0 = quantizeQ4_0Batch
 
 
-def quantizeBatch(x, scales, groupSize, dst):
-    """simd/dequant.nim:1717-1750: dst = toI8(x / scale); groupSize <= 0 is
-    per-tensor (QParams.scheme = qPerTensor)."""
-    mode = _mode(x, scales, dst)
+def quantizeBatch(x, scales, groupSize, dst, zeroPoint=None):
+    """simd/dequant.nim:1717-1750 (and its scalar fall-through quant.nim:48-60):
+    dst = toI8(x / scale[g] + zeroPoint[g]); ``zeroPoint`` None (or empty) is
+    the symmetric case (+ 0.0), groupSize <= 0 per tensor (QParams.scheme =
+    qPerTensor)."""
+    mode = _mode(x, scales, dst, zeroPoint)
     _check_dtype(x, np.float32, "x"); _check_dtype(scales, np.float32, "scales")
     _check_dtype(dst, np.int8, "dst")
+    if zeroPoint is not None:
+        _check_dtype(zeroPoint, np.float32, "zeroPoint")
     _call(mode, "quantize_batch", _ptr(x), _numel(x), _ptr(scales), _numel(scales),
-          int(groupSize), _ptr(dst), _numel(dst))
+          _ptr(zeroPoint), _numel(zeroPoint), int(groupSize), _ptr(dst), _numel(dst))
 
 
 def dequantizeBatch(q, scales, groupSize, dst, zeroPoint=None):

@@ -59,7 +59,8 @@ proc lph_quantize_q8_0_batch(src: pointer, srcLen: int64, blocks: pointer,
 proc lph_quantize_q4_0_batch(src: pointer, srcLen: int64, blocks: pointer,
     blocksLen: int64): cint {.importc, dynlib: lpLib.}
 proc lph_quantize_batch(x: pointer, xLen: int64, scales: pointer, scalesLen: int64,
-    gs: int64, dst: pointer, dstLen: int64): cint {.importc, dynlib: lpLib.}
+    zp: pointer, zpLen: int64, gs: int64, dst: pointer, dstLen: int64): cint {.
+    importc, dynlib: lpLib.}
 proc lph_dequantize_batch(q: pointer, qLen: int64, scales: pointer, scalesLen: int64,
     zp: pointer, zpLen: int64, gs: int64, dst: pointer, dstLen: int64): cint {.
     importc, dynlib: lpLib.}
@@ -156,12 +157,12 @@ proc groupOf(p: QParams): int64 =
   if p.scheme == qPerTensor: 0'i64 else: p.groupSize.int64
 
 proc quantizeBatch*(x: openArray[float32], p: QParams, dst: var openArray[I8]) =
-  ## The symmetric case, as the reference's vector form; QParams with zero
-  ## points are refused (the reference runs its scalar `quantize` for them).
-  if p.zeroPoint.len > 0:
-    raise newException(LowprecCudaError, "quantizeBatch: QParams with zero points")
-  check(lph_quantize_batch(base(x), x.len, base(p.scale), p.scale.len, groupOf(p),
-      base(dst), dst.len), "quantizeBatch")
+  ## toI8(x / scale + zeroPoint) per group: the reference's vector form for
+  ## symmetric QParams and its scalar `quantize` fall-through for QParams with
+  ## zero points, both in one kernel.
+  check(lph_quantize_batch(base(x), x.len, base(p.scale), p.scale.len,
+      base(p.zeroPoint), p.zeroPoint.len, groupOf(p), base(dst), dst.len),
+      "quantizeBatch")
 
 template defDequantizeBatch(T: untyped) =
   proc dequantizeBatch*(q: openArray[T], p: QParams, dst: var openArray[float32]) =
@@ -172,3 +173,128 @@ template defDequantizeBatch(T: untyped) =
 
 defDequantizeBatch(I8)
 defDequantizeBatch(I4)
+
+# ---- LpPool over this box's GPUs (parallel.nim:82-474) ----
+#
+# The reference's pool is one process with a worker per core; this one has a
+# worker per GPU.  Same procs and meaning: initPool(threads) (threads <= 0:
+# every GPU), shutdown (idempotent), threadCount (0 after shutdown), the
+# pooled int8-activation GEMV / GEMM forms, and the per-call par* forms with
+# a `threads` count.  Results equal the serial calls bit for bit.
+
+type LpPool* = object
+  h: pointer
+
+proc lph_pool_init(pool: ptr pointer, threads: cint): cint {.importc, dynlib: lpLib.}
+proc lph_pool_shutdown(pool: ptr pointer): cint {.importc, dynlib: lpLib.}
+proc lph_pool_thread_count(pool: pointer): cint {.importc, dynlib: lpLib.}
+proc lph_pool_dequant_gemv_q8(pool: pointer, wq: pointer, wqLen: int64, ws: pointer,
+    wsLen: int64, gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_pool_dequant_gemv_i4q8(pool: pointer, w: pointer, wLen: int64, ws: pointer,
+    wsLen: int64, gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_pool_dequant_gemm_q8(pool: pointer, wq: pointer, wqLen: int64, ws: pointer,
+    wsLen: int64, gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, n: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_pool_dequant_gemm_i4q8(pool: pointer, w: pointer, wLen: int64, ws: pointer,
+    wsLen: int64, gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, n: int64,
+    y: pointer, yLen: int64): cint {.importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv(wq: pointer, wqLen: int64, scales: pointer, scalesLen: int64,
+    gs: int64, x: pointer, xLen: int64, y: pointer, yLen: int64, threads: cint): cint {.
+    importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_i4(w: pointer, wLen: int64, scales: pointer, scalesLen: int64,
+    gs: int64, x: pointer, xLen: int64, y: pointer, yLen: int64, threads: cint): cint {.
+    importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_f4(w: pointer, wLen: int64, scales: pointer, scalesLen: int64,
+    gs: int64, x: pointer, xLen: int64, y: pointer, yLen: int64, threads: cint): cint {.
+    importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_q8_0(w: pointer, wLen: int64, bpr: int64, x: pointer,
+    xLen: int64, y: pointer, yLen: int64, threads: cint): cint {.importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_q4_0(w: pointer, wLen: int64, bpr: int64, x: pointer,
+    xLen: int64, y: pointer, yLen: int64, threads: cint): cint {.importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_q8(wq: pointer, wqLen: int64, ws: pointer, wsLen: int64,
+    gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, y: pointer,
+    yLen: int64, threads: cint): cint {.importc, dynlib: lpLib.}
+proc lph_par_dequant_gemv_i4q8(w: pointer, wLen: int64, ws: pointer, wsLen: int64,
+    gs: int64, xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, y: pointer,
+    yLen: int64, threads: cint): cint {.importc, dynlib: lpLib.}
+
+proc initPool*(threads = 0): LpPool =
+  ## Workers = `threads` GPUs (default: every visible GPU).  Call `shutdown`.
+  check(lph_pool_init(addr result.h, threads.cint), "initPool")
+
+proc shutdown*(p: var LpPool) =
+  ## Stop the workers and free the pool.  Idempotent.
+  check(lph_pool_shutdown(addr p.h), "shutdown")
+
+proc threadCount*(p: LpPool): int =
+  ## Workers in this pool, 0 if it was never initialized or is shut down.
+  lph_pool_thread_count(p.h).int
+
+proc parDequantGemvQ8*(pool: var LpPool, wq: openArray[I8], wScales: openArray[float32],
+    groupSize: int, xq: openArray[I8], xScales: openArray[float32],
+    y: var openArray[float32]) =
+  check(lph_pool_dequant_gemv_q8(pool.h, base(wq), wq.len, base(wScales), wScales.len,
+      groupSize, base(xq), xq.len, base(xScales), xScales.len, base(y), y.len),
+      "parDequantGemvQ8")
+
+proc parDequantGemvI4Q8*(pool: var LpPool, wpacked: openArray[byte],
+    wScales: openArray[float32], groupSize: int, xq: openArray[I8],
+    xScales: openArray[float32], y: var openArray[float32]) =
+  check(lph_pool_dequant_gemv_i4q8(pool.h, base(wpacked), wpacked.len, base(wScales),
+      wScales.len, groupSize, base(xq), xq.len, base(xScales), xScales.len, base(y), y.len),
+      "parDequantGemvI4Q8")
+
+proc parDequantGemmQ8*(pool: var LpPool, wq: openArray[I8], wScales: openArray[float32],
+    groupSize: int, xq: openArray[I8], xScales: openArray[float32], n: int,
+    y: var openArray[float32]) =
+  check(lph_pool_dequant_gemm_q8(pool.h, base(wq), wq.len, base(wScales), wScales.len,
+      groupSize, base(xq), xq.len, base(xScales), xScales.len, n, base(y), y.len),
+      "parDequantGemmQ8")
+
+proc parDequantGemmI4Q8*(pool: var LpPool, wpacked: openArray[byte],
+    wScales: openArray[float32], groupSize: int, xq: openArray[I8],
+    xScales: openArray[float32], n: int, y: var openArray[float32]) =
+  check(lph_pool_dequant_gemm_i4q8(pool.h, base(wpacked), wpacked.len, base(wScales),
+      wScales.len, groupSize, base(xq), xq.len, base(xScales), xScales.len, n, base(y),
+      y.len), "parDequantGemmI4Q8")
+
+proc parDequantGemv*(wq: openArray[I8], scales: openArray[float32], groupSize: int,
+    x: openArray[float32], y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv(base(wq), wq.len, base(scales), scales.len, groupSize,
+      base(x), x.len, base(y), y.len, threads.cint), "parDequantGemv")
+
+proc parDequantGemvI4*(wpacked: openArray[byte], scales: openArray[float32],
+    groupSize: int, x: openArray[float32], y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv_i4(base(wpacked), wpacked.len, base(scales), scales.len,
+      groupSize, base(x), x.len, base(y), y.len, threads.cint), "parDequantGemvI4")
+
+proc parDequantGemvF4*(wpacked: openArray[byte], scales: openArray[float32],
+    groupSize: int, x: openArray[float32], y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv_f4(base(wpacked), wpacked.len, base(scales), scales.len,
+      groupSize, base(x), x.len, base(y), y.len, threads.cint), "parDequantGemvF4")
+
+proc parDequantGemvQ8_0*(w: openArray[BlockQ8_0], blocksPerRow: int,
+    x: openArray[float32], y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv_q8_0(base(w), w.len, blocksPerRow, base(x), x.len, base(y),
+      y.len, threads.cint), "parDequantGemvQ8_0")
+
+proc parDequantGemvQ4_0*(w: openArray[BlockQ4_0], blocksPerRow: int,
+    x: openArray[float32], y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv_q4_0(base(w), w.len, blocksPerRow, base(x), x.len, base(y),
+      y.len, threads.cint), "parDequantGemvQ4_0")
+
+proc parDequantGemvQ8*(wq: openArray[I8], wScales: openArray[float32], groupSize: int,
+    xq: openArray[I8], xScales: openArray[float32], y: var openArray[float32],
+    threads = 0) =
+  check(lph_par_dequant_gemv_q8(base(wq), wq.len, base(wScales), wScales.len, groupSize,
+      base(xq), xq.len, base(xScales), xScales.len, base(y), y.len, threads.cint),
+      "parDequantGemvQ8")
+
+proc parDequantGemvI4Q8*(wpacked: openArray[byte], wScales: openArray[float32],
+    groupSize: int, xq: openArray[I8], xScales: openArray[float32],
+    y: var openArray[float32], threads = 0) =
+  check(lph_par_dequant_gemv_i4q8(base(wpacked), wpacked.len, base(wScales), wScales.len,
+      groupSize, base(xq), xq.len, base(xScales), xScales.len, base(y), y.len,
+      threads.cint), "parDequantGemvI4Q8")

@@ -8,14 +8,20 @@ depends only on its own weight row, so a sharded call gives the serial bits.
 
 * ``Pool(group)`` gathers the row slices of y with ``torch.distributed``
   (NCCL for CUDA tensors; any backend works, gloo included).
-* ``NcclPool(group, device)`` is the C-ABI pool (``lp_pool_*``): the library
-  runs the local slice and gathers y itself with one NCCL group of per-rank
-  broadcasts -- the form a Nim program uses through the shim.
+* ``NcclPool(group, device)`` is the C-ABI pool of one process per GPU
+  (``lp_pool_*``): the library runs the local slice and assembles y on every
+  rank itself, over NVLink peer stores (or an NCCL group of broadcasts).
+* ``LocalPool(threads)`` is the reference's own shape of pool -- one process,
+  one worker per GPU, host arrays (``lph_pool_*`` / ``lph_par_*``): every
+  worker runs its row slice on its GPU and writes its rows of the caller's
+  host y.  This is the form the Nim shim binds (``initPool``, ``shutdown``,
+  ``threadCount``, the pooled and per-call ``par*`` procs).
 
-The ``par*`` procs take the reference's arguments.  The weight arrays are
-either whole (the reference's call: each rank slices its rows) or, with
-``sharded=True``, already this rank's slice (weights resident per GPU).
-Activations and ``y`` are whole; every rank ends with all of ``y``.
+The ``par*`` procs take the reference's arguments.  For the multi-process
+pools the weight arrays are either whole (the reference's call: each rank
+slices its rows) or, with ``sharded=True``, already this rank's slice
+(weights resident per GPU); activations and ``y`` are whole and every rank
+ends with all of ``y``.  For ``LocalPool`` every array is a whole host array.
 """
 from __future__ import annotations
 
@@ -158,9 +164,111 @@ class NcclPool:
             pass
 
 
+class LocalPool:
+    """initPool(threads) of the reference (parallel.nim:134-171) over this
+    box's GPUs in one process: ``threads`` workers, one per GPU (<= 0: every
+    visible GPU).  ``shutdown`` is idempotent; ``threadCount`` is 0 after it."""
+
+    def __init__(self, threads: int = 0):
+        self._h = ctypes.c_void_p()
+        N.check(N.lib().lph_pool_init(ctypes.byref(self._h), int(threads)), "lph_pool_init")
+
+    def threadCount(self) -> int:
+        return int(N.lib().lph_pool_thread_count(self._h))
+
+    def shutdown(self):
+        N.check(N.lib().lph_pool_shutdown(ctypes.byref(self._h)), "lph_pool_shutdown")
+
+    def call(self, name: str, *args):
+        N.check(getattr(N.lib(), name)(self._h, *args), name)
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.shutdown()
+        except Exception:
+            pass
+
+
 def initPool(group=None, nccl: bool = False, device: int | None = None):
     """initPool (parallel.nim:134-151): this process's member of the pool."""
     return NcclPool(group, device) if nccl else Pool(group)
+
+
+def _hp(a):
+    a = np.ascontiguousarray(a)
+    return a, (a.ctypes.data_as(ctypes.c_void_p) if a.size else None)
+
+
+def _host_par(name, w, sc, gs, x, y, threads, wdt, blocks=None):
+    """lph_par_* over host arrays: the per-call par* procs (parallel.nim:186-418)."""
+    w, pw = _hp(w)
+    x, px = _hp(x)
+    if not (isinstance(y, np.ndarray) and y.flags.c_contiguous and y.dtype == np.float32):
+        raise TypeError("y must be a contiguous float32 numpy array")
+    py = y.ctypes.data_as(ctypes.c_void_p) if y.size else None
+    if blocks is not None:
+        N.check(getattr(N.lib(), name)(pw, w.size // blocks, int(gs), px, x.size, py, y.size,
+                                       int(threads)), name)
+        return
+    sc, ps = _hp(sc)
+    N.check(getattr(N.lib(), name)(pw, w.size, ps, sc.size, int(gs), px, x.size, py, y.size,
+                                   int(threads)), name)
+
+
+def parDequantGemvThreads(wq, scales, groupSize, x, y, threads=0):
+    """parDequantGemv(..., threads) (parallel.nim:186-253) on this box's GPUs."""
+    _host_par("lph_par_dequant_gemv", wq, scales, groupSize, x, y, threads, np.int8)
+
+
+def parDequantGemvI4Threads(wpacked, scales, groupSize, x, y, threads=0):
+    """parDequantGemvI4(..., threads) (parallel.nim:186-255)."""
+    _host_par("lph_par_dequant_gemv_i4", wpacked, scales, groupSize, x, y, threads, np.uint8)
+
+
+def parDequantGemvF4Threads(wpacked, scales, groupSize, x, y, threads=0):
+    """parDequantGemvF4(..., threads) (parallel.nim:186-257)."""
+    _host_par("lph_par_dequant_gemv_f4", wpacked, scales, groupSize, x, y, threads, np.uint8)
+
+
+def parDequantGemvQ8_0Threads(w, blocksPerRow, x, y, threads=0):
+    """parDequantGemvQ8_0(..., threads) (parallel.nim:260-307); w: Q8_0 block bytes."""
+    _host_par("lph_par_dequant_gemv_q8_0", np.asarray(w).reshape(-1).view(np.uint8), None,
+              blocksPerRow, x, y, threads, np.uint8, blocks=34)
+
+
+def parDequantGemvQ4_0Threads(w, blocksPerRow, x, y, threads=0):
+    """parDequantGemvQ4_0(..., threads) (parallel.nim:260-308); w: Q4_0 block bytes."""
+    _host_par("lph_par_dequant_gemv_q4_0", np.asarray(w).reshape(-1).view(np.uint8), None,
+              blocksPerRow, x, y, threads, np.uint8, blocks=18)
+
+
+def _host_q8(name, pool, w, ws, gs, xq, xs, y, threads=None, n=None):
+    w, pw = _hp(w)
+    ws, pws = _hp(ws)
+    xq, pxq = _hp(xq)
+    xs, pxs = _hp(xs)
+    if not (isinstance(y, np.ndarray) and y.flags.c_contiguous and y.dtype == np.float32):
+        raise TypeError("y must be a contiguous float32 numpy array")
+    py = y.ctypes.data_as(ctypes.c_void_p) if y.size else None
+    args = [pw, w.size, pws, ws.size, int(gs), pxq, xq.size, pxs, xs.size]
+    if n is not None:
+        args.append(int(n))
+    args += [py, y.size]
+    if pool is not None:
+        pool.call(name, *args)
+    else:
+        N.check(getattr(N.lib(), name)(*args, int(threads)), name)
+
+
+def parDequantGemvQ8Threads(wq, wScales, groupSize, xq, xScales, y, threads=0):
+    """The per-call parDequantGemvQ8 overload (parallel.nim:376-415)."""
+    _host_q8("lph_par_dequant_gemv_q8", None, wq, wScales, groupSize, xq, xScales, y, threads)
+
+
+def parDequantGemvI4Q8Threads(wpacked, wScales, groupSize, xq, xScales, y, threads=0):
+    """The per-call parDequantGemvI4Q8 overload (parallel.nim:376-418)."""
+    _host_q8("lph_par_dequant_gemv_i4q8", None, wpacked, wScales, groupSize, xq, xScales, y,
+             threads)
 
 
 # ------------------------------------------------------------ par* procs --
@@ -236,6 +344,9 @@ def parDequantGemvQ4_0(pool, w, blocksPerRow, x, y, sharded=False):
 
 
 def _q8(pool, name, fn, w, wScales, groupSize, xq, xScales, y, sharded):
+    if isinstance(pool, LocalPool):
+        return _host_q8(name.replace("lp_pool_", "lph_pool_"), pool, w, wScales, groupSize, xq,
+                        xScales, y)
     m = _numel(y)
     wl, sl = _w(pool, w, m, sharded), _w(pool, wScales, m, sharded)
     if isinstance(pool, NcclPool):
@@ -257,6 +368,9 @@ def parDequantGemvI4Q8(pool, wpacked, wScales, groupSize, xq, xScales, y, sharde
 
 
 def _gemm(pool, name, fn, w, wScales, groupSize, xq, xScales, n, y, sharded):
+    if isinstance(pool, LocalPool):
+        return _host_q8(name.replace("lp_pool_", "lph_pool_"), pool, w, wScales, groupSize, xq,
+                        xScales, y, n=n)
     m = _numel(y) // n
     wl, sl = _w(pool, w, m, sharded), _w(pool, wScales, m, sharded)
     if isinstance(pool, NcclPool):

@@ -69,7 +69,7 @@ def lib():
         L.lpo_calibrate_mx.restype = i64
         L.lpo_calibrate_mx.argtypes = [vp, i64, i64, ctypes.c_int, vp]
         L.lpo_quantize.argtypes = [vp, i64, vp, i64, ctypes.c_int, vp]
-        L.lpo_quantize_batch.argtypes = [vp, i64, vp, i64, vp]
+        L.lpo_quantize_batch.argtypes = [vp, i64, vp, vp, i64, vp]
         L.lpo_dequantize_batch.argtypes = [vp, i64, vp, vp, i64, vp]
         L.lpo_pack_int4.argtypes = [vp, i64, vp]
         L.lpo_pack_f4.argtypes = [vp, i64, vp]
@@ -159,11 +159,15 @@ def quantize(x, scales, groupSize: int, kind: str) -> np.ndarray:
     return out.view(np.uint8) if kind == "f4" else out
 
 
-def quantizeBatch(x, scales, groupSize: int) -> np.ndarray:
+def quantizeBatch(x, scales, groupSize: int, zeroPoint=None) -> np.ndarray:
+    """toI8(x / scale[g] + zeroPoint[g]) (simd/dequant.nim:1717-1750 =
+    quant.nim:48-60); ``zeroPoint`` None is symmetric (+ 0.0)."""
     x = _c(x, np.float32)
     scales = _c(scales, np.float32)
+    zp = None if zeroPoint is None or np.size(zeroPoint) == 0 else _c(zeroPoint, np.float32)
     out = np.empty(x.size, np.int8)
-    lib().lpo_quantize_batch(_p(x), x.size, _p(scales), groupSize, _p(out))
+    lib().lpo_quantize_batch(_p(x), x.size, _p(scales), _p(zp) if zp is not None else None,
+                             groupSize, _p(out))
     return out
 
 

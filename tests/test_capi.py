@@ -144,3 +144,26 @@ def test_nim_shim_binds_only_exported_symbols():
     for name in names:
         assert hasattr(L, name), name
         assert re.search(r"\b" + name + r"\s*\(", header), name
+
+
+def test_local_pool_handles_without_a_gpu():
+    """initPool / shutdown / threadCount (parallel.nim:134-171) at the C ABI:
+    shutdown of a null pool is a no-op (idempotent), threadCount of it is 0,
+    and without a GPU initPool reports LP_ERR_NO_DEVICE instead of failing
+    later.  The per-call forms check shapes before looking for a device."""
+    import ctypes
+    import torch
+    lib = N.lib()
+    h = ctypes.c_void_p()
+    assert lib.lph_pool_shutdown(ctypes.byref(h)) == N.LP_OK
+    assert lib.lph_pool_shutdown(None) == N.LP_OK
+    assert lib.lph_pool_thread_count(None) == 0
+    y = (ctypes.c_float * 3)()
+    x = (ctypes.c_float * 64)()
+    w = (ctypes.c_int8 * (3 * 64))()
+    s = (ctypes.c_float * 6)()
+    # 3 rows of 64 int8 weights need 3 * 2 scales at group 32: 5 is a shape error
+    assert lib.lph_par_dequant_gemv(w, 3 * 64, s, 5, 32, x, 64, y, 3, 0) == N.LP_ERR_SHAPE
+    if not torch.cuda.is_available():
+        assert lib.lph_pool_init(ctypes.byref(h), 2) == N.LP_ERR_NO_DEVICE
+        assert lib.lph_par_dequant_gemv(w, 3 * 64, s, 6, 32, x, 64, y, 3, 0) == N.LP_ERR_NO_DEVICE

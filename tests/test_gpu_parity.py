@@ -195,6 +195,16 @@ def test_quantize_batch_and_calibrate_vs_oracle(n, gs):
     qh = np.empty(n, np.int8)
     L.quantizeBatch(x, sc_o, gs, qh)
     assert np.array_equal(qh, O.quantizeBatch(x, sc_o, gs))
+    # QParams with zero points: the reference's scalar quantize fall-through,
+    # toI8(x / scale + zeroPoint), clamped (quant.nim:48-60)
+    zp = ((np.arange(sc_o.size, dtype=F) % 7) * F(9.5) - F(30.0)).astype(F)
+    want = O.quantizeBatch(x, sc_o, gs, zp)
+    assert want.min() == -128 and want.max() == 127  # both clamps reached
+    (zd,) = to_dev(zp)
+    L.quantizeBatch(xd, sc, gs, q, zd)
+    assert np.array_equal(to_host(q), want)
+    L.quantizeBatch(x, sc_o, gs, qh, zp)
+    assert np.array_equal(qh, want)
 
 
 @pytest.mark.parametrize("n,gs,asym,off", [

@@ -1,11 +1,13 @@
 """LpPool's row-sharded forms on several GPUs (one process per GPU, NCCL).
 
-Skipped unless at least two GPUs are visible.  Every rank computes the whole
-result on its own GPU with the ordinary entry points, then the pooled forms --
-``Pool`` (torch.distributed gather) and ``NcclPool`` (the C-ABI pool, NCCL
-inside the library) -- and the two must agree bit for bit: sharded == serial
+Skipped unless at least two GPUs are visible; runs one rank per visible GPU
+(up to 8).  Every rank computes the whole result on its own GPU with the
+ordinary entry points, then the pooled forms -- ``Pool`` (torch.distributed
+gather) and ``NcclPool`` (the C-ABI pool: NVLink peer stores from the GEMV,
+or an NCCL group) -- and the two must agree bit for bit: sharded == serial
 (test_parallel.nim), with an uneven row count so the last rank takes the
-remainder.
+remainder, and the reference test's own cases (300 / 64 / 1 rows, so some
+ranks hold no rows at all) for every pooled GEMV form.
 """
 import os
 import socket
@@ -88,6 +90,47 @@ def _rank_main(rank, world, port, q):
             y = torch.full((M * n,), float("nan"), device="cuda")
             P.parDequantGemmQ8(pool, wq, wd, 32, xq, xd, n, y)
             same(f"gemm/{i}", y, ref)
+        # test_parallel.nim:48-100 cases through the library pool: 300 / 64 / 1
+        # rows over every rank (with 1 row all but the last rank hold none)
+        import refcases as R
+        xp = torch.from_numpy(R.par_x()).cuda()
+        npl = pools[1]
+        for Mp in R.PAR_ROWS:
+            wq8, sc8 = (torch.from_numpy(a).cuda() for a in R.par_int8(Mp))
+            w4, sc4 = (torch.from_numpy(a).cuda() for a in R.par_int4(Mp))
+            wf4, scf = (torch.from_numpy(a).cuda() for a in R.par_f4(Mp))
+            q80, bpr = R.par_q8_0(Mp)
+            q40, _ = R.par_q4_0(Mp)
+            q80 = torch.from_numpy(q80.reshape(-1)).cuda()
+            q40 = torch.from_numpy(q40.reshape(-1)).cuda()
+            cases = [
+                ("int8", lambda y_: L.dequantGemv(wq8, sc8, R.PAR_GS, xp, y_),
+                 lambda y_: P.parDequantGemv(npl, wq8, sc8, R.PAR_GS, xp, y_)),
+                ("int4", lambda y_: L.dequantGemvI4(w4, sc4, R.PAR_GS, xp, y_),
+                 lambda y_: P.parDequantGemvI4(npl, w4, sc4, R.PAR_GS, xp, y_)),
+                ("f4", lambda y_: L.dequantGemvF4(wf4, scf, R.PAR_GS, xp, y_),
+                 lambda y_: P.parDequantGemvF4(npl, wf4, scf, R.PAR_GS, xp, y_)),
+                ("q8_0", lambda y_: L.dequantGemvQ8_0(q80, bpr, xp, y_),
+                 lambda y_: P.parDequantGemvQ8_0(npl, q80, bpr, xp, y_)),
+                ("q4_0", lambda y_: L.dequantGemvQ4_0(q40, bpr, xp, y_),
+                 lambda y_: P.parDequantGemvQ4_0(npl, q40, bpr, xp, y_)),
+            ]
+            for mode in ("exact", "fast"):
+                with L.fp32_mode(mode):
+                    for tag, ser, par in cases:
+                        ref_ = torch.full((Mp,), float("nan"), device="cuda")
+                        ser(ref_)
+                        y_ = torch.full((Mp,), float("nan"), device="cuda")
+                        par(y_)
+                        same(f"par-{tag}-{mode}-M{Mp}", y_, ref_)
+            pwq, pw4, pws, pxq, pxs = (torch.from_numpy(a).cuda() for a in R.pooled_case(Mp))
+            for tag, ser, par, w_ in (("q8", L.dequantGemvQ8, P.parDequantGemvQ8, pwq),
+                                      ("i4q8", L.dequantGemvI4Q8, P.parDequantGemvI4Q8, pw4)):
+                ref_ = torch.full((Mp,), float("nan"), device="cuda")
+                ser(w_, pws, R.PAR_GS, pxq, pxs, ref_)
+                y_ = torch.full((Mp,), float("nan"), device="cuda")
+                par(npl, w_, pws, R.PAR_GS, pxq, pxs, y_)
+                same(f"pooled-{tag}-M{Mp}", y_, ref_)
         # the library pool gathers over NVLink by default (one GPU per rank);
         # both transports, back-to-back gathers (alternating exchange halves)
         # and CUDA-graph replays give the single-GPU bits
@@ -137,7 +180,7 @@ def _rank_main(rank, world, port, q):
 
 def test_pooled_forms_equal_single_gpu_bits():
     import torch.multiprocessing as mp
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

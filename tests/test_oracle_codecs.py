@@ -227,3 +227,22 @@ def test_q8_0_split_matches_blocks():
     assert np.array_equal(blocks[:, 2:].reshape(-1).view(np.int8), qs)
     dh = blocks[:, :2].copy().view(np.uint16).reshape(-1)
     assert np.array_equal(dh.view(np.float16).astype(np.float32), d)
+
+
+@pytest.mark.parametrize("n,gs", [(1000, 0), (1000, 64), (333, 7)])
+def test_quantize_batch_with_zero_points_is_the_scalar_formula(n, gs):
+    """quantizeBatch with QParams carrying zero points falls through to the
+    scalar quantize (simd/dequant.nim:1717-1750 -> quant.nim:48-60):
+    toI8(fl(fl(x / scale) + zeroPoint)), ties away from zero, clamped to
+    [-128, 127]; the symmetric form adds 0.0."""
+    i = np.arange(n, dtype=np.float32)
+    x = (np.sin(i * np.float32(0.1)) * np.float32(5.0)).astype(np.float32)
+    sa, za = _affine(x, gs, -128.0, 127.0)
+    za = (za + np.float32(100.0) * (np.arange(za.size) % 2)).astype(np.float32)  # reach the clamp
+    g = np.arange(n) // (gs if gs > 0 else max(n, 1))
+    v = ((x / sa[g]).astype(np.float32) + za[g]).astype(np.float32).astype(np.float64)
+    want = np.clip(np.sign(v) * np.floor(np.abs(v) + 0.5), -128, 127).astype(np.int8)
+    assert np.array_equal(O.quantizeBatch(x, sa, gs, za), want)
+    v0 = ((x / sa[g]).astype(np.float32) + np.float32(0.0)).astype(np.float64)
+    want0 = np.clip(np.sign(v0) * np.floor(np.abs(v0) + 0.5), -128, 127).astype(np.int8)
+    assert np.array_equal(O.quantizeBatch(x, sa, gs), want0)
