@@ -127,6 +127,21 @@ int lp_dequant_gemv_q8_0(const void *w, int64_t w_len, int64_t blocks_per_row, c
 int lp_dequant_gemv_q4_0(const void *w, int64_t w_len, int64_t blocks_per_row, const float *x,
                          int64_t x_len, float *y, int64_t y_len, lp_stream_t stream);
 
+/* Fused k-quant GEMVs (GGUF Q4_K / Q6_K weights, fp32 activations): w is
+ * m x superblocks_per_row super-blocks of 256 elements (Q4_K 144 bytes, Q6_K
+ * 210 bytes, the layouts ggml.nim:99-213 decodes), x 256 * superblocks_per_row
+ * floats.  The element values are the reference's dequantizeQ4_K /
+ * dequantizeQ6_K values (ggml.nim:136-161, 163-213); the reference has no
+ * fused GEMV over them, so these have no counterpart proc.  Block-float
+ * arithmetic (exact integer 32-element dots, as LP_FP32_FAST) in every fp32
+ * mode: within a few ulp of sum|w x| per row of the exact product. */
+int lp_dequant_gemv_q4_k(const void *w, int64_t w_len, int64_t superblocks_per_row,
+                         const float *x, int64_t x_len, float *y, int64_t y_len,
+                         lp_stream_t stream);
+int lp_dequant_gemv_q6_k(const void *w, int64_t w_len, int64_t superblocks_per_row,
+                         const float *x, int64_t x_len, float *y, int64_t y_len,
+                         lp_stream_t stream);
+
 /* ======================= int8-activation GEMVs (bit-exact) ============ */
 
 /* dequantGemvQ8: int8 weights and int8 activations, exact int32 group sums.
@@ -183,6 +198,38 @@ int lp_dequant_gemm_i4q8(const uint8_t *wpacked, int64_t wpacked_len, const floa
                          int64_t w_scales_len, int64_t group_size, const int8_t *xq,
                          int64_t xq_len, const float *x_scales, int64_t x_scales_len, int64_t n,
                          float *y, int64_t y_len, lp_stream_t stream);
+
+/* ======================= FP4 x FP4 GEMMs on block-scaled tensor cores == */
+/* Both operands in a 4-bit float scheme, two e2m1 codes per byte (low nibble
+ * = even element): weights m rows of k/2 bytes, activations n columns of k/2
+ * bytes (K x n column-major, as dequantGemmQ8 takes xq), y m x n row-major:
+ *   y[r*n + c] = G * sum_b sw[r,b] * sx[c,b] * sum_{i in b} e2m1(w[r,i]) * e2m1(x[c,i])
+ * The products are exact and the sums fp32 (tensor-core accumulation), so
+ * results agree with an exact evaluation within fp32 rounding, not bit for bit
+ * with a sequential order.  Operands 16-byte aligned; m, n, k up to 2^30. */
+
+/* MXFP4 x MXFP4 (tcgen05.mma kind::mxf4, one E8M0 scale per 32 elements,
+ * G = 1): the GEMM form of dequantGemvF4 (simd/dequant.nim:341-420, whose
+ * e2m1 table and scale meaning it keeps) with the activations quantized by
+ * the same scheme (calibrateMX + packF4: lp_calibrate_mx,
+ * lp_quantize_f4_packed).  The scales are fp32 powers of two (calibrateMX's
+ * output), m x k/32 and n x k/32; group_size must be 32.  No single proc of
+ * the reference. */
+int lp_dequant_gemm_f4(const uint8_t *wpacked, int64_t wpacked_len, const float *w_scales,
+                       int64_t w_scales_len, int64_t group_size, const uint8_t *xpacked,
+                       int64_t xpacked_len, const float *x_scales, int64_t x_scales_len, int64_t n,
+                       float *y, int64_t y_len, lp_stream_t stream);
+
+/* NVFP4 x NVFP4 (tcgen05.mma kind::mxf4nvf4, one e4m3 scale per 16 elements,
+ * G = the product of the two global decode scales, each a DEVICE float as
+ * lp_quantize_nvfp4 writes it): the decode of nvfp4.nim:80-92 applied to both
+ * operands of a GEMM.  Block scales m x k/16 and n x k/16 bytes; k a multiple
+ * of 32.  No single proc of the reference. */
+int lp_gemm_nvfp4(const uint8_t *wpacked, int64_t wpacked_len, const uint8_t *w_block_scales,
+                  int64_t w_block_scales_len, const float *w_global_decode_scale,
+                  const uint8_t *xpacked, int64_t xpacked_len, const uint8_t *x_block_scales,
+                  int64_t x_block_scales_len, const float *x_global_decode_scale, int64_t n,
+                  float *y, int64_t y_len, lp_stream_t stream);
 
 /* ======================= encoders (bit-exact) ========================== */
 
@@ -399,6 +446,19 @@ int lp_pool_dequant_gemv_i4q8(lp_pool_t pool, const uint8_t *wpacked, int64_t wp
                               const float *w_scales, int64_t w_scales_len, int64_t group_size,
                               const int8_t *xq, int64_t xq_len, const float *x_scales,
                               int64_t x_scales_len, float *y, int64_t y_len, lp_stream_t stream);
+/* Pooled forms of lp_quantize_dequant_gemv_q8 / _i4q8: each rank quantizes
+ * the whole fp32 x to Q8_0 while staging it and runs its row slice; y is
+ * assembled on every rank (parDequantGemvQ8 / parDequantGemvI4Q8 after
+ * quantizeQ8_0 of the activations, parallel.nim:310-418). */
+int lp_pool_quantize_dequant_gemv_q8(lp_pool_t pool, const int8_t *wq, int64_t wq_len,
+                                     const float *w_scales, int64_t w_scales_len,
+                                     int64_t group_size, const float *x, int64_t x_len, float *y,
+                                     int64_t y_len, lp_stream_t stream);
+int lp_pool_quantize_dequant_gemv_i4q8(lp_pool_t pool, const uint8_t *wpacked,
+                                       int64_t wpacked_len, const float *w_scales,
+                                       int64_t w_scales_len, int64_t group_size, const float *x,
+                                       int64_t x_len, float *y, int64_t y_len,
+                                       lp_stream_t stream);
 int lp_pool_dequant_gemm_q8(lp_pool_t pool, const int8_t *wq, int64_t wq_len,
                             const float *w_scales, int64_t w_scales_len, int64_t group_size,
                             const int8_t *xq, int64_t xq_len, const float *x_scales,

@@ -99,6 +99,12 @@ SIGNATURES = {
     "lp_pool_dequant_gemv_i4q8": "ppnpnnpnpnpnp",
     "lp_pool_dequant_gemm_q8": "ppnpnnpnpnnpnp",
     "lp_pool_dequant_gemm_i4q8": "ppnpnnpnpnnpnp",
+    "lp_pool_quantize_dequant_gemv_q8": "ppnpnnpnpnp",
+    "lp_pool_quantize_dequant_gemv_i4q8": "ppnpnnpnpnp",
+    "lp_dequant_gemm_f4": "pnpnnpnpnnpnp",
+    "lp_dequant_gemv_q4_k": "pnnpnpnp",
+    "lp_dequant_gemv_q6_k": "pnnpnpnp",
+    "lp_gemm_nvfp4": "pnpnppnpnpnpnp",
     "lph_pool_init": "pi",
     "lph_pool_shutdown": "p",
     "lph_pool_thread_count": "p",

@@ -144,8 +144,10 @@ int lp_device_error(void) {
   unsigned int e = lp::take_error_gemv();
   const unsigned int e2 = lp::take_error_gemm_tc();
   const unsigned int e3 = lp::take_error_pool();
+  const unsigned int e4 = lp::take_error_gemm_fp4();
   if (!e) e = e2;
   if (!e) e = e3;
+  if (!e) e = e4;
   return static_cast<int>(e);
 }
 
@@ -233,6 +235,30 @@ int lp_dequant_gemv_q8_0(const void* w, int64_t w_len, int64_t bpr, const float*
 int lp_dequant_gemv_q4_0(const void* w, int64_t w_len, int64_t bpr, const float* x, int64_t x_len,
                          float* y, int64_t y_len, lp_stream_t stream) {
   return gemv_f32_blocks(1, w, w_len, bpr, x, x_len, y, y_len, stream);
+}
+
+// Fused k-quant GEMVs: w is m x sbpr super-blocks (144 / 210 bytes), x is
+// 256 * sbpr floats.  Always the block-float arithmetic (no reference order
+// exists for a fused k-quant GEMV).
+static int gemv_kquant(int q6, const void* w, int64_t w_len, int64_t sbpr, const float* x,
+                       int64_t x_len, float* y, int64_t y_len, lp_stream_t st) {
+  const int64_t m = y_len;
+  LP_REQUIRE(sbpr >= 0 && fits(m, sbpr * 256));
+  LP_REQUIRE(w_len == m * sbpr && x_len == sbpr * 256);
+  if (bad(w, w_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
+  LP_VALIDATED();
+  const int64_t rb = sbpr * (q6 ? 210 : 144);
+  GemvParams p = base(w, nullptr, x, nullptr, y, m, sbpr * 256, 32, sbpr * 8, rb);
+  return q6 ? lp::launch_gemv<lp::FmtQ6_KF>(p, S(st)) : lp::launch_gemv<lp::FmtQ4_KF>(p, S(st));
+}
+
+int lp_dequant_gemv_q4_k(const void* w, int64_t w_len, int64_t sbpr, const float* x,
+                         int64_t x_len, float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_kquant(0, w, w_len, sbpr, x, x_len, y, y_len, stream);
+}
+int lp_dequant_gemv_q6_k(const void* w, int64_t w_len, int64_t sbpr, const float* x,
+                         int64_t x_len, float* y, int64_t y_len, lp_stream_t stream) {
+  return gemv_kquant(1, w, w_len, sbpr, x, x_len, y, y_len, stream);
 }
 
 // ------------------------------------------------ int8-activation GEMVs
@@ -369,6 +395,46 @@ int lp_dequant_gemm_i4q8(const uint8_t* wp, int64_t wp_len, const float* w_scale
                          float* y, int64_t y_len, lp_stream_t stream) {
   return gemm_common(1, wp, wp_len, w_scales, w_scales_len, group_size, xq, xq_len, x_scales,
                      x_scales_len, n, y, y_len, stream);
+}
+
+// ------------------------------------------ FP4 x FP4 block-scaled GEMMs
+
+int lp_dequant_gemm_f4(const uint8_t* wp, int64_t wp_len, const float* w_scales,
+                       int64_t w_scales_len, int64_t group_size, const uint8_t* xp,
+                       int64_t xp_len, const float* x_scales, int64_t x_scales_len, int64_t n,
+                       float* y, int64_t y_len, lp_stream_t stream) {
+  LP_REQUIRE(n >= 1 && y_len >= 0 && xp_len >= 0 && y_len % n == 0 && xp_len % n == 0);
+  const int64_t m = y_len / n, rb = xp_len / n, k = 2 * rb;
+  LP_REQUIRE(group_size == 32 && k % 32 == 0 && fits(m, k) && fits(n, k));
+  LP_REQUIRE(wp_len == m * rb && w_scales_len == m * (k / 32) && x_scales_len == n * (k / 32));
+  if (bad(wp, wp_len) || bad(w_scales, w_scales_len) || bad(xp, xp_len) ||
+      bad(x_scales, x_scales_len) || bad(y, y_len))
+    return LP_ERR_ARG;
+  LP_VALIDATED();
+  if (m == 0) return LP_OK;
+  if (k == 0) return lp::cuda_status(cudaMemsetAsync(y, 0, static_cast<size_t>(y_len) * 4, S(stream)));
+  return lp::launch_gemm_mxf4(wp, w_scales, xp, x_scales, n, y, m, k, S(stream));
+}
+
+int lp_gemm_nvfp4(const uint8_t* wp, int64_t wp_len, const uint8_t* w_block_scales,
+                  int64_t w_block_scales_len, const float* w_global_decode_scale,
+                  const uint8_t* xp, int64_t xp_len, const uint8_t* x_block_scales,
+                  int64_t x_block_scales_len, const float* x_global_decode_scale, int64_t n,
+                  float* y, int64_t y_len, lp_stream_t stream) {
+  LP_REQUIRE(n >= 1 && y_len >= 0 && xp_len >= 0 && y_len % n == 0 && xp_len % n == 0);
+  const int64_t m = y_len / n, rb = xp_len / n, k = 2 * rb;
+  LP_REQUIRE(k % 32 == 0 && fits(m, k) && fits(n, k));
+  LP_REQUIRE(wp_len == m * rb && w_block_scales_len == m * (k / 16) &&
+             x_block_scales_len == n * (k / 16));
+  if (bad(wp, wp_len) || bad(w_block_scales, w_block_scales_len) || bad(xp, xp_len) ||
+      bad(x_block_scales, x_block_scales_len) || bad(y, y_len) || !w_global_decode_scale ||
+      !x_global_decode_scale)
+    return LP_ERR_ARG;
+  LP_VALIDATED();
+  if (m == 0) return LP_OK;
+  if (k == 0) return lp::cuda_status(cudaMemsetAsync(y, 0, static_cast<size_t>(y_len) * 4, S(stream)));
+  return lp::launch_gemm_nvf4(wp, w_block_scales, w_global_decode_scale, xp, x_block_scales,
+                              x_global_decode_scale, n, y, m, k, S(stream));
 }
 
 // -------------------------------------------------------------- encoders

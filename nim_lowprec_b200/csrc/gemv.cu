@@ -47,6 +47,8 @@ template <> int x_stage_bytes<FmtI4F>(const GemvParams& p) { return planes_bytes
 template <> int x_stage_bytes<FmtF4F>(const GemvParams& p) { return planes_bytes(p); }
 template <> int x_stage_bytes<FmtQ8_0F>(const GemvParams& p) { return planes_bytes(p); }
 template <> int x_stage_bytes<FmtQ4_0F>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtQ4_KF>(const GemvParams& p) { return planes_bytes(p); }
+template <> int x_stage_bytes<FmtQ6_KF>(const GemvParams& p) { return planes_bytes(p); }
 template <> int x_stage_bytes<FmtQ8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtI4Q8>(const GemvParams& p) { return q8_bytes(p); }
 template <> int x_stage_bytes<FmtQ8_0Q8>(const GemvParams& p) { return q8_bytes(p); }
@@ -210,6 +212,8 @@ template int launch_gemv<FmtI4F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtF4F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8_0F>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ4_0F>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ4_KF>(GemvParams, cudaStream_t);
+template int launch_gemv<FmtQ6_KF>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtI4Q8>(GemvParams, cudaStream_t);
 template int launch_gemv<FmtQ8FromF32>(GemvParams, cudaStream_t);

@@ -851,6 +851,177 @@ struct FmtI8F : FmtGroupF<CodesI8> {};
 struct FmtI4F : FmtGroupF<CodesI4> {};
 struct FmtF4F : FmtGroupF<CodesF4> {};
 
+// ------------------------------------------- k-quant fused GEMVs (GGUF)
+// The reference dequantizes k-quant super-blocks (ggml.nim:108-213) but has
+// no fused GEMV over them; these compute y = W x over the super-blocks
+// directly, on the block-float path, with one 32-element group of a 256-
+// element super-block as the skeleton's group.  Element values are the
+// reference's: Q4_K fl(d*sc)*q - fl(dmin*m) (q 0..15, 6-bit sc/m per 32),
+// Q6_K fl(d*sc)*(q - 32) (q 0..63, int8 sc per 16).  A group's integer dot
+// sum(q * X) against the activation digit planes is exact, so a term is the
+// block-float group value times fl(d*sc), minus (Q4_K) fl(dmin*m) times the
+// group's activation sum -- within a few ulp of the exact term, not the
+// reference's element order (none exists for a fused form).
+
+// get_scale_min_k4 of ggml.nim:118-128: 6-bit scale and min of sub-block j.
+__device__ __forceinline__ void kq_scale_min(int j, const uint8_t* q, int& sc, int& m) {
+  if (j < 4) {
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ uint32_t h16_at(const uint8_t* p) {
+  return static_cast<uint32_t>(p[0]) | (static_cast<uint32_t>(p[1]) << 8);
+}
+
+// Sequential fp32 group sums from the unstaged activations (groups holding a
+// non-finite or huge activation), over the reference's dequantized values.
+__device__ __forceinline__ float seq_q4_k(const uint8_t* blk, int j, const float* xg) {
+  int sc, m;
+  kq_scale_min(j, blk + 4, sc, m);
+  const float d1 = fmul(h2f(h16_at(blk)), i2f_rn(sc)), mm = fmul(h2f(h16_at(blk + 2)), i2f_rn(m));
+  const uint8_t* qs = blk + 16 + 32 * (j >> 1);
+  float partial = 0.0f;
+  for (int l = 0; l < 32; ++l) {
+    const int q = (j & 1) ? (qs[l] >> 4) : (qs[l] & 15);
+    partial = fadd(partial, fmul(__fsub_rn(fmul(d1, i2f_rn(q)), mm), xg[l]));
+  }
+  return partial;
+}
+__device__ __forceinline__ int q6_code(const uint8_t* blk, int hh, int k, int l) {
+  const uint32_t lo = blk[64 * hh + 32 * (k & 1) + l], hi = blk[128 + 32 * hh + l];
+  return static_cast<int>(((k & 2) ? (lo >> 4) : (lo & 15u)) | (((hi >> (2 * k)) & 3u) << 4));
+}
+__device__ __forceinline__ float seq_q6_k(const uint8_t* blk, int gi, const float* xg) {
+  const int hh = gi >> 2, k = gi & 3;
+  const float d = h2f(h16_at(blk + 208));
+  float partial = 0.0f;
+  for (int l = 0; l < 32; ++l) {
+    const int sc = static_cast<int8_t>(blk[192 + 8 * hh + (l >> 4) + 2 * k]);
+    const float v = fmul(fmul(d, i2f_rn(sc)), i2f_rn(q6_code(blk, hh, k, l) - 32));
+    partial = fadd(partial, fmul(v, xg[l]));
+  }
+  return partial;
+}
+
+// dequantizeQ4_K's values (ggml.nim:136-161) in a fused GEMV: 144-byte
+// super-blocks (d, dmin, 12 bytes of 6-bit scales/mins, 128 bytes of
+// nibbles); group j of a super-block is nibble j & 1 of qs bytes 32 (j >> 1)..
+struct FmtQ4_KF : StageXPlanes<false> {
+  static constexpr bool kScales = false;
+  static constexpr Fold kFold = Fold::Tree;
+  static constexpr bool kFix = true;
+  static constexpr bool kTwoPairs = true;
+  PlaneCache<1> pc;  // kOff = 1: b[p] = -(digit sum of plane p) -- the group's activation sum
+  float xsum = 0.0f;
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    pc.load(p, xsm, g);
+    xsum = bf_value<true>(-pc.b[0], -pc.b[1], -pc.b[2]) * pc.s;
+  }
+  __device__ __forceinline__ void fix2(const GemvParams& p, const uint8_t* wA, const uint8_t* wB,
+                                       const float*, const float*, int g, float& tA, float& tB) {
+    if (isnan(pc.s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * 32;
+      tA = seq_q4_k(wA + (g >> 3) * 144, g & 7, xg);
+      tB = seq_q4_k(wB + (g >> 3) * 144, g & 7, xg);
+    }
+  }
+  __device__ __forceinline__ float one(const uint8_t* blk, int j) const {
+    const uint4* q = reinterpret_cast<const uint4*>(blk + 16 + 32 * (j >> 1));
+    const uint4 u0 = q[0], u1 = q[1];
+    const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    const int sh = 4 * (j & 1);
+    int a[3] = {0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) LP_DP3_US(a, (w[i] >> sh) & 0x0F0F0F0Fu, pc.P[0][i], pc.P[1][i], pc.P[2][i]);
+    int sc, m;
+    kq_scale_min(j, blk + 4, sc, m);
+    const float d1 = h2f(h16_at(blk)) * static_cast<float>(sc);
+    const float mm = h2f(h16_at(blk + 2)) * static_cast<float>(m);
+    return d1 * (bf_value<true>(a[0], a[1], a[2]) * pc.s) - mm * xsum;
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*, const uint8_t* wA,
+                                        const uint8_t* wB, const float*, const float*, int g,
+                                        float& tA, float& tB) {
+    tA = one(wA + (g >> 3) * 144, g & 7);
+    tB = one(wB + (g >> 3) * 144, g & 7);
+  }
+};
+
+// dequantizeQ6_K's values (ggml.nim:163-213) in a fused GEMV: 210-byte
+// super-blocks (ql[128], qh[64], int8 scales[16], d); group gi = 4 hh + k of a
+// super-block holds elements 128 hh + 32 k + l, two scales (l < 16, l >= 16).
+struct FmtQ6_KF : StageXPlanes<false> {
+  static constexpr bool kScales = false;
+  static constexpr Fold kFold = Fold::Tree;
+  static constexpr bool kFix = true;
+  static constexpr bool kTwoPairs = true;
+  PlaneCache<0> pc;
+  int off32[2][3];  // -32 * digit sums of each half of the group, per plane
+  __device__ __forceinline__ void prepare(const GemvParams& p, const uint8_t* xsm, int g) {
+    pc.load(p, xsm, g);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int s[3] = {0, 0, 0};
+#pragma unroll
+      for (int i = 4 * h; i < 4 * h + 4; ++i) {
+        s[0] = dp4a_uu(0x01010101u, pc.P[0][i], s[0]);
+        s[1] = dp4a_uu(0x01010101u, pc.P[1][i], s[1]);
+        s[2] = dp4a_us(0x01010101u, pc.P[2][i], s[2]);
+      }
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) off32[h][pl] = -32 * s[pl];
+    }
+  }
+  __device__ __forceinline__ void fix2(const GemvParams& p, const uint8_t* wA, const uint8_t* wB,
+                                       const float*, const float*, int g, float& tA, float& tB) {
+    if (isnan(pc.s)) {
+      const float* xg = static_cast<const float*>(p.x) + g * 32;
+      tA = seq_q6_k(wA + (g >> 3) * 210, g & 7, xg);
+      tB = seq_q6_k(wB + (g >> 3) * 210, g & 7, xg);
+    }
+  }
+  __device__ __forceinline__ float one(const uint8_t* blk, int gi) const {
+    const int hh = gi >> 2, k = gi & 3;
+    uint32_t lo[8], hi[8], w[9];
+    // 32 bytes at a 2-byte-aligned address: a word window and byte permutes
+    int off = load_window<9>(blk + 64 * hh + 32 * (k & 1), w);
+    uint32_t sel = off ? 0x5432u : 0x3210u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) lo[i] = prmt(w[i], w[i + 1], sel);
+    off = load_window<9>(blk + 128 + 32 * hh, w);
+    sel = off ? 0x5432u : 0x3210u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hi[i] = prmt(w[i], w[i + 1], sel);
+    const int lsh = (k & 2) ? 4 : 0, hsh = 2 * k;
+    int a[2][3];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int pl = 0; pl < 3; ++pl) a[h][pl] = off32[h][pl];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t code = ((lo[i] >> lsh) & 0x0F0F0F0Fu) | (((hi[i] >> hsh) & 0x03030303u) << 4);
+      LP_DP3_US(a[i >> 2], code, pc.P[0][i], pc.P[1][i], pc.P[2][i]);
+    }
+    const float d = h2f(h16_at(blk + 208));
+    const float s0 = d * static_cast<float>(static_cast<int8_t>(blk[192 + 8 * hh + 2 * k]));
+    const float s1 = d * static_cast<float>(static_cast<int8_t>(blk[192 + 8 * hh + 2 * k + 1]));
+    return (s0 * bf_value<true>(a[0][0], a[0][1], a[0][2]) +
+            s1 * bf_value<true>(a[1][0], a[1][1], a[1][2])) * pc.s;
+  }
+  __device__ __forceinline__ void term2(const GemvParams&, const uint8_t*, const uint8_t* wA,
+                                        const uint8_t* wB, const float*, const float*, int g,
+                                        float& tA, float& tB) {
+    tA = one(wA + (g >> 3) * 210, g & 7);
+    tB = one(wB + (g >> 3) * 210, g & 7);
+  }
+};
+
 // ============================================= int8-activation formats
 
 // Group-scale int8 activations: xq (k bytes) then xScales (gpr floats).

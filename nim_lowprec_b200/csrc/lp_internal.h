@@ -50,6 +50,8 @@ struct FmtI4F;
 struct FmtF4F;
 struct FmtQ8_0F;
 struct FmtQ4_0F;
+struct FmtQ4_KF;
+struct FmtQ6_KF;
 struct FmtQ8FromF32;
 struct FmtI4Q8FromF32;
 struct FmtQ8;
@@ -91,11 +93,18 @@ int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* 
                    const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
 int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
                 const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
+// FP4 x FP4 block-scaled tensor-core GEMMs (gemm_fp4.cu)
+int launch_gemm_mxf4(const uint8_t* w, const float* ws, const uint8_t* x, const float* xs,
+                     int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
+int launch_gemm_nvf4(const uint8_t* w, const uint8_t* ws, const float* gw, const uint8_t* x,
+                     const uint8_t* xs, const float* gx, int64_t n, float* y, int64_t m, int64_t k,
+                     cudaStream_t st);
 
 // error words of the translation units whose kernels wait (read + clear)
 unsigned int take_error_gemv();
 unsigned int take_error_gemm_tc();
 unsigned int take_error_pool();
+unsigned int take_error_gemm_fp4();
 
 // While on (this thread only), the lp_* entry points run their shape and
 // argument checks and return without launching anything (capi.cu).

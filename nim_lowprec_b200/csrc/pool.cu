@@ -549,6 +549,24 @@ int lp_pool_dequant_gemv_i4q8(lp_pool_t pool, const uint8_t* wp, int64_t wp_len,
                                       xq_len, x_scales, x_scales_len, yl_, yl_len_, stream);
   LP_POOL_POST(1)
 }
+int lp_pool_quantize_dequant_gemv_q8(lp_pool_t pool, const int8_t* wq, int64_t wq_len,
+                                     const float* w_scales, int64_t w_scales_len,
+                                     int64_t group_size, const float* x, int64_t x_len, float* y,
+                                     int64_t y_len, lp_stream_t stream) {
+  LP_POOL_PRE(y_len, 1)
+  const int r_ = lp_quantize_dequant_gemv_q8(wq, wq_len, w_scales, w_scales_len, group_size, x,
+                                             x_len, yl_, yl_len_, stream);
+  LP_POOL_POST(1)
+}
+int lp_pool_quantize_dequant_gemv_i4q8(lp_pool_t pool, const uint8_t* wp, int64_t wp_len,
+                                       const float* w_scales, int64_t w_scales_len,
+                                       int64_t group_size, const float* x, int64_t x_len,
+                                       float* y, int64_t y_len, lp_stream_t stream) {
+  LP_POOL_PRE(y_len, 1)
+  const int r_ = lp_quantize_dequant_gemv_i4q8(wp, wp_len, w_scales, w_scales_len, group_size,
+                                               x, x_len, yl_, yl_len_, stream);
+  LP_POOL_POST(1)
+}
 int lp_pool_dequant_gemm_q8(lp_pool_t pool, const int8_t* wq, int64_t wq_len,
                             const float* w_scales, int64_t w_scales_len, int64_t group_size,
                             const int8_t* xq, int64_t xq_len, const float* x_scales,

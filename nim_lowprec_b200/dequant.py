@@ -404,3 +404,48 @@ def dequantizeNVFP4(codes, blockScales, globalDecodeScale, dst):
     N.check(N.lib().lp_dequantize_nvfp4(_ptr(codes), _numel(codes), _ptr(blockScales),
                                         _numel(blockScales), float(globalDecodeScale),
                                         _ptr(dst), _numel(dst), _stream()), "dequantize_nvfp4")
+
+
+def dequantGemmF4(wpacked, wScales, groupSize, xpacked, xScales, n, y):
+    """MXFP4 x MXFP4 GEMM on the block-scaled tensor cores (tcgen05 kind::mxf4):
+    the GEMM form of dequantGemvF4 (simd/dequant.nim:341-420) with MXFP4
+    activations (K x n column-major packed codes, n x K/32 power-of-two fp32
+    scales).  y is m x n row-major.  Torch CUDA tensors."""
+    _dev_only("dequantGemmF4", wpacked, wScales, xpacked, xScales, y)
+    N.check(N.lib().lp_dequant_gemm_f4(_ptr(wpacked), _numel(wpacked), _ptr(wScales),
+                                       _numel(wScales), int(groupSize), _ptr(xpacked),
+                                       _numel(xpacked), _ptr(xScales), _numel(xScales), int(n),
+                                       _ptr(y), _numel(y), _stream()), "dequant_gemm_f4")
+
+
+def gemmNVFP4(wpacked, wBlockScales, wGlobalDecodeScale, xpacked, xBlockScales,
+              xGlobalDecodeScale, n, y):
+    """NVFP4 x NVFP4 GEMM on the block-scaled tensor cores (tcgen05
+    kind::mxf4nvf4): packed e2m1 codes, e4m3 block scales per 16 elements and
+    the two global decode scales (one-element CUDA tensors, as quantizeNVFP4
+    writes them); the decode of nvfp4.nim:80-92 on both operands."""
+    _dev_only("gemmNVFP4", wpacked, wBlockScales, wGlobalDecodeScale, xpacked, xBlockScales,
+              xGlobalDecodeScale, y)
+    N.check(N.lib().lp_gemm_nvfp4(_ptr(wpacked), _numel(wpacked), _ptr(wBlockScales),
+                                  _numel(wBlockScales), _ptr(wGlobalDecodeScale), _ptr(xpacked),
+                                  _numel(xpacked), _ptr(xBlockScales), _numel(xBlockScales),
+                                  _ptr(xGlobalDecodeScale), int(n), _ptr(y), _numel(y),
+                                  _stream()), "gemm_nvfp4")
+
+
+def dequantGemvQ4_K(w, superBlocksPerRow, x, y):
+    """Fused GEMV over GGUF Q4_K super-blocks (144 bytes, ggml.nim:136-161
+    values) with fp32 activations; block-float arithmetic.  Torch CUDA tensors."""
+    _dev_only("dequantGemvQ4_K", w, x, y)
+    N.check(N.lib().lp_dequant_gemv_q4_k(_ptr(w), _blocks(w, Q4_K_BYTES), int(superBlocksPerRow),
+                                         _ptr(x), _numel(x), _ptr(y), _numel(y), _stream()),
+            "dequant_gemv_q4_k")
+
+
+def dequantGemvQ6_K(w, superBlocksPerRow, x, y):
+    """Fused GEMV over GGUF Q6_K super-blocks (210 bytes, ggml.nim:163-213
+    values) with fp32 activations; block-float arithmetic.  Torch CUDA tensors."""
+    _dev_only("dequantGemvQ6_K", w, x, y)
+    N.check(N.lib().lp_dequant_gemv_q6_k(_ptr(w), _blocks(w, Q6_K_BYTES), int(superBlocksPerRow),
+                                         _ptr(x), _numel(x), _ptr(y), _numel(y), _stream()),
+            "dequant_gemv_q6_k")

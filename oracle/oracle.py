@@ -96,6 +96,7 @@ def lib():
         L.lpo_shard.restype = None
         L.lpo_shard.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
         L.lpo_run.argtypes = [vp, ctypes.c_int, vp, vp, i64, vp, vp, i64, i64, vp, i64]
+        L.lpo_gemm_fp4.argtypes = [vp, vp, vp, vp, ctypes.c_int, i64, i64, i64, ctypes.c_double, vp]
         _lib = L
     return _lib
 
@@ -392,3 +393,21 @@ def shard(rows: int, workers: int, worker: int):
 
 def shardCount(rows: int, threads: int) -> int:
     return int(lib().lpo_shard_count(int(rows), int(threads)))
+
+
+def gemmFp4(wpacked, wScales, xpacked, xScales, n: int, nvfp4: bool = False,
+            globalScale: float = 1.0) -> np.ndarray:
+    """FP4 x FP4 GEMM in fp64 (lpo_gemm_fp4): MXFP4 (fp32 power-of-two scales
+    per 32 elements) or NVFP4 (e4m3 byte scales per 16 elements times the
+    product of the global decode scales).  Returns y (m x n row-major, fp64)."""
+    wpacked = _c(wpacked, np.uint8)
+    xpacked = _c(xpacked, np.uint8)
+    dt = np.uint8 if nvfp4 else np.float32
+    ws = _c(wScales, dt)
+    xs = _c(xScales, dt)
+    k = xpacked.size * 2 // n
+    m = wpacked.size * 2 // k
+    y = np.empty(m * n, np.float64)
+    lib().lpo_gemm_fp4(_p(wpacked), _p(ws), _p(xpacked), _p(xs), 1 if nvfp4 else 0, m, k, n,
+                       float(globalScale), _p(y))
+    return y

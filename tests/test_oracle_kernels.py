@@ -244,3 +244,33 @@ def test_shard_count_rules():
     assert O.shardCount(300, 64) == 4
     assert O.shardCount(300, 3) == 3
     assert O.shardCount(64, 2) == 1
+
+
+def test_fp4_gemm_oracle_is_the_exact_gemm_of_the_decoded_operands():
+    """lpo_gemm_fp4 against numpy: e2m1 table (simd/dequant.nim:57-58,
+    halved) times the per-block scales, fp64 GEMM; MXFP4 and NVFP4."""
+    rng = np.random.default_rng(5)
+    m, k, n = 7, 96, 5
+    wp = rng.integers(0, 256, m * k // 2, dtype=np.uint8)
+    xp = rng.integers(0, 256, n * k // 2, dtype=np.uint8)
+    tab = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6])
+
+    def dec(p, rows):
+        v = np.empty((rows, k))
+        q = p.reshape(rows, k // 2)
+        v[:, 0::2], v[:, 1::2] = tab[q & 15], tab[q >> 4]
+        return v
+    ws = np.ldexp(1.0, rng.integers(-8, 3, m * k // 32)).astype(np.float32)
+    xs = np.ldexp(1.0, rng.integers(-8, 3, n * k // 32)).astype(np.float32)
+    W = dec(wp, m) * np.repeat(ws.reshape(m, -1).astype(np.float64), 32, 1)
+    X = dec(xp, n) * np.repeat(xs.reshape(n, -1).astype(np.float64), 32, 1)
+    got = O.gemmFp4(wp, ws, xp, xs, n)
+    assert np.allclose(got, (W @ X.T).reshape(-1), rtol=1e-12, atol=1e-300)
+    # NVFP4: e4m3 block scales per 16, global factor
+    wb = rng.integers(0x20, 0x50, m * k // 16, dtype=np.uint8)
+    xb = rng.integers(0x20, 0x50, n * k // 16, dtype=np.uint8)
+    e4 = np.array([O.lib().lpo_f8e4m3_to_f32(int(c)) for c in range(256)], np.float64)
+    W = dec(wp, m) * np.repeat(e4[wb].reshape(m, -1), 16, 1)
+    X = dec(xp, n) * np.repeat(e4[xb].reshape(n, -1), 16, 1)
+    got = O.gemmFp4(wp, wb, xp, xb, n, nvfp4=True, globalScale=0.75)
+    assert np.allclose(got, 0.75 * (W @ X.T).reshape(-1), rtol=1e-12, atol=1e-300)
