@@ -567,6 +567,8 @@ def main():
     ap.add_argument("--no-formats", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="launch each hot kernel once (for ncu), no timing")
+    ap.add_argument("--sweep-only", action="store_true",
+                    help="one GPU: W + K eager config-4 sweeps and nothing else (ncu launch list)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -576,6 +578,17 @@ def main():
         import nim_lowprec_b200 as L
         for name in profile_kernels(torch, L):
             print("launched:", name, flush=True)
+        return 0
+    if args.sweep_only:
+        import torch
+
+        import nim_lowprec_b200 as L
+        wl4 = Cfg4Workload(torch, L, 1, 0)
+        torch.cuda.synchronize()
+        for _ in range(args.warmup + args.steps):
+            wl4.sweep(None)
+        torch.cuda.synchronize()
+        print(f"swept {args.warmup + args.steps} times", flush=True)
         return 0
 
     import torch
@@ -817,8 +830,8 @@ def main():
     return 0
 
 
-PROFILE_KERNELS = ("gemv_kernel|k_gemm_tc|k_quantize_q8_0|k_dequantize_q4_k|k_dequantize_q6_k"
-                   "|k_dequantize_batch")
+PROFILE_KERNELS = ("gemv_kernel|k_gemm_tc|k_gemm_fp4|k_quantize_q8_0|k_dequantize_q4_k"
+                   "|k_dequantize_q6_k|k_dequantize_batch")
 
 
 def profile_kernels(torch, L):
@@ -915,6 +928,41 @@ def profile_kernels(torch, L):
     out = torch.empty(16_000_000, device="cuda")
     run("dequantizeBatch 16000000 group 128", lambda: L.dequantizeBatch(q, sc, 128, out))
     del q, sc, out
+    torch.cuda.empty_cache()
+
+    # fused k-quant GEMVs, 11008 x 4096
+    Mk, sbpr = 11008, 16
+    for bb, fn, dpos, name in ((144, L.dequantGemvQ4_K, (0, 2), "Q4_K"),
+                               (210, L.dequantGemvQ6_K, (208,), "Q6_K")):
+        g.manual_seed(9)
+        raw = torch.randint(0, 256, (Mk * sbpr, bb), dtype=torch.uint8, device="cuda", generator=g)
+        for p_ in dpos:
+            raw[:, p_:p_ + 2] = (torch.randn(Mk * sbpr, device="cuda", generator=g) * 0.01).half() \
+                .view(torch.uint8).view(Mk * sbpr, 2)
+        xk, yk = rnd(4096, 19), torch.empty(Mk, device="cuda")
+        run(f"gemv {name} 11008x4096", lambda: fn(raw.view(-1), sbpr, xk, yk))
+        del raw, xk, yk
+
+    # FP4 x FP4 GEMMs 4096 x 4096 x 512 on the block-scaled tensor cores
+    M = K = 4096
+    B = 512
+    w, x = rnd(M * K, 12, 0.02), rnd(K * B, 13)
+    ws_, xs_ = (torch.empty(t.numel() // 32, device="cuda") for t in (w, x))
+    L.calibrateMX(w, 32, 2, ws_)
+    L.calibrateMX(x, 32, 2, xs_)
+    wp, xp = (torch.empty(t.numel() // 2, dtype=torch.uint8, device="cuda") for t in (w, x))
+    L.quantizeF4Packed(w, ws_, 32, wp)
+    L.quantizeF4Packed(x, xs_, 32, xp)
+    y = torch.empty(M * B, device="cuda")
+    run("gemm MXFP4 4096x4096x512", lambda: L.dequantGemmF4(wp, ws_, 32, xp, xs_, B, y))
+    enc = []
+    for t in (w, x):
+        c = torch.empty(t.numel(), dtype=torch.uint8, device="cuda")
+        bs = torch.empty(t.numel() // 16, dtype=torch.uint8, device="cuda")
+        gd = torch.empty(1, device="cuda")
+        L.quantizeNVFP4(t, c, bs, gd)
+        enc.append(((c[0::2] | (c[1::2] << 4)).contiguous(), bs, gd))
+    run("gemm NVFP4 4096x4096x512", lambda: L.gemmNVFP4(*enc[0], *enc[1], B, y))
     return done
 
 

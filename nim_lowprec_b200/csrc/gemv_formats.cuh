@@ -1051,31 +1051,49 @@ struct StageXQ8FromF32 {
     float* xs = reinterpret_cast<float*>(xsm + ((p.k + 15) & ~15));
     const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const int ntask = p.gpr * 8;
-    for (int t0 = tid & ~31; t0 < ntask; t0 += nthr) {
-      const int t = t0 + (tid & 31);
-      const bool valid = t < ntask;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (valid)
-        v = vec ? __ldg(reinterpret_cast<const float4*>(x) + t)
-                : make_float4(__ldg(x + 4 * t), __ldg(x + 4 * t + 1), __ldg(x + 4 * t + 2),
-                              __ldg(x + 4 * t + 3));
-      float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
-      if (!valid) continue;
-      const float d = __fdiv_rn(a, 127.0f);
-      const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-      const float e[4] = {v.x, v.y, v.z, v.w};
-      uint32_t word = 0;
+    // Under the weight stream an activation load waits on the order of a
+    // microsecond, so each thread issues the loads of up to kR rounds before
+    // it uses any (one wait instead of one per round).
+    constexpr int kR = 8;
+    for (int b0 = tid & ~31; b0 < ntask; b0 += kR * nthr) {
+      float4 v[kR];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float r = roundf(__fmul_rn(e[i], id));
-        r = fminf(fmaxf(r, -127.0f), 127.0f);
-        word |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * i);
+      for (int r = 0; r < kR; ++r) {
+        const int t = b0 + r * nthr + (tid & 31);
+        v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < ntask)
+          v[r] = vec ? __ldg(reinterpret_cast<const float4*>(x) + t)
+                     : make_float4(__ldg(x + 4 * t), __ldg(x + 4 * t + 1), __ldg(x + 4 * t + 2),
+                                   __ldg(x + 4 * t + 3));
       }
-      q[t] = word;
-      if ((t & 7) == 0) xs[t >> 3] = h2f(__half_as_ushort(__float2half_rn(d)));
+#pragma unroll
+      for (int r = 0; r < kR; ++r) {
+        const int t = b0 + r * nthr + (tid & 31);
+        if (b0 + r * nthr >= ntask) break;  // warp-uniform
+        float a = fmaxf(fmaxf(fabsf(v[r].x), fabsf(v[r].y)), fmaxf(fabsf(v[r].z), fabsf(v[r].w)));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+        // d and 1/d once per 32-element block (lane 0 of its 8), then shared
+        float d = 0.0f, id = 0.0f;
+        if ((tid & 7) == 0) {
+          d = __fdiv_rn(a, 127.0f);
+          id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        }
+        d = __shfl_sync(0xffffffffu, d, (tid & 31) & ~7);
+        id = __shfl_sync(0xffffffffu, id, (tid & 31) & ~7);
+        if (t >= ntask) continue;
+        const float e[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float rr = roundf(__fmul_rn(e[i], id));
+          rr = fminf(fmaxf(rr, -127.0f), 127.0f);
+          word |= (static_cast<uint32_t>(static_cast<int>(rr)) & 0xFFu) << (8 * i);
+        }
+        q[t] = word;
+        if ((t & 7) == 0) xs[t >> 3] = h2f(__half_as_ushort(__float2half_rn(d)));
+      }
     }
   }
 };
