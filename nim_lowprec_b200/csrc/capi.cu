@@ -375,8 +375,8 @@ static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, in
                      : lp::launch_gemv<lp::FmtQ8Cols>(p, S(st));
     if (r != LP_ERR_UNSUPPORTED) return r;
   }
-  if (!i4) {
-    const int r = lp::launch_gemm_tc(static_cast<const int8_t*>(w), ws, gs, xq, xs, n, y, m, k, S(st));
+  {
+    const int r = lp::launch_gemm_tc(w, i4, ws, gs, xq, xs, n, y, m, k, S(st));
     if (r != LP_ERR_UNSUPPORTED) return r;
   }
   return lp::launch_gemm(static_cast<const uint8_t*>(w), i4, ws, gs, xq, xs, n, y, m, k, S(st));

@@ -150,16 +150,45 @@ __device__ __forceinline__ void stage_scales(uint8_t* atoms, const void* src, in
   }
 }
 
-template <bool NV, int NT>
+// The same from a stage's raw scale tile in shared memory (row r at r * SB
+// bytes: MXFP4 8 fp32 scales, NVFP4 16 e4m3 bytes), as TMA left it.
+template <bool NV>
+__device__ __forceinline__ void stage_scales_smem(uint8_t* atoms, const uint8_t* raw, int r,
+                                                  bool valid) {
+  constexpr int NB = NV ? 16 : 8;
+#pragma unroll
+  for (int a = 0; a < NB / 4; ++a) {
+    uint32_t word = 0;
+    if (valid) {
+      if (NV) {
+        word = reinterpret_cast<const uint32_t*>(raw + 16 * r)[a];
+      } else {
+        const float4 f = reinterpret_cast<const float4*>(raw + 32 * r)[a];
+        word = e8m0_code(f.x) | (e8m0_code(f.y) << 8) | (e8m0_code(f.z) << 16) |
+               (e8m0_code(f.w) << 24);
+      }
+    }
+    *reinterpret_cast<uint32_t*>(atoms + 512 * a + sf_off(r, 0)) = word;
+  }
+}
+
+// TS: the stage's scale tiles come in by TMA with the codes (row strides of
+// the scale arrays a multiple of 16 bytes: K % 256 == 0); otherwise the
+// scale warps read them from global memory.
+template <bool NV, int NT, bool TS>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_fp4(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
                const Fp4Args a) {
   constexpr int NB = NV ? 16 : 8;          // scale blocks per stage
   constexpr int NATOM = NB / 4;            // atoms per operand per stage
+  constexpr int SB = NV ? 16 : 32;         // raw scale bytes per row and stage
   constexpr int A_BYTES = 128 * kStageBytes;
   constexpr int B_BYTES = NT * kStageBytes;
+  constexpr int RAW_A = TS ? 128 * SB : 0, RAW_B = TS ? NT * SB : 0;
   constexpr int SF_BYTES = 2 * NATOM * 512;
-  constexpr int STAGE = A_BYTES + B_BYTES + SF_BYTES;
+  constexpr int SF_OFF = A_BYTES + B_BYTES + RAW_A + RAW_B;
+  constexpr int STAGE = SF_OFF + SF_BYTES;
   constexpr uint32_t kTmemCols = 256;
   constexpr uint32_t kSfaCol = 128, kSfbCol = 128 + 4 * NATOM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -197,9 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, &s_abort)) break;
         if (s_abort) break;
         uint8_t* st = smem + s * STAGE;
-        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES + RAW_A + RAW_B);
         tma_load_2d(st, &tmA, kb * kStageBytes, m0, &full[s]);
         tma_load_2d(st + A_BYTES, &tmB, kb * kStageBytes, n0, &full[s]);
+        if constexpr (TS) {
+          tma_load_2d(st + A_BYTES + B_BYTES, &tmSA, kb * SB, m0, &full[s]);
+          tma_load_2d(st + A_BYTES + B_BYTES + RAW_A, &tmSB, kb * SB, n0, &full[s]);
+        }
       }
       for (int u = max(0, kb - kStages); u < kb; ++u)
         mbar_wait(&full[u % kStages], (u / kStages) & 1);
@@ -213,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&sfull[s], (kb / kStages) & 1, &s_abort)) break;
         fence_after();
         const uint8_t* st = smem + s * STAGE;
-        const uint8_t* sfa = st + A_BYTES + B_BYTES;
+        const uint8_t* sfa = st + SF_OFF;
         const uint8_t* sfb = sfa + NATOM * 512;
 #pragma unroll
         for (int t = 0; t < NATOM; ++t) {
@@ -242,11 +275,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x - 64;  // 0..127: one A row and one B row each
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % kStages;
-      if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, &s_abort)) break;
-      if (s_abort) break;
-      uint8_t* sfa = smem + s * STAGE + A_BYTES + B_BYTES;
-      stage_scales<NV>(sfa, a.ws, m0 + r, a.m, a.nblk, kb * NB, r);
-      stage_scales<NV>(sfa + NATOM * 512, a.xs, n0 + r, min(a.n, n0 + NT), a.nblk, kb * NB, r);
+      uint8_t* st = smem + s * STAGE;
+      uint8_t* sfa = st + SF_OFF;
+      if constexpr (TS) {
+        // the producer reissued this stage only after its previous MMAs
+        // (and scale copies) completed, so the atoms are free once it lands
+        if (!mbar_wait(&full[s], (kb / kStages) & 1, &s_abort)) break;
+        if (s_abort) break;
+        stage_scales_smem<NV>(sfa, st + A_BYTES + B_BYTES, r, true);
+        // rows past the column tile (NT = 64) hold zeros; their raw rows do not exist
+        stage_scales_smem<NV>(sfa + NATOM * 512, st + A_BYTES + B_BYTES + RAW_A, r, r < NT);
+      } else {
+        if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, &s_abort)) break;
+        if (s_abort) break;
+        stage_scales<NV>(sfa, a.ws, m0 + r, a.m, a.nblk, kb * NB, r);
+        stage_scales<NV>(sfa + NATOM * 512, a.xs, n0 + r, min(a.n, n0 + NT), a.nblk, kb * NB, r);
+      }
       // generic-proxy writes, read by tcgen05.cp (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -285,19 +329,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool NV, int NT>
+template <bool NV, int NT, bool TS>
 int launch_nt(const uint8_t* w, const void* ws, const uint8_t* x, const void* xs, int n, float* y,
               int m, int k, const float* gw, const float* gx, cudaStream_t st) {
-  CUtensorMap tmA, tmB;
+  constexpr int SB = NV ? 16 : 32;  // raw scale bytes per row and stage
+  const int64_t srow = static_cast<int64_t>(k) / (NV ? 16 : 32) * (NV ? 1 : 4);  // scale row bytes
+  CUtensorMap tmA, tmB, tmSA, tmSB;
   if (!encode_u8(&tmA, w, k / 2, m, kStageBytes, 128, true) ||
       !encode_u8(&tmB, x, k / 2, n, kStageBytes, NT, true))
     return LP_ERR_UNSUPPORTED;
+  if (TS) {
+    if (!encode_u8(&tmSA, ws, srow, m, SB, 128, false) ||
+        !encode_u8(&tmSB, xs, srow, n, SB, NT, false))
+      return LP_ERR_UNSUPPORTED;
+  } else {
+    tmSA = tmA;  // unused
+    tmSB = tmB;
+  }
   constexpr int NATOM = (NV ? 16 : 8) / 4;
-  constexpr int STAGE = (128 + NT) * kStageBytes + 2 * NATOM * 512;
+  constexpr int STAGE = (128 + NT) * kStageBytes + (TS ? (128 + NT) * SB : 0) + 2 * NATOM * 512;
   const int smem = 1024 + kStages * STAGE;
   const DeviceInfo& di = device_info();
   if (smem > di.max_smem_optin - 2048) return LP_ERR_UNSUPPORTED;
-  auto kern = k_gemm_fp4<NV, NT>;
+  auto kern = k_gemm_fp4<NV, NT, TS>;
   static int attr_set[kMaxDevices];
   const int slot = di.ordinal % kMaxDevices;
   if (attr_set[slot] < smem) {
@@ -309,8 +363,18 @@ int launch_nt(const uint8_t* w, const void* ws, const uint8_t* x, const void* xs
   }
   Fp4Args args{ws, xs, y, m, k, n, k / (NV ? 16 : 32), gw, gx};
   const dim3 grid((n + NT - 1) / NT, (m + 127) / 128);
-  kern<<<grid, kThreads, smem, st>>>(tmA, tmB, args);
+  kern<<<grid, kThreads, smem, st>>>(tmA, tmB, tmSA, tmSB, args);
   return cuda_status(cudaGetLastError());
+}
+
+template <bool NV, bool TS>
+int launch_tiles(const uint8_t* w, const void* ws, const uint8_t* x, const void* xs, int64_t n,
+                 float* y, int64_t m, int64_t k, const float* gw, const float* gx, cudaStream_t st) {
+  if (n <= 64)
+    return launch_nt<NV, 64, TS>(w, ws, x, xs, static_cast<int>(n), y, static_cast<int>(m),
+                                 static_cast<int>(k), gw, gx, st);
+  return launch_nt<NV, 128, TS>(w, ws, x, xs, static_cast<int>(n), y, static_cast<int>(m),
+                                static_cast<int>(k), gw, gx, st);
 }
 
 template <bool NV>
@@ -320,11 +384,11 @@ int launch_fp4(const uint8_t* w, const void* ws, const uint8_t* x, const void* x
   if (k % 32 != 0 || m > (1 << 30) || n > (1 << 30) || k > (1 << 30)) return LP_ERR_UNSUPPORTED;
   // TMA: 16-byte aligned bases and row strides (k/2 bytes)
   if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) return LP_ERR_UNSUPPORTED;
-  if (n <= 64)
-    return launch_nt<NV, 64>(w, ws, x, xs, static_cast<int>(n), y, static_cast<int>(m),
-                             static_cast<int>(k), gw, gx, st);
-  return launch_nt<NV, 128>(w, ws, x, xs, static_cast<int>(n), y, static_cast<int>(m),
-                            static_cast<int>(k), gw, gx, st);
+  // scale tiles by TMA when the scale rows are 16-byte multiples and aligned
+  const bool ts = k % 256 == 0 &&
+                  ((reinterpret_cast<uintptr_t>(ws) | reinterpret_cast<uintptr_t>(xs)) & 15) == 0;
+  return ts ? launch_tiles<NV, true>(w, ws, x, xs, n, y, m, k, gw, gx, st)
+            : launch_tiles<NV, false>(w, ws, x, xs, n, y, m, k, gw, gx, st);
 }
 
 }  // namespace

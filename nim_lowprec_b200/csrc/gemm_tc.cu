@@ -14,6 +14,10 @@
 //              128-byte swizzle -- weights [128 rows x 128 B] and activations
 //              [NT columns x 128 B] (xq is K x n column-major, so both are
 //              K-major) -- into a kStages-deep ring.
+//   warps 2-3  (dequantGemmI4Q8 only) widen the stage's packed int4 weight
+//              tile, loaded by TMA as [128 rows x 64 B], to the int8 A tile
+//              in the 128-byte-swizzled layout the MMA reads (two rows per
+//              thread), then release it to the MMA issuer.
 //   warp 1     owns the TMEM allocation; one lane issues the stage's four
 //              MMAs (one per group, M=128, N=NT, K=32) into the four
 //              accumulators of TMEM stage slot kb mod ER and commits once to
@@ -65,7 +69,17 @@ constexpr uint32_t idesc_i8() {
          (static_cast<uint32_t>(128 >> 4) << 24);
 }
 
-template <int NT>
+// Two's-complement nibbles (low = even column) of a packed word -> the eight
+// int8 values in column order: out[0] = columns 0-3, out[1] = columns 4-7.
+__device__ __forceinline__ void widen_i4(uint32_t w, uint32_t& o0, uint32_t& o1) {
+  uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+  lo |= (lo & 0x08080808u) * 0x1Eu;  // sign-extend each byte: n >= 8 -> n - 16
+  hi |= (hi & 0x08080808u) * 0x1Eu;
+  o0 = prmt(lo, hi, 0x5140u);
+  o1 = prmt(lo, hi, 0x7362u);
+}
+
+template <int NT, bool I4>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const TcArgs a) {
@@ -75,9 +89,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int ER = static_cast<int>(kTmemCols) / (4 * NT);  // TMEM stage slots
   constexpr int A_BYTES = 128 * kKStage;
   constexpr int B_BYTES = NT * kKStage;
-  constexpr int STAGE = A_BYTES + B_BYTES;
+  constexpr int RAW_BYTES = I4 ? 128 * kKStage / 2 : 0;  // packed int4 tile
+  constexpr int STAGE = A_BYTES + B_BYTES + RAW_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t full[kStages], empty[kStages], tfull[ER], tempty[ER], mma_done;
+  __shared__ uint64_t full[kStages], empty[kStages], cvt[kStages], tfull[ER], tempty[ER], mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int s_abort;
 
@@ -92,6 +107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&cvt[s], 2);
     }
     for (int e = 0; e < ER; ++e) {
       mbar_init(&tfull[e], 1);
@@ -116,8 +132,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, &s_abort)) break;
         if (s_abort) break;
         uint8_t* st = smem + s * STAGE;
-        mbar_arrive_expect_tx(&full[s], STAGE);
-        tma_load_2d(st, &tmA, kb * kKStage, m0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], (I4 ? RAW_BYTES : A_BYTES) + B_BYTES);
+        if (I4) tma_load_2d(st + A_BYTES + B_BYTES, &tmA, kb * (kKStage / 2), m0, &full[s]);
+        else tma_load_2d(st, &tmA, kb * kKStage, m0, &full[s]);
         tma_load_2d(st + A_BYTES, &tmB, kb * kKStage, n0, &full[s]);
       }
       // never leave with a tile still landing in shared memory
@@ -132,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kb % kStages;
         const int e = kb % ER;
         if (!mbar_wait(&full[s], (kb / kStages) & 1, &s_abort)) break;
+        if (I4 && !mbar_wait(&cvt[s], (kb / kStages) & 1, &s_abort)) break;
         if (kb >= ER && !mbar_wait(&tempty[e], ((kb / ER) - 1) & 1, &s_abort)) break;
         fence_after();
         const uint8_t* st = smem + s * STAGE;
@@ -146,7 +164,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0);
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // ------------------------------------------- int4 -> int8 converters
+    if constexpr (I4) {
+      const int t = threadIdx.x - 64;  // 0..63
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        // the producer reloaded this stage only after its previous MMAs
+        // completed, so the A tile is free once the new data has landed
+        if (!mbar_wait(&full[s], (kb / kStages) & 1, &s_abort)) break;
+        uint8_t* st = smem + s * STAGE;
+        const uint8_t* raw = st + A_BYTES + B_BYTES;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = t + 64 * h;
+          const uint4 u0 = reinterpret_cast<const uint4*>(raw + r * (kKStage / 2))[0];
+          const uint4 u1 = reinterpret_cast<const uint4*>(raw + r * (kKStage / 2))[1];
+          const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = packed words 2c, 2c+1
+            uint32_t o[4];
+            widen_i4(w[2 * c], o[0], o[1]);
+            widen_i4(w[2 * c + 1], o[2], o[3]);
+            // 128-byte swizzle: chunk c of row r at chunk c ^ (r & 7)
+            *reinterpret_cast<uint4*>(st + r * kKStage + ((c ^ (r & 7)) << 4)) =
+                make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&cvt[s]);
+      }
+    }
+  } else {
     // ------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter = 32 rows
     const int h = (warp - 4) >> 2;          // column slice
@@ -262,18 +312,19 @@ bool encode_rows(CUtensorMap* tm, const void* base, int64_t k, int64_t rows, int
   return encode_u8(tm, base, k, rows, kKStage, box_rows, true);
 }
 
-template <int NT>
-int launch_nt(const int8_t* wq, const float* ws, const int8_t* xq, const float* xs, int n,
+template <int NT, bool I4>
+int launch_nt(const void* wq, const float* ws, const int8_t* xq, const float* xs, int n,
               float* y, int m, int k, cudaStream_t st) {
   const int gpr = k / 32;
   CUtensorMap tmA, tmB;
-  if (!encode_rows(&tmA, wq, k, m, 128) || !encode_rows(&tmB, xq, k, n, NT))
-    return LP_ERR_UNSUPPORTED;
-  constexpr int STAGE = (128 + NT) * kKStage;
+  const bool aok = I4 ? encode_u8(&tmA, wq, k / 2, m, kKStage / 2, 128, false)
+                      : encode_rows(&tmA, wq, k, m, 128);
+  if (!aok || !encode_rows(&tmB, xq, k, n, NT)) return LP_ERR_UNSUPPORTED;
+  constexpr int STAGE = (128 + NT) * kKStage + (I4 ? 128 * kKStage / 2 : 0);
   const int smem = 1024 + stages_for<NT>() * STAGE + gpr * NT * 4;
   const DeviceInfo& di = device_info();
   if (smem > di.max_smem_optin - 2048) return LP_ERR_UNSUPPORTED;  // (static smem: 1 KB)
-  auto kern = k_gemm_tc<NT>;
+  auto kern = k_gemm_tc<NT, I4>;
   static int attr_set[kMaxDevices];
   const int slot = di.ordinal % kMaxDevices;
   if (attr_set[slot] < smem) {
@@ -294,7 +345,7 @@ int launch_nt(const int8_t* wq, const float* ws, const int8_t* xq, const float* 
 // Tensor-core dequantGemmQ8 for 32-wide groups, K a multiple of 128 and
 // 16-byte aligned operands; LP_ERR_UNSUPPORTED otherwise (the caller then
 // runs the CUDA-core kernel).
-int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* xq,
+int launch_gemm_tc(const void* wq, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
                    const float* xs, int64_t n, float* y, int64_t m, int64_t k,
                    cudaStream_t st) {
   if (gs != 32 || k % kKStage != 0 || k <= 0 || m <= 0 || n <= 0) return LP_ERR_UNSUPPORTED;
@@ -302,12 +353,12 @@ int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* 
   const uintptr_t al = reinterpret_cast<uintptr_t>(wq) | reinterpret_cast<uintptr_t>(xq) |
                        reinterpret_cast<uintptr_t>(ws);
   if (al & 15) return LP_ERR_UNSUPPORTED;
-  if (n <= 64) {
-    return launch_nt<16>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
-                         static_cast<int>(k), st);
-  }
-  return launch_nt<32>(wq, ws, xq, xs, static_cast<int>(n), y, static_cast<int>(m),
-                       static_cast<int>(k), st);
+  const int ni = static_cast<int>(n), mi = static_cast<int>(m), ki = static_cast<int>(k);
+  if (packed_i4)
+    return n <= 64 ? launch_nt<16, true>(wq, ws, xq, xs, ni, y, mi, ki, st)
+                   : launch_nt<32, true>(wq, ws, xq, xs, ni, y, mi, ki, st);
+  return n <= 64 ? launch_nt<16, false>(wq, ws, xq, xs, ni, y, mi, ki, st)
+                 : launch_nt<32, false>(wq, ws, xq, xs, ni, y, mi, ki, st);
 }
 
 unsigned int take_error_gemm_tc() {

@@ -89,7 +89,7 @@ int launch_dequantize_nvfp4(const uint8_t* codes, const uint8_t* scales, float g
                             float* dst, cudaStream_t st);
 
 // GEMM (gemm_tc.cu: tcgen05, LP_ERR_UNSUPPORTED outside its shapes; gemm.cu: CUDA cores)
-int launch_gemm_tc(const int8_t* wq, const float* ws, int64_t gs, const int8_t* xq,
+int launch_gemm_tc(const void* wq, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
                    const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);
 int launch_gemm(const uint8_t* w, int packed_i4, const float* ws, int64_t gs, const int8_t* xq,
                 const float* xs, int64_t n, float* y, int64_t m, int64_t k, cudaStream_t st);

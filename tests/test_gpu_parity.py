@@ -488,6 +488,24 @@ def test_gemm_q8_tensor_core_shapes(M, K, n):
     assert_bits(to_host(y), want)
 
 
+@pytest.mark.parametrize("M,K,n", [(128, 128, 17), (129, 512, 64), (300, 256, 64),
+                                   (256, 512, 100), (128, 4096, 512), (257, 384, 65)])
+def test_gemm_i4q8_tensor_core_shapes(M, K, n):
+    """dequantGemmI4Q8 (simd/dequant.nim:1460-1583) past 16 columns runs on
+    tcgen05 kind::i8: the packed int4 tile is widened to int8 in shared memory
+    before the MMA; bit-exact like every other path."""
+    w = weights(M + K + n + 1, M * K)
+    x = acts(M + K + n + 1, K * n)
+    ws = O.calibrateSymmetric(w, 32, 7.0)
+    wp = O.packInt4(O.quantize(w, ws, 32, "i4"))
+    xq, xd = O.quantizeQ8_0Split(x)
+    want = O.dequantGemmI4Q8(wp, ws, 32, xq, xd, n)
+    d = to_dev(wp, ws, xq, xd)
+    y = dev_y(M * n)
+    L.dequantGemmI4Q8(*d[:2], 32, *d[2:], n, y)
+    assert_bits(to_host(y), want)
+
+
 @pytest.mark.parametrize("M,K,n", [(1, 32, 1), (37, 512, 2), (300, 256, 3), (149, 4096, 7),
                                    (4100, 1024, 8), (333, 512, 9), (150, 2048, 16),
                                    (64, 512, 17), (97, 11008, 8)])
