@@ -216,7 +216,9 @@ class Cfg4Workload:
     matrix and of down (P divides both; the reference's slicing).  A step is
     one decode sweep: per layer, quantizeQ8_0 + dequantGemvI4Q8 over the
     concatenated matrix and over down, each one launch; with P > 1 each is the
-    pooled call, whose output (38400 / 4096 floats) every rank ends up holding."""
+    pooled call; the two outputs of a layer (38400 + 4096 floats, side by side)
+    form one gather group, so every rank holds the layer's whole output after
+    one exchange."""
 
     def __init__(self, torch, L, world, rank, layers=LAYERS):
         assert CAT_ROWS % world == 0 and DOWN_ROWS % world == 0
@@ -242,11 +244,13 @@ class Cfg4Workload:
                                  dtype=torch.float32)
         self.x = self.xflat[:layers * K1].view(layers, K1)
         self.xd = self.xflat[layers * K1:].view(layers, DOWN_K)
-        # every layer's outputs (whole vectors) in one flat buffer
+        # every layer's outputs in one flat buffer, a layer's two whole
+        # vectors side by side (one gathered vector per layer)
         self.yflat = torch.zeros(layers * (CAT_ROWS + DOWN_ROWS), dtype=torch.float32,
                                  device="cuda")
-        self.ycat = self.yflat[:layers * CAT_ROWS].view(layers, CAT_ROWS)
-        self.ydown = self.yflat[layers * CAT_ROWS:].view(layers, DOWN_ROWS)
+        self.ylayer = self.yflat.view(layers, CAT_ROWS + DOWN_ROWS)
+        self.ycat = self.ylayer[:, :CAT_ROWS]
+        self.ydown = self.ylayer[:, CAT_ROWS:]
         torch.cuda.empty_cache()
 
     def layer(self, pool, layer):
@@ -259,10 +263,13 @@ class Cfg4Workload:
             return
         from nim_lowprec_b200 import parallel as P
         st = P._stream()
+        # the layer's two GEMVs push into one gathered vector, received once
+        pool.group_begin(self.ylayer[layer])
         for w, s, x, y in ((self.wc[layer], self.sc[layer], self.x[layer], self.ycat[layer]),
                            (self.wd[layer], self.sd[layer], self.xd[layer], self.ydown[layer])):
             pool.call("lp_pool_quantize_dequant_gemv_i4q8", w.data_ptr(), w.numel(), s.data_ptr(),
                       s.numel(), 32, x.data_ptr(), x.numel(), y.data_ptr(), y.numel(), st)
+        pool.group_end()
 
     def sweep(self, pool):
         for layer in range(self.layers):
@@ -785,7 +792,7 @@ def main():
         return 1
     if rank != 0:
         return 0
-    launches_per_step = 2 * LAYERS * (2 if world > 1 else 1)
+    launches_per_step = LAYERS * (3 if world > 1 else 2)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6),
@@ -798,9 +805,9 @@ def main():
             "weight_bytes_per_step": sweep_bytes, "layers": LAYERS,
             "rows_per_gpu": {"concatenated": CAT_ROWS // world, "down": DOWN_ROWS // world},
             "parallelism": "single GPU" if world == 1 else
-                           f"rows sharded over {world} GPUs (library pool, reference slicing); each "
-                           "GEMV's output assembled on every GPU by NVLink peer stores from the GEMV "
-                           "plus a receive kernel",
+                           f"rows sharded over {world} GPUs (library pool, reference slicing); a "
+                           "layer's outputs assembled on every GPU by NVLink peer stores from both "
+                           "GEMVs plus one receive kernel per layer",
             "l2": f"{sweep_bytes // world / 1e6:.0f} MB of weights per GPU per step (> 3x L2)",
             "timing": "CUDA-graph replays, CUDA events on the launching stream, max over ranks",
         },

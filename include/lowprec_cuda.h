@@ -414,6 +414,17 @@ int lp_pool_size(lp_pool_t pool, int *nranks, int *rank);
  * LP_ERR_UNSUPPORTED: the exchange could not be mapped on every rank. */
 int lp_pool_set_p2p(lp_pool_t pool, int enable);
 int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
+/* Gather group (no counterpart in the reference): pooled calls made between
+ * begin and end whose y lies inside [y, y + y_len) (each its own row-sharded
+ * part of that vector, at most 4) store their rows into the other ranks as
+ * usual, and the whole vector is received once, at end, in stream order --
+ * one exchange for several GEMVs (config 4: a layer's two GEMVs).  Every rank
+ * makes the same calls.  On the NVLink transport a pooled call outside the
+ * vector, or a fifth part, returns LP_ERR_ARG; begin returns
+ * LP_ERR_UNSUPPORTED for a vector larger than the exchange (2^20 floats).
+ * On the NCCL transport every call gathers on its own and end does nothing. */
+int lp_pool_group_begin(lp_pool_t pool, float *y, int64_t y_len);
+int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream);
 /* Gather every rank's row slice of y (m rows of per_row floats) in place:
  * the output exchange inside the reference's par* procs (parallel.nim:186-474),
  * on its own. */

@@ -88,6 +88,8 @@ SIGNATURES = {
     "lp_pool_destroy": "p",
     "lp_pool_size": "ppp",
     "lp_pool_gather_rows": "ppnnp",
+    "lp_pool_group_begin": "ppn",
+    "lp_pool_group_end": "pp",
     "lp_pool_set_p2p": "pi",
     "lp_pool_get_p2p": "pp",
     "lp_pool_dequant_gemv": "ppnpnnpnpnp",

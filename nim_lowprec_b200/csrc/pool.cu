@@ -40,6 +40,14 @@ constexpr int64_t kXchgBytes = 2 * kXchgFloats * 8;  // two halves of 8-byte wor
 struct PeerBufs {
   uint8_t* p[kMaxP2pRanks];
 };
+// A gathered vector made of up to kMaxParts regions, each m rows of per_row
+// floats at element offset off, its rows sliced over the ranks.
+constexpr int kMaxParts = 4;
+struct GatherParts {
+  int64_t off[kMaxParts], m[kMaxParts], prow[kMaxParts];
+  int send[kMaxParts];  // 1: the receive kernel also stores this rank's rows of the part
+  int n;
+};
 }  // namespace
 
 struct lp_pool {
@@ -51,6 +59,12 @@ struct lp_pool {
   uint32_t* state; // [0] gathers finished, [1] CTAs finished in the current one
   PeerBufs peers;  // every rank's exchange buffer as mapped here
   lp::PushCtx* push;  // device copy of peers/state for the GEMVs' own stores
+  // gather group (lp_pool_group_begin/end): pooled calls whose outputs are
+  // parts of one vector push into it and the group receives once
+  bool grp;
+  float* grp_y;
+  int64_t grp_len;
+  GatherParts grp_parts;
 };
 
 namespace {
@@ -138,9 +152,8 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 // complete before it reads the gather count: that GEMV had waited for the
 // previous gather in turn, so the count is final, and this gather completes
 // only after its GEMV has.
-__global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t per_row,
-                                                   int nranks, int rank, PeerBufs peers,
-                                                   uint32_t* state, int send) {
+__global__ void __launch_bounds__(256) k_gather_p2p(float* y, GatherParts parts, int nranks,
+                                                   int rank, PeerBufs peers, uint32_t* state) {
   __shared__ uint32_t s_e;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t C = gridDim.x;
@@ -151,48 +164,54 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
   const uint32_t e = s_e;
   const uint64_t tag = static_cast<uint64_t>(e) << 32;
   const int64_t half = (e & 1u) * kXchgFloats;
-  int64_t b, en;
-  rows_of(m, nranks, rank, &b, &en);
-  const int64_t off = b * per_row, len = (en - b) * per_row;
-  const int64_t chunk = (len + C - 1) / C;
-  const int64_t lo = min(len, blockIdx.x * chunk), hi = min(len, lo + chunk);
-  for (int64_t i = lo + tid; send && i < hi; i += nthr) {
-    const uint64_t w = tag | __float_as_uint(y[off + i]);
-    for (int q = 0; q < nranks; ++q)
-      if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
+  for (int pi = 0; pi < parts.n; ++pi) {
+    if (!parts.send[pi]) continue;
+    int64_t b, en;
+    rows_of(parts.m[pi], nranks, rank, &b, &en);
+    const int64_t off = parts.off[pi] + b * parts.prow[pi], len = (en - b) * parts.prow[pi];
+    const int64_t chunk = (len + C - 1) / C;
+    const int64_t lo = min(len, blockIdx.x * chunk), hi = min(len, lo + chunk);
+    for (int64_t i = lo + tid; i < hi; i += nthr) {
+      const uint64_t w = tag | __float_as_uint(y[off + i]);
+      for (int q = 0; q < nranks; ++q)
+        if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
+    }
   }
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(peers.p[rank]) + half;
   bool ok = true;
   const uint64_t t0 = lp::global_ns();
-  for (int q = 0; q < nranks && ok; ++q) {
-    if (q == rank) continue;
-    int64_t qb, qe;
-    rows_of(m, nranks, q, &qb, &qe);
-    const int64_t qo = qb * per_row, ql = (qe - qb) * per_row;
-    const int64_t qc = (ql + C - 1) / C;
-    const int64_t qlo = min(ql, blockIdx.x * qc), qhi = min(ql, qlo + qc);
-    // eight words in flight per thread, then wait on any that is not there yet
-    for (int64_t i0 = qlo + tid; i0 < qhi && ok; i0 += 8 * nthr) {
-      uint64_t w[8];
+  for (int pi = 0; pi < parts.n && ok; ++pi) {
+    for (int q = 0; q < nranks && ok; ++q) {
+      if (q == rank) continue;
+      int64_t qb, qe;
+      rows_of(parts.m[pi], nranks, q, &qb, &qe);
+      const int64_t qo = parts.off[pi] + qb * parts.prow[pi];
+      const int64_t ql = (qe - qb) * parts.prow[pi];
+      const int64_t qc = (ql + C - 1) / C;
+      const int64_t qlo = min(ql, blockIdx.x * qc), qhi = min(ql, qlo + qc);
+      // eight words in flight per thread, then wait on any that is not there yet
+      for (int64_t i0 = qlo + tid; i0 < qhi && ok; i0 += 8 * nthr) {
+        uint64_t w[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int64_t i = i0 + k * nthr;
-        w[k] = i < qhi ? ld_word(mine + qo + i) : 0;
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int64_t i = i0 + k * nthr;
-        if (i >= qhi || !ok) continue;
-        for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
-          if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
-            lp::raise_error(LP_ERR_TIMEOUT);
-            ok = false;
-            break;
-          }
-          __nanosleep(64);  // leave the issue slots to the GEMV on this SM
-          w[k] = ld_word(mine + qo + i);
+        for (int k = 0; k < 8; ++k) {
+          const int64_t i = i0 + k * nthr;
+          w[k] = i < qhi ? ld_word(mine + qo + i) : 0;
         }
-        if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w[k]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int64_t i = i0 + k * nthr;
+          if (i >= qhi || !ok) continue;
+          for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
+            if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
+              lp::raise_error(LP_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+            __nanosleep(64);  // leave the issue slots to the GEMV on this SM
+            w[k] = ld_word(mine + qo + i);
+          }
+          if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w[k]));
+        }
       }
     }
   }
@@ -208,12 +227,15 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, int64_t m, int64_t
   }
 }
 
-int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {
-  const int64_t total = m * per_row;
-  const int64_t per_rank = (total + p->nranks - 1) / p->nranks;
+int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st) {
+  int64_t total = 0, per_rank = 0;
+  for (int i = 0; i < parts.n; ++i) {
+    total += parts.m[i] * parts.prow[i];
+    per_rank += (parts.m[i] / p->nranks + 1) * parts.prow[i];
+  }
   // CTAs enough for ~1024 received words each, at most 64 (all resident at
   // once on 148 SMs: a sending CTA waits only after its own stores)
-  const int64_t recv = total - per_rank;
+  const int64_t recv = std::max<int64_t>(0, total - per_rank);
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(64, (recv + 1023) / 1024)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -224,8 +246,18 @@ int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, m, per_row, p->nranks, p->rank,
-                                            p->peers, p->state, send));
+  return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, parts, p->nranks, p->rank,
+                                            p->peers, p->state));
+}
+
+int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {
+  GatherParts parts{};
+  parts.n = 1;
+  parts.off[0] = 0;
+  parts.m[0] = m;
+  parts.prow[0] = per_row;
+  parts.send[0] = send;
+  return gather_parts(p, y, parts, st);
 }
 
 // y[0, m*per_row) from every rank's slice of rows.
@@ -451,6 +483,27 @@ int lp_pool_get_p2p(lp_pool_t pool, int* enabled) {
   return LP_OK;
 }
 
+int lp_pool_group_begin(lp_pool_t pool, float* y, int64_t y_len) {
+  if (!pool || y_len < 0 || (y_len > 0 && !y) || pool->grp) return LP_ERR_ARG;
+  if (pool->p2p && y_len > kXchgFloats) return LP_ERR_UNSUPPORTED;  // beyond the exchange buffer
+  pool->grp = true;
+  pool->grp_y = y;
+  pool->grp_len = y_len;
+  pool->grp_parts.n = 0;
+  return LP_OK;
+}
+
+int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream) {
+  if (!pool || !pool->grp) return LP_ERR_ARG;
+  pool->grp = false;
+  if (pool->grp_parts.n == 0 || pool->nranks < 2) return LP_OK;
+  int r = lp::cuda_status(cudaSetDevice(pool->device));
+  if (r) return r;
+  r = gather_parts(pool, pool->grp_y, pool->grp_parts, S(stream));
+  pool->grp_parts.n = 0;
+  return r;
+}
+
 int lp_pool_gather_rows(lp_pool_t pool, float* y, int64_t m, int64_t per_row, lp_stream_t stream) {
   if (!pool || m < 0 || per_row < 1 || (m > 0 && !y)) return LP_ERR_ARG;
   int r = lp::cuda_status(cudaSetDevice(pool->device));
@@ -473,9 +526,16 @@ int lp_pool_gather_rows(lp_pool_t pool, float* y, int64_t m, int64_t per_row, lp
   rows_of(m_, pool->nranks, pool->rank, &b_, &e_);                    \
   float* yl_ = y + b_ * (per_row);                                    \
   const int64_t yl_len_ = (e_ - b_) * (per_row);                      \
-  const bool fuse_ = pool->p2p && pool->push && m_ * (per_row) <= kXchgFloats; \
+  /* inside a gather group: this output is a part of the group's vector */ \
+  const int64_t goff_ = pool->grp ? static_cast<int64_t>(y - pool->grp_y) : 0; \
+  const bool ingrp_ = pool->grp && pool->p2p && pool->push && goff_ >= 0 &&   \
+                      goff_ + (ylen) <= pool->grp_len && pool->grp_parts.n < kMaxParts; \
+  /* an open group on the exchange takes every pooled call as a part */ \
+  if (pool->grp && pool->p2p && pool->push && !ingrp_) return LP_ERR_ARG; \
+  const bool fuse_ = pool->p2p && pool->push &&                        \
+                     (ingrp_ ? pool->grp_len : m_ * (per_row)) <= kXchgFloats; \
   lp::g_push = fuse_ ? pool->push : nullptr;                          \
-  lp::g_push_off = b_ * (per_row);                                    \
+  lp::g_push_off = goff_ * ingrp_ + b_ * (per_row);                   \
   lp::g_pushed = false;
 
 // The local GEMV stored its outputs into the other ranks already (fused
@@ -487,6 +547,17 @@ int lp_pool_gather_rows(lp_pool_t pool, float* y, int64_t m, int64_t per_row, lp
   lp::g_push = nullptr;                                               \
   lp::g_pushed = false;                                               \
   if (r_) return r_;                                                  \
+  if (ingrp_ && pool->nranks > 1) {                                   \
+    /* received with the rest of the group at lp_pool_group_end; a   \
+       kernel without the push has its rows sent there too */         \
+    GatherParts& gp_ = pool->grp_parts;                               \
+    gp_.off[gp_.n] = goff_;                                           \
+    gp_.m[gp_.n] = m_;                                                \
+    gp_.prow[gp_.n] = per_row;                                     \
+    gp_.send[gp_.n] = pushed_ ? 0 : 1;                                \
+    ++gp_.n;                                                          \
+    return LP_OK;                                                     \
+  }                                                                   \
   if (pushed_ && pool->nranks > 1)                                    \
     return gather_p2p(pool, y, m_, per_row, S(stream), 0);            \
   return gather(pool, y, m_, per_row, S(stream));

@@ -139,6 +139,14 @@ class NcclPool:
     def call(self, name: str, *args):
         N.check(getattr(N.lib(), name)(self._h, *args), name)
 
+    def group_begin(self, y):
+        """Pooled calls until group_end write parts of y and are received
+        once (lp_pool_group_begin)."""
+        N.check(N.lib().lp_pool_group_begin(self._h, _dev(y), _numel(y)), "lp_pool_group_begin")
+
+    def group_end(self):
+        N.check(N.lib().lp_pool_group_end(self._h, _stream()), "lp_pool_group_end")
+
     @property
     def p2p(self) -> bool:
         """True when gathers use the NVLink exchange buffers (the default when

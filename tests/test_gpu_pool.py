@@ -131,6 +131,31 @@ def _rank_main(rank, world, port, q):
                 y_ = torch.full((Mp,), float("nan"), device="cuda")
                 par(npl, w_, pws, R.PAR_GS, pxq, pxs, y_)
                 same(f"pooled-{tag}-M{Mp}", y_, ref_)
+        # a gather group: two pooled GEMVs (pushing) and a wide pooled GEMM
+        # (tensor-core path, which does not push) as parts of one vector,
+        # received once -- the single-GPU bits, twice in a row
+        npl = pools[1]
+        if npl.p2p:
+            ng = 24
+            refq8 = torch.empty(M, device="cuda")
+            L.dequantGemvQ8(wq, wd, 32, xq[:K], xd[:K // 32], refq8)
+            refq4 = torch.empty(M, device="cuda")
+            L.dequantGemvQ4_0(blk, K // 32, x[:K], refq4)
+            xqg = torch.empty(K * ng, dtype=torch.int8, device="cuda")
+            xdg = torch.empty(K * ng // 32, device="cuda")
+            L.quantizeQ8_0Split(rnd(K * ng), xqg, xdg)
+            refgm = torch.empty(M * ng, device="cuda")
+            L.dequantGemmQ8(wq, wd, 32, xqg, xdg, ng, refgm)
+            for rep_ in range(2):
+                yg = torch.full((2 * M + M * ng,), float("nan"), device="cuda")
+                npl.group_begin(yg)
+                P.parDequantGemvQ8(npl, wq, wd, 32, xq[:K], xd[:K // 32], yg[:M])
+                P.parDequantGemvQ4_0(npl, blk, K // 32, x[:K], yg[M:2 * M])
+                P.parDequantGemmQ8(npl, wq, wd, 32, xqg, xdg, ng, yg[2 * M:])
+                npl.group_end()
+                same(f"group{rep_}-q8", yg[:M], refq8)
+                same(f"group{rep_}-q4_0", yg[M:2 * M], refq4)
+                same(f"group{rep_}-gemm", yg[2 * M:], refgm)
         # the library pool gathers over NVLink by default (one GPU per rank);
         # both transports, back-to-back gathers (alternating exchange halves)
         # and CUDA-graph replays give the single-GPU bits
