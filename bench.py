@@ -253,46 +253,74 @@ class Cfg4Workload:
         self.ydown = self.ylayer[:, CAT_ROWS:]
         torch.cuda.empty_cache()
 
-    def layer(self, pool, layer):
+    def calls(self, pool, layer, ycat=None, ydown=None):
+        """The layer's two GEMVs (pooled when a pool is given)."""
         L = self.L
+        yc = self.ycat[layer] if ycat is None else ycat
+        yd = self.ydown[layer] if ydown is None else ydown
         if pool is None:
-            L.quantizeDequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.x[layer],
-                                      self.ycat[layer])
-            L.quantizeDequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.xd[layer],
-                                      self.ydown[layer])
+            L.quantizeDequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.x[layer], yc)
+            L.quantizeDequantGemvI4Q8(self.wd[layer], self.sd[layer], 32, self.xd[layer], yd)
             return
         from nim_lowprec_b200 import parallel as P
         st = P._stream()
-        # the layer's two GEMVs push into one gathered vector, received once
-        pool.group_begin(self.ylayer[layer])
-        for w, s, x, y in ((self.wc[layer], self.sc[layer], self.x[layer], self.ycat[layer]),
-                           (self.wd[layer], self.sd[layer], self.xd[layer], self.ydown[layer])):
+        for w, s, x, y in ((self.wc[layer], self.sc[layer], self.x[layer], yc),
+                           (self.wd[layer], self.sd[layer], self.xd[layer], yd)):
             pool.call("lp_pool_quantize_dequant_gemv_i4q8", w.data_ptr(), w.numel(), s.data_ptr(),
                       s.numel(), 32, x.data_ptr(), x.numel(), y.data_ptr(), y.numel(), st)
+
+    def layer(self, pool, layer):
+        """Per-call form: two launches; pooled, one gather group per layer."""
+        if pool is None:
+            self.calls(None, layer)
+            return
+        pool.group_begin(self.ylayer[layer])
+        self.calls(pool, layer)
         pool.group_end()
 
-    def sweep(self, pool):
-        for layer in range(self.layers):
-            self.layer(pool, layer)
+    def sweep(self, pool, batched=True):
+        """One decode sweep.  Batched (the headline): the 64 GEMVs queued in
+        one lp_batch and run as one persistent launch; pooled, every GEMV's
+        rows go to the other GPUs from its fold as they are made, and one
+        gather group over the whole sweep receives them once at the end (no
+        layer here reads another layer's output).  Per call: one launch per
+        GEMV and, pooled, one receive per layer."""
+        if not batched:
+            for layer in range(self.layers):
+                self.layer(pool, layer)
+            return
+        with self.L.batch():
+            if pool is not None:
+                pool.group_begin(self.yflat)
+            for layer in range(self.layers):
+                self.calls(pool, layer)
+            if pool is not None:
+                pool.group_end()
+
+    def local_sweep(self, ylc, yld):
+        """This rank's rows of the batched sweep, no pool (the roofline's kernel)."""
+        with self.L.batch():
+            for layer in range(self.layers):
+                self.calls(None, layer, ylc[layer], yld[layer])
 
     def local_cat(self, layer, out):
         """This rank's concatenated-matrix GEMV alone (the dominant kernel)."""
         self.L.quantizeDequantGemvI4Q8(self.wc[layer], self.sc[layer], 32, self.x[layer], out)
 
-    def check(self, pool, dist, layers=None):
-        """Parity before timing.  For layers {0, last}: the pooled (or single
-        GPU) sweep's whole outputs equal every rank's single-GPU rows bit for
-        bit (gathered with torch.distributed), and on rank 0 sampled rows equal
-        the CPU oracle of the reference (quantizeQ8_0 then dequantGemvI4Q8)."""
+    def check(self, pool, dist, batched=True, layers=None):
+        """Parity before timing, of the sweep form that is timed: one whole
+        sweep, then for layers {0, last} its whole outputs equal every rank's
+        single-GPU rows bit for bit (gathered with torch.distributed), and on
+        rank 0 sampled rows equal the CPU oracle of the reference (quantizeQ8_0
+        then dequantGemvI4Q8)."""
         torch, L = self.torch, self.L
         from oracle import oracle as O
         layers = layers or sorted({0, self.layers - 1})
-        out = {"layers": layers, "rows_compared": 0, "mismatches": 0, "oracle_rows": 0,
-               "oracle_mismatches": 0}
+        out = {"form": "batched" if batched else "per call", "layers": layers,
+               "rows_compared": 0, "mismatches": 0, "oracle_rows": 0, "oracle_mismatches": 0}
+        self.yflat.fill_(float("nan"))
+        self.sweep(pool, batched)
         for layer in layers:
-            self.ycat[layer].fill_(float("nan"))
-            self.ydown[layer].fill_(float("nan"))
-            self.layer(pool, layer)
             for w, s, x, yw, rows in ((self.wc, self.sc, self.x, self.ycat, self.rc),
                                       (self.wd, self.sd, self.xd, self.ydown, self.rd)):
                 loc = torch.empty(rows, dtype=torch.float32, device="cuda")
@@ -631,9 +659,11 @@ def main():
 
     # ---------------- headline: config 4, strong scaling over the N GPUs
     wl4 = Cfg4Workload(torch, L, world, rank)
-    par4 = wl4.check(pool, dist)
-    if max_over_ranks(par4["mismatches"] + par4["oracle_mismatches"]) > 0:
-        failures.append(f"config 4 parity: {par4}")
+    par4 = wl4.check(pool, dist, batched=True)
+    par4c = wl4.check(pool, dist, batched=False)
+    if max_over_ranks(par4["mismatches"] + par4["oracle_mismatches"] +
+                      par4c["mismatches"] + par4c["oracle_mismatches"]) > 0:
+        failures.append(f"config 4 parity: {par4} {par4c}")
 
     clk = ClockSampler(device_uuid(torch))
     clk.start()
@@ -645,18 +675,31 @@ def main():
     sweep_bytes = LAYERS * cfg4_bytes_per_layer()
     value = sweep_bytes / (per_step_ms / 1e3) / 1e9
 
-    # roofline of the dominant kernel: this rank's 38400/N-row GEMV (quantize
-    # fused), timed alone over the 32 layers' matrices (weights > 3x L2)
-    ycl = torch.empty(wl4.rc, dtype=torch.float32, device="cuda")
-    kms, g2 = graph_time(torch, lambda i: wl4.local_cat(i % LAYERS, ycl), 640, 3, barrier, chunk=320)
+    # the same sweep with one launch per GEMV (and, pooled, a receive per layer)
+    cms, gc = graph_time(torch, lambda i: wl4.sweep(pool, batched=False), args.steps, W, barrier,
+                         chunk=50)
+    del gc
+    per_call_ms = max_over_ranks(cms) / args.steps
+    per_call = {"GB/s": round(sweep_bytes / (per_call_ms / 1e3) / 1e9, 1),
+                "ms_per_sweep": round(per_call_ms, 4), "launches_per_sweep":
+                LAYERS * (3 if world > 1 else 2), "parity": par4c}
+
+    # roofline of the dominant kernel: the batch kernel over this rank's rows
+    # of all 64 GEMVs, timed as the unpooled batched sweep (its images kernel
+    # included, so an upper bound on the kernel's time)
+    ylc = torch.empty(LAYERS, wl4.rc, dtype=torch.float32, device="cuda")
+    yld = torch.empty(LAYERS, wl4.rd, dtype=torch.float32, device="cuda")
+    kms, g2 = graph_time(torch, lambda i: wl4.local_sweep(ylc, yld), 100, 3, barrier, chunk=50)
     del g2
-    kernel_us = max_over_ranks(kms / 640 * 1e3)
-    cat_bytes = i4_bytes(wl4.rc, K1) + K1 * 4 + wl4.rc * 4
-    achieved = cat_bytes / (kernel_us / 1e6) / 1e9
-    t4 = traffic.get("gemv_i4q8_cfg4_cat")
+    kernel_us = max_over_ranks(kms / 100 * 1e3)
+    local_bytes = LAYERS * (i4_bytes(wl4.rc, K1) + K1 * 4 + wl4.rc * 4 +
+                            i4_bytes(wl4.rd, DOWN_K) + DOWN_K * 4 + wl4.rd * 4)
+    achieved = local_bytes / (kernel_us / 1e6) / 1e9
+    t4 = traffic.get("gemv_batch_cfg4")
     tr = None
-    if isinstance(t4, dict) and t4.get("rows"):
-        tr = int(round(t4["bytes"] * wl4.rc / t4["rows"]))
+    if isinstance(t4, dict) and t4.get("bytes_per_layer_n1"):
+        # measured on one GPU's full rows; scaled by this rank's share
+        tr = int(round(t4["bytes_per_layer_n1"] * LAYERS / world))
 
     # e2e through the public API: every layer's x from page-locked host
     # memory in, every layer's whole output back, each step
@@ -792,7 +835,7 @@ def main():
         return 1
     if rank != 0:
         return 0
-    launches_per_step = LAYERS * (3 if world > 1 else 2)
+    launches_per_step = 3 if world > 1 else 2  # images + batch kernel (+ the receive)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 6),
@@ -805,9 +848,12 @@ def main():
             "weight_bytes_per_step": sweep_bytes, "layers": LAYERS,
             "rows_per_gpu": {"concatenated": CAT_ROWS // world, "down": DOWN_ROWS // world},
             "parallelism": "single GPU" if world == 1 else
-                           f"rows sharded over {world} GPUs (library pool, reference slicing); a "
-                           "layer's outputs assembled on every GPU by NVLink peer stores from both "
-                           "GEMVs plus one receive kernel per layer",
+                           f"rows sharded over {world} GPUs (library pool, reference slicing); "
+                           "every GEMV's fold stores its rows into the other GPUs over NVLink as "
+                           "it makes them, one receive kernel per sweep assembles all 32 layers' "
+                           "outputs on every GPU",
+            "launch": "one lp_batch per sweep: an images kernel stages the 64 GEMVs' "
+                      "activations, one persistent batch kernel runs the 64 GEMVs",
             "l2": f"{sweep_bytes // world / 1e6:.0f} MB of weights per GPU per step (> 3x L2)",
             "timing": "CUDA-graph replays, CUDA events on the launching stream, max over ranks",
         },
@@ -816,8 +862,10 @@ def main():
                                                 "any mismatch"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": tr,
-                     "kernel": f"gemv_kernel<FmtI4Q8FromF32> over {CAT_ROWS // world}x4096 (quantize "
-                               f"fused), {kernel_us:.3f} us per launch, algorithmic {cat_bytes} B",
+                     "kernel": f"gemv_batch_kernel<FmtI4Q8FromF32>: this GPU's rows of the 64 "
+                               f"GEMVs ({CAT_ROWS // world}x4096 + {DOWN_ROWS // world}x11008 per "
+                               f"layer) in one launch, {kernel_us:.3f} us per launch (images "
+                               f"kernel included), algorithmic {local_bytes} B",
                      "peak_kind": f"{peak_kind} hbm_gbs"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -828,6 +876,7 @@ def main():
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clocks,
     }
+    line["config4_per_call"] = per_call
     if cfg2:
         line["config2_mxfp4_row_sharded"] = cfg2
     line["config1_q4_0_11008x4096"] = cfg1

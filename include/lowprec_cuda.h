@@ -10,9 +10,9 @@
  *
  * Two forms per kernel:
  *   lp_*   DEVICE pointers + a CUDA stream; asynchronous, stream-ordered,
- *          allocates nothing, reentrant across streams.  Activations and
- *          outputs may also be page-locked host memory, passed by the
- *          address lp_host_device_pointer gives.
+ *          allocates nothing (but see lp_batch_begin), reentrant across
+ *          streams.  Activations and outputs may also be page-locked host
+ *          memory, passed by the address lp_host_device_pointer gives.
  *   lph_*  HOST pointers, blocking: the literal drop-in for the Nim
  *          signature.  Stages through a cached per-thread device workspace,
  *          copies every input host->device, runs, copies the output back.
@@ -82,14 +82,44 @@ int lp_host_device_pointer(const void *host, void **dev);
  * not be written by the kernel before it in the stream. */
 int lp_copy_in(void *dst, const void *src, int64_t bytes, lp_stream_t stream);
 
+/* Batched GEMV launches (no counterpart in the reference; the reference
+ * runs each call on the CPU as it comes).  Device-form GEMVs of the
+ * int8-activation formats (lp_dequant_gemv_q8 / _i4q8, the fused
+ * lp_quantize_dequant_gemv_q8 / _i4q8, lp_dequant_gemv_q8_0q8 / _q4_0q8,
+ * and their pooled forms) that this thread makes on `stream` between begin
+ * and end are queued and run as one persistent launch per run of up to 64
+ * consecutive same-format calls: the weights of call i+1 stream while call
+ * i's last rows fold, and each call's activations are staged once, by a small
+ * kernel, for the whole launch.  A lone GEMV pays about 6 us of launch, staging
+ * and fold latency; a decode step of many GEMVs pays it once.
+ * Every call keeps its own checks and its results, bit for bit those of the
+ * call made on its own.  Argument errors return at once.  Queued calls are
+ * launched at end, or earlier when this thread makes any other launch of the
+ * library (stream order holds), a call of another format or stream, a call
+ * whose x or y meets an earlier queued call's y, or a 65th call; a launch
+ * failure is returned by the call that launched, or by end.  y and x
+ * pointers are read at launch, so queued buffers must stay allocated until
+ * then.  Each launch stages the activations in a stream-ordered allocation
+ * (cudaMallocAsync from the device's default pool, a few KB per call, freed
+ * in stream order after it; graph memory nodes under stream capture) -- the
+ * one allocation of the device forms.  Pooled calls in a gather group may
+ * share a launch; the group's receive launches the queue first.  begin on an
+ * open batch ends it. */
+int lp_batch_begin(lp_stream_t stream);
+int lp_batch_end(lp_stream_t stream);
+
 /* ======================= fp32-activation fused dequant-GEMVs ========== */
 
 /* Arithmetic of the fp32-activation GEMVs (process-wide, default FAST).
  *   LP_FP32_FAST   activations as block-float integers (22-bit per group,
- *                  three int8 planes), exact integer group dots: within a few
- *                  ulp of the exact dot, inside the reference's 1e-5 relative
- *                  tolerance, not bit-identical to its summation order.  Used
- *                  when the group size is a multiple of 8.
+ *                  three int8 planes), exact integer group dots: per row the
+ *                  error is a few ulp of sum|w*x| (measured on config 1: at
+ *                  most 4.7e-8 of it), not bit-identical to the reference's
+ *                  summation order.  Where a row's dot cancels, the relative
+ *                  error of that element can pass 1e-5 -- as the reference's
+ *                  own fp32 order does against an fp64 dot (config 1: 195 of
+ *                  11008 rows here, 99 for the reference order).  Used when
+ *                  the group size is a multiple of 8.
  *   LP_FP32_EXACT  the reference scalar path's exact operation order
  *                  (simd/dequant.nim:253-256 and kin): bit-identical results.
  * No counterpart in the reference (its x86 build runs the scalar order).
@@ -416,12 +446,12 @@ int lp_pool_set_p2p(lp_pool_t pool, int enable);
 int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
 /* Gather group (no counterpart in the reference): pooled calls made between
  * begin and end whose y lies inside [y, y + y_len) (each its own row-sharded
- * part of that vector, at most 4) store their rows into the other ranks as
+ * part of that vector, at most 64) store their rows into the other ranks as
  * usual, and the whole vector is received once, at end, in stream order --
  * one exchange for several GEMVs (config 4: a layer's two GEMVs).  Every rank
  * makes the same calls.  On the NVLink transport a pooled call outside the
- * vector, or a fifth part, returns LP_ERR_ARG; begin returns
- * LP_ERR_UNSUPPORTED for a vector larger than the exchange (2^20 floats).
+ * vector, or a 65th part, returns LP_ERR_ARG; begin returns
+ * LP_ERR_UNSUPPORTED for a vector larger than the exchange (2^21 floats).
  * On the NCCL transport every call gathers on its own and end does nothing. */
 int lp_pool_group_begin(lp_pool_t pool, float *y, int64_t y_len);
 int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream);

@@ -8,7 +8,7 @@ API without the built library raises.
 """
 from . import _native
 from .dequant import (  # noqa: F401
-    calibrateMX, calibrateSymmetric, dequantGemmF4, dequantGemmI4Q8, dequantGemmQ8, dequantGemv,
+    batch, calibrateMX, calibrateSymmetric, dequantGemmF4, dequantGemmI4Q8, dequantGemmQ8, dequantGemv,
     dequantGemvF4, dequantGemvI4, dequantGemvI4Q8, dequantGemvQ4_0, dequantGemvQ4_0Q8,
     dequantGemvQ8, dequantGemvQ8_0, dequantGemvQ8_0Q8, dequantGemvQ4_K, dequantGemvQ6_K,
     dequantizeBatch, dequantizeQ4_0Batch,

@@ -85,6 +85,8 @@ SIGNATURES = {
     "lp_pool_rows": "niipp",
     "lp_pool_unique_id": "p",
     "lp_pool_init": "ppiii",
+    "lp_batch_begin": "p",
+    "lp_batch_end": "p",
     "lp_pool_destroy": "p",
     "lp_pool_size": "ppp",
     "lp_pool_gather_rows": "ppnnp",

@@ -75,7 +75,14 @@ namespace {
     if (t_validate_only) return LP_OK;   \
   } while (0)
 
-inline cudaStream_t S(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
+// The stream of a launch.  S: any launch but a GEMV's -- it first launches
+// the GEMVs recorded in this thread's open batch (a failure there is kept for
+// lp_batch_end), so stream order holds.  SG: a GEMV, which may join the batch.
+inline cudaStream_t SG(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
+inline cudaStream_t S(lp_stream_t s) {
+  if (lp::batch_open()) lp::batch_flush_keep();
+  return static_cast<cudaStream_t>(s);
+}
 
 GemvParams base(const void* w, const float* ws, const void* x, const float* xs, float* y,
                 int64_t m, int64_t k, int64_t gs, int64_t gpr, int64_t row_bytes) {
@@ -151,6 +158,10 @@ int lp_device_error(void) {
   return static_cast<int>(e);
 }
 
+int lp_batch_begin(lp_stream_t stream) { return lp::batch_begin(static_cast<cudaStream_t>(stream)); }
+
+int lp_batch_end(lp_stream_t stream) { return lp::batch_end(static_cast<cudaStream_t>(stream)); }
+
 int lp_host_device_pointer(const void* host, void** dev) {
   if (!host || !dev) return LP_ERR_ARG;
   void* d = nullptr;
@@ -186,15 +197,15 @@ static int gemv_f32_group(int fmt, const void* w, int64_t w_len, const float* sc
   GemvParams p = base(w, scales, x, nullptr, y, m, k, gs, gpr, rb);
   if (fast_fp32(gs)) {
     switch (fmt) {
-      case 0: return lp::launch_gemv<lp::FmtI8F>(p, S(st));
-      case 1: return lp::launch_gemv<lp::FmtI4F>(p, S(st));
-      default: return lp::launch_gemv<lp::FmtF4F>(p, S(st));
+      case 0: return lp::launch_gemv<lp::FmtI8F>(p, SG(st));
+      case 1: return lp::launch_gemv<lp::FmtI4F>(p, SG(st));
+      default: return lp::launch_gemv<lp::FmtF4F>(p, SG(st));
     }
   }
   switch (fmt) {
-    case 0: return lp::launch_gemv<lp::FmtI8>(p, S(st));
-    case 1: return lp::launch_gemv<lp::FmtI4>(p, S(st));
-    default: return lp::launch_gemv<lp::FmtF4>(p, S(st));
+    case 0: return lp::launch_gemv<lp::FmtI8>(p, SG(st));
+    case 1: return lp::launch_gemv<lp::FmtI4>(p, SG(st));
+    default: return lp::launch_gemv<lp::FmtF4>(p, SG(st));
   }
 }
 
@@ -224,8 +235,8 @@ static int gemv_f32_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, co
   const int64_t rb = bpr * (q4 ? 18 : 34);
   GemvParams p = base(w, nullptr, x, nullptr, y, m, bpr * 32, 32, bpr, rb);
   if (fast_fp32(32))
-    return q4 ? lp::launch_gemv<lp::FmtQ4_0F>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0F>(p, S(st));
-  return q4 ? lp::launch_gemv<lp::FmtQ4_0>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0>(p, S(st));
+    return q4 ? lp::launch_gemv<lp::FmtQ4_0F>(p, SG(st)) : lp::launch_gemv<lp::FmtQ8_0F>(p, SG(st));
+  return q4 ? lp::launch_gemv<lp::FmtQ4_0>(p, SG(st)) : lp::launch_gemv<lp::FmtQ8_0>(p, SG(st));
 }
 
 int lp_dequant_gemv_q8_0(const void* w, int64_t w_len, int64_t bpr, const float* x, int64_t x_len,
@@ -249,7 +260,7 @@ static int gemv_kquant(int q6, const void* w, int64_t w_len, int64_t sbpr, const
   LP_VALIDATED();
   const int64_t rb = sbpr * (q6 ? 210 : 144);
   GemvParams p = base(w, nullptr, x, nullptr, y, m, sbpr * 256, 32, sbpr * 8, rb);
-  return q6 ? lp::launch_gemv<lp::FmtQ6_KF>(p, S(st)) : lp::launch_gemv<lp::FmtQ4_KF>(p, S(st));
+  return q6 ? lp::launch_gemv<lp::FmtQ6_KF>(p, SG(st)) : lp::launch_gemv<lp::FmtQ4_KF>(p, SG(st));
 }
 
 int lp_dequant_gemv_q4_k(const void* w, int64_t w_len, int64_t sbpr, const float* x,
@@ -277,7 +288,7 @@ static int gemv_q8_group(int i4, const void* w, int64_t w_len, const float* ws, 
     return LP_ERR_ARG;
   LP_VALIDATED();
   GemvParams p = base(w, ws, xq, xs, y, m, k, gs, gpr, rb);
-  return i4 ? lp::launch_gemv<lp::FmtI4Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8>(p, S(st));
+  return i4 ? lp::launch_gemv<lp::FmtI4Q8>(p, SG(st)) : lp::launch_gemv<lp::FmtQ8>(p, SG(st));
 }
 
 // quantizeQ8_0 (ggml.nim:60-75) of fp32 x, then the Q8-activation GEMV, as
@@ -293,8 +304,8 @@ static int gemv_q8_from_f32(int i4, const void* w, int64_t w_len, const float* w
   if (bad(w, w_len) || bad(ws, ws_len) || bad(x, x_len) || bad(y, y_len)) return LP_ERR_ARG;
   LP_VALIDATED();
   GemvParams p = base(w, ws, x, nullptr, y, m, k, 32, gpr, rb);
-  return i4 ? lp::launch_gemv<lp::FmtI4Q8FromF32>(p, S(st))
-            : lp::launch_gemv<lp::FmtQ8FromF32>(p, S(st));
+  return i4 ? lp::launch_gemv<lp::FmtI4Q8FromF32>(p, SG(st))
+            : lp::launch_gemv<lp::FmtQ8FromF32>(p, SG(st));
 }
 
 int lp_quantize_dequant_gemv_q8(const int8_t* wq, int64_t wq_len, const float* w_scales,
@@ -336,7 +347,7 @@ static int gemv_q8_blocks(int q4, const void* w, int64_t w_len, int64_t bpr, con
   LP_VALIDATED();
   const int64_t rb = bpr * (q4 ? 18 : 34);
   GemvParams p = base(w, nullptr, xq, nullptr, y, m, bpr * 32, 32, bpr, rb);
-  return q4 ? lp::launch_gemv<lp::FmtQ4_0Q8>(p, S(st)) : lp::launch_gemv<lp::FmtQ8_0Q8>(p, S(st));
+  return q4 ? lp::launch_gemv<lp::FmtQ4_0Q8>(p, SG(st)) : lp::launch_gemv<lp::FmtQ8_0Q8>(p, SG(st));
 }
 
 int lp_dequant_gemv_q8_0q8(const void* w, int64_t w_len, int64_t bpr, const void* xq,
@@ -371,8 +382,8 @@ static int gemm_common(int i4, const void* w, int64_t w_len, const float* ws, in
   if (gs == 32 && n <= kGemmColsMax && m >= 1) {
     GemvParams p = base(w, ws, xq, xs, y, m, k, gs, gpr, rb);
     p.ncol = static_cast<int>(n);
-    const int r = i4 ? lp::launch_gemv<lp::FmtI4Q8Cols>(p, S(st))
-                     : lp::launch_gemv<lp::FmtQ8Cols>(p, S(st));
+    const int r = i4 ? lp::launch_gemv<lp::FmtI4Q8Cols>(p, SG(st))
+                     : lp::launch_gemv<lp::FmtQ8Cols>(p, SG(st));
     if (r != LP_ERR_UNSUPPORTED) return r;
   }
   {

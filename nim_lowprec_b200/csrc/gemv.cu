@@ -1,6 +1,8 @@
 // gemv.cu -- launch planning for the fused dequant-GEMV kernels.
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
+#include <vector>
 
 #include "gemv_formats.cuh"
 #include "lp_internal.h"
@@ -70,12 +72,245 @@ struct SmemLimits {
 
 }  // namespace
 
+// ------------------------------------------------------ batched launches
+// GEMV calls made between lp_batch_begin and lp_batch_end on the batch's
+// stream are recorded here (this thread only) and launched as one
+// gemv_batch_kernel per run of same-format calls, after one
+// gemv_images_kernel that stages every job's activations.
+namespace {
+
+template <class Fmt> struct Batchable : std::false_type {};
+template <> struct Batchable<FmtQ8> : std::true_type {};
+template <> struct Batchable<FmtI4Q8> : std::true_type {};
+template <> struct Batchable<FmtQ8FromF32> : std::true_type {};
+template <> struct Batchable<FmtI4Q8FromF32> : std::true_type {};
+template <> struct Batchable<FmtQ8_0Q8> : std::true_type {};
+template <> struct Batchable<FmtQ4_0Q8> : std::true_type {};
+
+constexpr int kNotRecorded = -1000;
+// Weights + scales of one tile, at most.  Fewer, larger copies stream
+// faster per SM: on the config-4 sweep (one GPU), 80 KB tiles x 2 stages ran
+// 25.7 us per layer, 60 KB x 2 30.4 us, 40 KB x 4 32.8 us.  76 KB leaves room
+// for three activation buffers next to two stages (see launch_batch).
+constexpr int kBatchTile = 76 * 1024;
+constexpr int kBatchTerms = 48 * 1024;    // term slots, at most
+constexpr int kBatchFlight = 160 * 1024;  // weight stages, at most
+
+struct Range {
+  uintptr_t lo, hi;
+  bool meets(const Range& o) const { return lo < o.hi && o.lo < hi; }
+};
+
+struct BatchState {
+  bool open = false;
+  cudaStream_t st = nullptr;
+  const void* fmt = nullptr;  // launcher of the recorded format
+  int (*launch)(std::vector<GemvParams>&, cudaStream_t) = nullptr;
+  int (*single)(GemvParams, cudaStream_t) = nullptr;
+  std::vector<GemvParams> jobs;
+  std::vector<Range> outs;    // the recorded jobs' y
+  int kept = LP_OK;           // first failed flush made on another call's behalf
+};
+thread_local BatchState g_batch;
+
+// Plan the batch's common layout and launch the images and batch kernels;
+// LP_ERR_UNSUPPORTED when the jobs do not share one layout in shared memory.
+template <class Fmt>
+int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
+  const DeviceInfo& di = device_info();
+  auto kern = gemv_batch_kernel<Fmt, kNcw>;
+  static int one[kMaxDevices];
+  static std::once_flag once[kMaxDevices];
+  const int slot = di.ordinal % kMaxDevices;
+  std::call_once(once[slot], [&] {
+    cudaFuncAttributes fa;
+    int st_bytes = 0;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) st_bytes = static_cast<int>(fa.sharedSizeBytes);
+    one[slot] = di.max_smem_optin - st_bytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, one[slot]) !=
+        cudaSuccess)
+      one[slot] = 0;
+  });
+  static thread_local GemvBatch b;
+  b.n = static_cast<int>(jobs.size());
+  int sw = 0, ss = 0, tslot = 0, xs = 0, fbmax = 1, mmax = 0;
+  for (int j = 0; j < b.n; ++j) {
+    GemvParams& p = jobs[j];
+    const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
+    // Rows per tile: what fits kBatchTile (at most 32, one folder lane each),
+    // in whole row pairs.
+    int rt = std::min(32, std::max(1, kBatchTile / std::max(row_total, 1)));
+    rt = rt >= 2 ? rt & ~1 : 1;
+    p.rt = rt;
+    p.tstride = round_up(p.gpr, 32) + 4;
+    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / rt));
+    p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(p.ws);
+    p.bulk = (p.row_bytes % 16 == 0) && (wa % 16 == 0) &&
+             (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
+    sw = std::max(sw, round_up(rt * p.row_bytes, 128));
+    ss = std::max(ss, Fmt::kScales ? round_up(rt * p.gpr * 4, 128) : 0);
+    tslot = std::max(tslot, round_up(rt * p.tstride, 32));
+    xs = std::max(xs, round_up(p.x_bytes, 128));
+    fbmax = std::max(fbmax, p.fb);
+    mmax = std::max(mmax, p.m);
+  }
+  // term ring: two passes of the longest fold batch, within kBatchTerms
+  int ring = 2;
+  while (ring < 2 * fbmax && 2 * ring * tslot * 4 <= kBatchTerms) ring *= 2;
+  for (auto& p : jobs) p.fb = std::min(p.fb, ring / 2);
+  const int per_stage = sw + ss;
+  int xbufs = 3, stages = 0;
+  for (; xbufs >= 2; --xbufs) {
+    const int fixed = 128 + xbufs * xs + ring * tslot * 4 + 8 * (2 * kMaxStages + 2 * ring + 2 * xbufs);
+    stages = std::min(kMaxStages, (one[slot] - fixed) / per_stage);
+    stages = std::min(stages, std::max(2, kBatchFlight / per_stage));
+    if (stages >= 2) break;
+  }
+  if (stages < 2 || one[slot] <= 0) return LP_ERR_UNSUPPORTED;
+  b.stages = stages;
+  b.ring = ring;
+  b.xbufs = xbufs;
+  b.stage_w_bytes = sw;
+  b.stage_s_bytes = ss;
+  b.tslot = tslot;
+  b.x_stride = xs;
+  b.off_w = xbufs * xs;
+  b.off_s = b.off_w + stages * sw;
+  b.off_t = b.off_s + stages * ss;
+  b.off_b = b.off_t + ring * tslot * 4;
+  const int smem = 128 + b.off_b + 8 * (2 * stages + 2 * ring + 2 * xbufs);
+  for (int j = 0; j < b.n; ++j) b.job[j] = jobs[j];
+  // The images live for this launch only: a stream-ordered allocation, freed
+  // in stream order after the batch kernel (graph memory nodes when the
+  // stream is being captured), so batches on other streams or in other
+  // graphs never share them.
+  void* img = nullptr;
+  int r = cuda_status(cudaMallocAsync(&img, static_cast<size_t>(b.n) * xs, st));
+  if (r != LP_OK) return r;
+  b.img = static_cast<uint8_t*>(img);
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(b.n);
+  cfg.blockDim = dim3(512);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  r = cuda_status(cudaLaunchKernelEx(&cfg, gemv_images_kernel<Fmt>, b));
+  if (r == LP_OK) {
+    cfg.gridDim = dim3(std::min(mmax, di.sm_count));
+    cfg.blockDim = dim3(32 * (kNcw + 2));
+    cfg.dynamicSmemBytes = smem;
+    r = cuda_status(cudaLaunchKernelEx(&cfg, kern, b));
+  }
+  const int rf = cuda_status(cudaFreeAsync(img, st));
+  return r != LP_OK ? r : rf;
+}
+
+// Record a GEMV into the open batch (flushing first when it cannot join the
+// recorded jobs); kNotRecorded for a call on another stream.
+template <class Fmt>
+int batch_record(GemvParams p, cudaStream_t st) {
+  BatchState& bs = g_batch;
+  if (st != bs.st) return kNotRecorded;
+  const void* fmt = reinterpret_cast<const void*>(&launch_batch<Fmt>);
+  // The images kernel reads every job's activations before any job writes:
+  // a call reading an earlier call's output, writing where one writes, or
+  // pushing into another pool's exchange starts a new launch.
+  const int xb = std::max(p.k * 4, 1);
+  const Range xr{reinterpret_cast<uintptr_t>(p.x), reinterpret_cast<uintptr_t>(p.x) + xb};
+  const Range sr{reinterpret_cast<uintptr_t>(p.xs),
+                 reinterpret_cast<uintptr_t>(p.xs) + (p.xs ? p.gpr * 4 : 0)};
+  const Range yr{reinterpret_cast<uintptr_t>(p.y),
+                 reinterpret_cast<uintptr_t>(p.y) + static_cast<uintptr_t>(p.m) * 4};
+  bool join = bs.fmt == fmt && static_cast<int>(bs.jobs.size()) < kMaxBatch;
+  for (size_t i = 0; join && i < bs.outs.size(); ++i)
+    join = !bs.outs[i].meets(xr) && !bs.outs[i].meets(sr) && !bs.outs[i].meets(yr);
+  if (join && g_push && !bs.jobs.empty() && bs.jobs[0].push && bs.jobs[0].push != g_push) join = false;
+  if (!join && !bs.jobs.empty()) {
+    const int r = batch_flush();
+    if (r != LP_OK) return r;
+  }
+  if (g_push) {
+    p.push = g_push;
+    p.push_off = g_push_off;
+    g_pushed = true;
+  }
+  bs.fmt = fmt;
+  bs.launch = &launch_batch<Fmt>;
+  bs.single = &launch_gemv<Fmt>;
+  bs.jobs.push_back(p);
+  bs.outs.push_back(yr);
+  return LP_OK;
+}
+
+}  // namespace
+
+bool batch_open() { return g_batch.open; }
+
+int batch_flush() {
+  BatchState& bs = g_batch;
+  if (bs.jobs.empty()) return LP_OK;
+  std::vector<GemvParams> jobs;
+  jobs.swap(bs.jobs);
+  bs.outs.clear();
+  auto launch = bs.launch;
+  auto single = bs.single;
+  bs.fmt = nullptr;
+  int r = launch(jobs, bs.st);
+  if (r == LP_ERR_UNSUPPORTED) {
+    // no common layout: one launch per job, planned as a lone call (the
+    // recorded jobs keep their push context)
+    bs.open = false;
+    r = LP_OK;
+    for (size_t i = 0; i < jobs.size() && r == LP_OK; ++i) r = single(jobs[i], bs.st);
+    bs.open = true;
+  }
+  return r;
+}
+
+void batch_flush_keep() {
+  const int r = batch_flush();
+  if (r != LP_OK && g_batch.kept == LP_OK) g_batch.kept = r;
+}
+
+int batch_begin(cudaStream_t st) {
+  const int r = batch_end(nullptr);
+  g_batch.open = true;
+  g_batch.st = st;
+  return r;
+}
+
+int batch_end(cudaStream_t st) {
+  (void)st;
+  int r = batch_flush();
+  if (r == LP_OK) r = g_batch.kept;
+  g_batch.kept = LP_OK;
+  g_batch.open = false;
+  g_batch.st = nullptr;
+  return r;
+}
+
 thread_local const PushCtx* g_push = nullptr;
 thread_local int64_t g_push_off = 0;
 thread_local bool g_pushed = false;
 
 template <class Fmt>
 int launch_gemv(GemvParams p, cudaStream_t st) {
+  if (batch_open()) {
+    if constexpr (Batchable<Fmt>::value)
+      if (p.m > 0 && p.gpr > 0) {
+        const int r = batch_record<Fmt>(p, st);
+        if (r != kNotRecorded) return r;
+      }
+    const int r = batch_flush();
+    if (r != LP_OK) return r;
+  }
   if (p.m == 0) {
     g_pushed = g_push != nullptr;  // an empty slice has nothing to send
     return LP_OK;

@@ -509,4 +509,318 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
   }
 }
 
+
+// ------------------------------------------------------ batched launches
+// Several GEMVs of one format in one persistent launch (lp_batch_begin ..
+// lp_batch_end).  A lone GEMV pays, per launch, the CTA start, the
+// activation staging after its grid-dependency wait, the first copy's
+// latency and the last tile's fold -- about 5.7 us at K = 4096 and 8.1 us at
+// K = 11008 with one row per SM, more than a 4800 x 4096 int4 slice takes
+// to stream.  Here the producer streams job after job without a break, the
+// folder trails the consumers across job boundaries, and each job's staged
+// activations come from an image a small kernel builds once for the whole
+// batch (byte for byte what the job's consumers would have staged), copied
+// by one bulk copy into one of `xbufs` buffers while earlier jobs compute.
+//
+// Common layout: every job uses the same weight stages, term slots and
+// activation buffers, so the barriers' phases run on over the whole batch
+// (tile counter tg across jobs).  Per job: rows per tile rt, term stride
+// tstride, fold batch fb (<= ring / 2) and its image's byte count x_bytes.
+// Ordered folds only (the bit-exact paths).
+constexpr int kMaxBatch = 64;
+
+struct GemvBatch {
+  int n;                     // jobs
+  int stages, ring, xbufs;   // weight stages, term slots, activation buffers
+  int stage_w_bytes, stage_s_bytes;
+  int tslot;                 // floats per term slot
+  int x_stride;              // bytes per activation buffer and per image (128-multiple)
+  int off_w, off_s, off_t, off_b;  // activation buffers from 0, x_stride apart
+  uint8_t* img;              // n images, x_stride apart
+  GemvParams job[kMaxBatch];
+};
+
+// This CTA's rows of a job: [rb, re) in tiles of p.rt (nt = 0: none).
+__device__ __forceinline__ int batch_rows(const GemvParams& p, int& rb, int& nt) {
+  rb = static_cast<int>((static_cast<int64_t>(p.m) * blockIdx.x) / gridDim.x);
+  const int re = static_cast<int>((static_cast<int64_t>(p.m) * (blockIdx.x + 1)) / gridDim.x);
+  nt = (re - rb + p.rt - 1) / p.rt;
+  return re;
+}
+
+// One block per job: the job's staged activations, written to its image.
+template <class Fmt>
+__global__ void __launch_bounds__(512) gemv_images_kernel(const __grid_constant__ GemvBatch b) {
+  // the batch kernel may start streaming weights now; it reads the images
+  // only after this grid has completed (its own grid-dependency wait)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int j = blockIdx.x;
+  if (j < b.n)
+    Fmt::stage_x(b.img + static_cast<int64_t>(j) * b.x_stride, b.job[j], threadIdx.x, blockDim.x);
+}
+
+template <class Fmt, int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 2), 1)
+    gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
+  static_assert(Fmt::kFold != Fold::Tree && !ColsOf<Fmt>::value, "ordered row folds only");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ volatile int s_abort;
+  uint8_t* smem = smem_raw + ((128u - (saddr(smem_raw) & 127u)) & 127u);
+  uint8_t* stw = smem + b.off_w;
+  uint8_t* sts = smem + b.off_s;
+  float* terms = reinterpret_cast<float*>(smem + b.off_t);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + b.off_b);
+  uint64_t* empty = full + b.stages;
+  uint64_t* tfull = empty + b.stages;
+  uint64_t* tempty = tfull + b.ring;
+  uint64_t* xfull = tempty + b.ring;  // image landed in buffer i
+  uint64_t* xempty = xfull + b.xbufs; // every consumer warp done with buffer i
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < b.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    for (int r = 0; r < b.ring; ++r) {
+      mbar_init(&tfull[r], NCW);
+      mbar_init(&tempty[r], 1);
+    }
+    for (int i = 0; i < b.xbufs; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], NCW);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------ producer
+    // Weights are never written by kernels this launch may overlap (see
+    // gemv_kernel), so the stream starts before the grid-dependency wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint64_t pol = l2_evict_first();
+    int tg = 0;
+    bool stop = false;
+    for (int j = 0; j < b.n && !stop; ++j) {
+      const GemvParams& p = b.job[j];
+      int rb, nt;
+      const int re = batch_rows(p, rb, nt);
+      for (int t = 0; t < nt; ++t, ++tg) {
+        const int s = tg % b.stages;
+        if (tg >= b.stages && !mbar_wait_idle(&empty[s], ((tg / b.stages) - 1) & 1, &s_abort)) {
+          stop = true;
+          break;
+        }
+        if (s_abort) {
+          stop = true;
+          break;
+        }
+        const int r0 = rb + t * p.rt;
+        const int rows = min(p.rt, re - r0);
+        const uint32_t bw = static_cast<uint32_t>(rows) * p.row_bytes;
+        const uint32_t bs = Fmt::kScales ? static_cast<uint32_t>(rows) * p.gpr * 4u : 0u;
+        const uint8_t* gw = p.w + static_cast<int64_t>(r0) * p.row_bytes;
+        const float* gsc = Fmt::kScales ? p.ws + static_cast<int64_t>(r0) * p.gpr : nullptr;
+        uint8_t* dw = stw + s * b.stage_w_bytes;
+        uint8_t* ds = sts + s * b.stage_s_bytes;
+        if (p.bulk) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[s], bw + bs);
+            bulk_g2s(dw, gw, bw, &full[s], pol);
+            if (Fmt::kScales) bulk_g2s(ds, gsc, bs, &full[s], pol);
+          }
+        } else {
+          for (uint32_t i = lane; i < bw; i += 32) dw[i] = gw[i];
+          if constexpr (Fmt::kScales)
+            for (uint32_t i = lane; i < bs / 4; i += 32) reinterpret_cast<float*>(ds)[i] = gsc[i];
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[s]);
+        }
+      }
+    }
+    // never leave the CTA with a bulk copy still landing in shared memory
+    if (lane == 0)
+      for (int u = max(0, tg - b.stages); u < tg; ++u)
+        mbar_wait(&full[u % b.stages], (u / b.stages) & 1);
+  } else if (warp == 1) {
+    // --------------------------------------------------------- folder
+    // Lane l folds row l % rt of tile l / rt of each pass of fb tiles.  The
+    // jobs of a pooled batch share one exchange and one gather number.
+    PushTag pt;
+    for (int j = 0; j < b.n; ++j)
+      if (b.job[j].push) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        pt = push_tag(b.job[j]);
+        break;
+      }
+    int tg = 0;
+    bool stop = false;
+    for (int j = 0; j < b.n && !stop; ++j) {
+      const GemvParams& p = b.job[j];
+      int rb, nt;
+      const int re = batch_rows(p, rb, nt);
+      const int ti = lane / p.rt, r = lane - ti * p.rt;
+      for (int t0 = 0; t0 < nt; t0 += p.fb) {
+        const int nb = min(p.fb, nt - t0);
+        bool ok = true;
+        for (int i = 0; i < nb && ok; ++i)
+          ok = mbar_wait_idle(&tfull[(tg + t0 + i) % b.ring], ((tg + t0 + i) / b.ring) & 1,
+                              &s_abort);
+        if (!ok || s_abort) {
+          stop = true;
+          break;
+        }
+        if (ti < nb) {
+          const int t = t0 + ti;
+          const int r0 = rb + t * p.rt;
+          if (r < min(p.rt, re - r0)) {
+            const int64_t idx = static_cast<int64_t>(r0) + r;
+            const float val = fold_row<Fmt::kFold>(
+                terms + ((tg + t) % b.ring) * b.tslot + r * p.tstride, p.gpr);
+            p.y[idx] = val;
+            if (p.push) push_out(p, pt, idx, val);
+          }
+        }
+        __syncwarp();
+        if (lane == 0)
+          for (int i = 0; i < nb; ++i) mbar_arrive(&tempty[(tg + t0 + i) % b.ring]);
+      }
+      tg += nt;
+    }
+  } else {
+    // ------------------------------------------------------ consumers
+    const int ct = threadIdx.x - 64;
+    constexpr int NC = NCW * 32;
+    // The images (and the activations they came from) belong to the kernels
+    // before this one in the stream.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint64_t ipol = l2_evict_last();
+    int issued = 0;  // images requested (thread ct == 0 only)
+    auto request = [&](int i) {
+      const int buf = i % b.xbufs;
+      const uint32_t bytes = static_cast<uint32_t>(b.job[i].x_bytes);
+      mbar_arrive_expect_tx(&xfull[buf], bytes);
+      bulk_g2s(smem + buf * b.x_stride, b.img + static_cast<int64_t>(i) * b.x_stride, bytes,
+               &xfull[buf], ipol);
+      ++issued;
+    };
+    if (ct == 0)
+      for (int i = 0; i < min(b.n, b.xbufs - 1); ++i) request(i);
+    int tg = 0;
+    int waited = 0;  // images this thread has seen land
+    for (int j = 0; j < b.n; ++j) {
+      const GemvParams& p = b.job[j];
+      int rb, nt;
+      const int re = batch_rows(p, rb, nt);
+      // The next image goes into the buffer of job j - 1 once every consumer
+      // warp is done with it.
+      if (ct == 0 && j + b.xbufs - 1 < b.n) {
+        bool ok = true;
+        if (j >= 1) ok = mbar_wait(&xempty[(j - 1) % b.xbufs], ((j - 1) / b.xbufs) & 1, &s_abort);
+        if (ok && !s_abort) request(j + b.xbufs - 1);
+      }
+      __syncwarp();
+      const int buf = j % b.xbufs;
+      if (!mbar_wait(&xfull[buf], (j / b.xbufs) & 1, &s_abort) || s_abort) break;
+      if (ct == 0) ++waited;
+      const uint8_t* xsm = smem + buf * b.x_stride;
+      Fmt f;
+      const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
+      const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
+      const bool fixed = dpr >= 1;
+      const bool idle = fixed && ct >= dpr * p.gpr;
+      if (fixed && !idle) f.prepare(p, xsm, g0);
+      bool stop = false;
+      for (int t = 0; t < nt; ++t, ++tg) {
+        const int s = tg % b.stages;
+        const int tb = tg % b.ring;
+        bool ok = mbar_wait(&full[s], (tg / b.stages) & 1, &s_abort);
+        if (ok && tg >= b.ring) ok = mbar_wait(&tempty[tb], ((tg / b.ring) - 1) & 1, &s_abort);
+        if (!ok || s_abort) {
+          stop = true;
+          break;
+        }
+        const int r0 = rb + t * p.rt;
+        const int rows = min(p.rt, re - r0);
+        const uint8_t* W = stw + s * b.stage_w_bytes;
+        const float* S = reinterpret_cast<const float*>(sts + s * b.stage_s_bytes);
+        float* T = terms + tb * b.tslot;
+        const int npairs = (rows + 1) >> 1;
+        if (fixed) {
+          const int g = g0;
+          int pr = idle ? npairs : pr0;
+          for (; Fmt::kTwoPairs && pr + dpr < npairs; pr += 2 * dpr) {
+            const int ra = 2 * pr, rc = 2 * (pr + dpr);
+            const int rb2 = min(ra + 1, rows - 1), rd = min(rc + 1, rows - 1);
+            float t0, t1, t2, t3;
+            f.term2(p, xsm, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                    S + rb2 * p.gpr, g, t0, t1);
+            f.term2(p, xsm, W + rc * p.row_bytes, W + rd * p.row_bytes, S + rc * p.gpr,
+                    S + rd * p.gpr, g, t2, t3);
+            if constexpr (Fmt::kFix) {
+              f.fix2(p, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                     S + rb2 * p.gpr, g, t0, t1);
+              f.fix2(p, W + rc * p.row_bytes, W + rd * p.row_bytes, S + rc * p.gpr,
+                     S + rd * p.gpr, g, t2, t3);
+            }
+            T[ra * p.tstride + g] = t0;
+            if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+            T[rc * p.tstride + g] = t2;
+            if (rc + 1 < rows) T[(rc + 1) * p.tstride + g] = t3;
+          }
+          for (; pr < npairs; pr += dpr) {
+            const int ra = 2 * pr;
+            const int rb2 = min(ra + 1, rows - 1);
+            float t0, t1;
+            f.term2(p, xsm, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                    S + rb2 * p.gpr, g, t0, t1);
+            if constexpr (Fmt::kFix)
+              f.fix2(p, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                     S + rb2 * p.gpr, g, t0, t1);
+            T[ra * p.tstride + g] = t0;
+            if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+          }
+        } else {
+          int g = g0;
+          for (int pr = pr0; pr < npairs;) {
+            const int ra = 2 * pr;
+            const int rb2 = min(ra + 1, rows - 1);
+            float t0, t1;
+            f.prepare(p, xsm, g);
+            f.term2(p, xsm, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                    S + rb2 * p.gpr, g, t0, t1);
+            if constexpr (Fmt::kFix)
+              f.fix2(p, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
+                     S + rb2 * p.gpr, g, t0, t1);
+            T[ra * p.tstride + g] = t0;
+            if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
+            g += dg;
+            pr += dpr;
+            if (g >= p.gpr) {
+              g -= p.gpr;
+              ++pr;
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty[s]);
+          mbar_arrive(&tfull[tb]);
+        }
+      }
+      if (stop) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xempty[buf]);
+    }
+    // never leave with an image still landing in shared memory
+    if (ct == 0)
+      for (int i = waited; i < issued; ++i) mbar_wait(&xfull[i % b.xbufs], (i / b.xbufs) & 1);
+  }
+}
+
 }  // namespace lp

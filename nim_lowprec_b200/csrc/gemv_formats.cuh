@@ -1261,15 +1261,20 @@ struct FmtQ8Cols : StageXCols {
                                             const uint8_t* wA, const uint8_t* wB, const float* sA,
                                             const float* sB, int g, float* TA, float* TB,
                                             int tstride) {
+    // Consecutive lanes take consecutive groups, 32 bytes apart: lanes g
+    // and g + 4 would meet in the same banks, so lanes with bit 2 of g set
+    // read the second 16 bytes first (weights and activations alike; the
+    // integer dot does not depend on the order of its words).
+    const int sw = (g >> 2) & 1;
     const uint4* pa = reinterpret_cast<const uint4*>(wA + g * 32);
     const uint4* pb = reinterpret_cast<const uint4*>(wB + g * 32);
-    const uint4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
+    const uint4 a0 = pa[sw], a1 = pa[sw ^ 1], b0 = pb[sw], b1 = pb[sw ^ 1];
     const float ga = sA[g], gb = sB[g];
     const float* xs = xscales(p, xsm);
 #pragma unroll 2
     for (int c = 0; c < p.ncol; ++c) {
       const uint4* px = reinterpret_cast<const uint4*>(xsm + c * p.k + g * 32);
-      const uint4 x0 = px[0], x1 = px[1];
+      const uint4 x0 = px[sw], x1 = px[sw ^ 1];
       int ia = 0, ib = 0;
       ia = dp4a_ss(a0.x, x0.x, ia); ib = dp4a_ss(b0.x, x0.x, ib);
       ia = dp4a_ss(a0.y, x0.y, ia); ib = dp4a_ss(b0.y, x0.y, ib);
@@ -1340,20 +1345,31 @@ struct FmtI4Q8Cols : StageXCols {
     const float ga = sA[g], gb = sB[g];
     const float* xs = xscales(p, xsm);
     const int* s8 = sums8(p, xsm);
+    // As in FmtQ8Cols: lanes with bit 2 of g set read the odd half (16
+    // bytes) of their 32 first, paired with the odd-column weights.
+    const int sw = (g >> 2) & 1;
+    uint32_t a1[4], a2[4], b1[4], b2[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a1[j] = sw ? ahi[j] : alo[j];
+      a2[j] = sw ? alo[j] : ahi[j];
+      b1[j] = sw ? bhi[j] : blo[j];
+      b2[j] = sw ? blo[j] : bhi[j];
+    }
 #pragma unroll 2
     for (int c = 0; c < p.ncol; ++c) {
       const int u = c * p.gpr + g;
       const uint4* px = reinterpret_cast<const uint4*>(xsm + u * 32);
-      const uint4 e = px[0], o = px[1];
+      const uint4 h1 = px[sw], h2 = px[sw ^ 1];  // paired with a1/b1, a2/b2
       int ia = -s8[u], ib = ia;
-      ia = dp4a_us(alo[0], e.x, ia); ib = dp4a_us(blo[0], e.x, ib);
-      ia = dp4a_us(ahi[0], o.x, ia); ib = dp4a_us(bhi[0], o.x, ib);
-      ia = dp4a_us(alo[1], e.y, ia); ib = dp4a_us(blo[1], e.y, ib);
-      ia = dp4a_us(ahi[1], o.y, ia); ib = dp4a_us(bhi[1], o.y, ib);
-      ia = dp4a_us(alo[2], e.z, ia); ib = dp4a_us(blo[2], e.z, ib);
-      ia = dp4a_us(ahi[2], o.z, ia); ib = dp4a_us(bhi[2], o.z, ib);
-      ia = dp4a_us(alo[3], e.w, ia); ib = dp4a_us(blo[3], e.w, ib);
-      ia = dp4a_us(ahi[3], o.w, ia); ib = dp4a_us(bhi[3], o.w, ib);
+      ia = dp4a_us(a1[0], h1.x, ia); ib = dp4a_us(b1[0], h1.x, ib);
+      ia = dp4a_us(a2[0], h2.x, ia); ib = dp4a_us(b2[0], h2.x, ib);
+      ia = dp4a_us(a1[1], h1.y, ia); ib = dp4a_us(b1[1], h1.y, ib);
+      ia = dp4a_us(a2[1], h2.y, ia); ib = dp4a_us(b2[1], h2.y, ib);
+      ia = dp4a_us(a1[2], h1.z, ia); ib = dp4a_us(b1[2], h1.z, ib);
+      ia = dp4a_us(a2[2], h2.z, ia); ib = dp4a_us(b2[2], h2.z, ib);
+      ia = dp4a_us(a1[3], h1.w, ia); ib = dp4a_us(b1[3], h1.w, ib);
+      ia = dp4a_us(a2[3], h2.w, ia); ib = dp4a_us(b2[3], h2.w, ib);
       const float xsc = xs[u];
       TA[c * tstride + g] = fmul(fmul(i2f_rn(ia), ga), xsc);
       if (TB) TB[c * tstride + g] = fmul(fmul(i2f_rn(ib), gb), xsc);

@@ -28,7 +28,7 @@ struct GemvParams;
 // every rank.  A pooled GEMV given a PushCtx stores its outputs straight into
 // every other rank's buffer from its fold (pool.cu then only receives).
 constexpr int kMaxPushRanks = 8;
-constexpr int64_t kXchgWords = int64_t{1} << 20;
+constexpr int64_t kXchgWords = int64_t{1} << 21;
 struct PushCtx {
   uint8_t* peers[kMaxPushRanks];  // every rank's exchange buffer as mapped here
   uint32_t* state;                // this rank's finished-gather count (state[0])
@@ -63,6 +63,15 @@ struct FmtI4Q8Cols;
 
 template <class Fmt>
 int launch_gemv(GemvParams p, cudaStream_t st);
+
+// Batched GEMV launches (gemv.cu): GEMVs this thread makes on the stream of
+// its open batch are recorded and launched together at the next flush.
+// Every other launch of the library flushes first, so stream order holds.
+bool batch_open();
+int batch_flush();
+void batch_flush_keep();  // a failure is returned by batch_end
+int batch_begin(cudaStream_t st);
+int batch_end(cudaStream_t st);
 
 // per-step inputs from page-locked host memory (transfer.cu)
 int launch_copy_in(void* dst, const void* src, int64_t bytes, cudaStream_t st);

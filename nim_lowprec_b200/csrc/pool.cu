@@ -42,7 +42,7 @@ struct PeerBufs {
 };
 // A gathered vector made of up to kMaxParts regions, each m rows of per_row
 // floats at element offset off, its rows sliced over the ranks.
-constexpr int kMaxParts = 4;
+constexpr int kMaxParts = 64;  // a 32-layer sweep's two GEMVs per layer
 struct GatherParts {
   int64_t off[kMaxParts], m[kMaxParts], prow[kMaxParts];
   int send[kMaxParts];  // 1: the receive kernel also stores this rank's rows of the part
@@ -112,7 +112,12 @@ int nccl_status(ncclResult_t r) {
   return LP_ERR_NCCL;
 }
 
-inline cudaStream_t S(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
+// The stream of a receive or NCCL gather: the GEMVs queued in this thread's
+// open batch (lp_batch_begin) launch first -- they push what is received.
+inline cudaStream_t S(lp_stream_t s) {
+  if (lp::batch_open()) lp::batch_flush_keep();
+  return static_cast<cudaStream_t>(s);
+}
 
 __host__ __device__ inline void rows_of(int64_t m, int nranks, int rank, int64_t* b, int64_t* e) {
   const int64_t per = m / nranks;

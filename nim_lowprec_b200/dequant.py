@@ -17,6 +17,8 @@ or uint8 arrays/tensors whose total size is a multiple of the block size.
 """
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 
 from . import _native as N
@@ -91,6 +93,29 @@ def _blocks(a, bb: int) -> int:
 
 def _stream():
     return torch.cuda.current_stream().cuda_stream
+
+
+@contextlib.contextmanager
+def batch():
+    """Run the int8-activation GEMVs made inside as persistent launches
+    (lp_batch_begin / lp_batch_end on the current stream; no counterpart in
+    the reference).  Calls of dequantGemvQ8/I4Q8, quantizeDequantGemvQ8/I4Q8,
+    dequantGemvQ8_0Q8/Q4_0Q8 and their pooled forms are queued and launched
+    together -- up to 64 consecutive same-format calls per launch -- with the
+    results of the calls made one by one, bit for bit.  Any other call of the
+    library launches the queue first.  Device tensors only, and every tensor
+    a queued call reads or writes must stay alive until the block ends (a
+    temporary freed earlier may be reused by the allocator before the launch)."""
+    st = _stream()
+    N.check(N.lib().lp_batch_begin(st), "batch_begin")
+    ok = False
+    try:
+        yield
+        ok = True
+    finally:
+        r = N.lib().lp_batch_end(st)
+        if ok:
+            N.check(r, "batch_end")
 
 
 def _call(mode, name, *args):

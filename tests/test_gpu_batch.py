@@ -1,0 +1,198 @@
+"""Batched GEMV launches (lp_batch_begin / lp_batch_end, ``L.batch()``).
+
+Every call queued in a batch must give the bits of the same call made on its
+own, and the oracle's: across jobs of different shapes in one launch (rows
+fewer than the SMs, one row, K = 4096 and 11008, group tails), for every
+format that batches, when a later call reads an earlier call's output (the
+queue launches first), when another library call comes in between, past the
+64-call limit, and replayed from a CUDA graph.
+"""
+import numpy as np
+import pytest
+
+from gpu_util import acts, bits_equal, mismatch_report, to_dev, to_host, weights
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+import nim_lowprec_b200 as L  # noqa: E402
+from nim_lowprec_b200 import _native as N  # noqa: E402
+
+# (rows, K): fewer rows than SMs, one row, the config-4 shapes, a row of
+# one group, and K = 96 (three groups)
+SHAPES = [(1, 32), (7, 4096), (148, 4096), (300, 11008), (4800, 4096), (512, 11008),
+          (4096, 4096), (149, 64), (2, 96), (1000, 2048)]
+
+
+def dev_y(m):
+    return torch.full((m,), float("nan"), dtype=torch.float32, device="cuda")
+
+
+def assert_bits(got, want):
+    assert bits_equal(got, want), mismatch_report(got, want)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert N.device_error() == 0
+
+
+def i4_case(seed, m, k):
+    w = weights(seed, m * k)
+    s4 = O.calibrateSymmetric(w, 32, 7.0)
+    return O.packInt4(O.quantize(w, s4, 32, "i4")), s4
+
+
+def q8_case(seed, m, k):
+    return O.quantizeQ8_0Split(weights(seed, m * k))
+
+
+def cases(make, shapes=SHAPES, seed=0):
+    out = []
+    for i, (m, k) in enumerate(shapes):
+        wt, st = make(seed + 200 + i, m, k)
+        x = acts(seed + 300 + i, k)
+        out.append((m, k, wt, st, x, *to_dev(wt, st, x)))
+    return out
+
+
+@pytest.mark.parametrize("fmt", ["i4q8", "q8"])
+def test_batch_fused_quantize_gemv_equals_lone_calls(fmt):
+    fused = L.quantizeDequantGemvI4Q8 if fmt == "i4q8" else L.quantizeDequantGemvQ8
+    ofn = O.dequantGemvI4Q8 if fmt == "i4q8" else O.dequantGemvQ8
+    cs = cases(i4_case if fmt == "i4q8" else q8_case)
+    lone = []
+    for m, k, _, _, _, wd, sd, xd in cs:
+        y = dev_y(m)
+        fused(wd, sd, 32, xd, y)
+        lone.append(to_host(y))
+    ys = [dev_y(c[0]) for c in cs]
+    with L.batch():
+        for c, y in zip(cs, ys):
+            fused(c[5], c[6], 32, c[7], y)
+    for (m, k, wt, st, x, *_), y, yl in zip(cs, ys, lone):
+        got = to_host(y)
+        assert_bits(got, yl)
+        xq, xs = O.quantizeQ8_0Split(x)
+        assert_bits(got, ofn(wt, st, 32, xq, xs))
+
+
+@pytest.mark.parametrize("fmt", ["i4q8", "q8"])
+def test_batch_prequantized_gemv_equals_lone_calls(fmt):
+    fn = L.dequantGemvI4Q8 if fmt == "i4q8" else L.dequantGemvQ8
+    ofn = O.dequantGemvI4Q8 if fmt == "i4q8" else O.dequantGemvQ8
+    cs = cases(i4_case if fmt == "i4q8" else q8_case, seed=50)
+    acts_q = []
+    for m, k, wt, st, x, *_ in cs:
+        xq, xs = O.quantizeQ8_0Split(x)
+        acts_q.append((xq, xs, *to_dev(xq, xs)))
+    ys = [dev_y(c[0]) for c in cs]
+    with L.batch():
+        for c, a, y in zip(cs, acts_q, ys):
+            fn(c[5], c[6], 32, a[2], a[3], y)
+    for (m, k, wt, st, x, wd, sd, _), a, y in zip(cs, acts_q, ys):
+        yl = dev_y(m)
+        fn(wd, sd, 32, a[2], a[3], yl)
+        assert_bits(to_host(y), to_host(yl))
+        assert_bits(to_host(y), ofn(wt, st, 32, a[0], a[1]))
+
+
+def test_batch_ggml_q8_0q8_and_q4_0q8_mixed_formats():
+    """Calls alternating between the two ggml formats (each switch launches
+    the queue) and runs of one format."""
+    shapes = [(1, 1), (9, 3), (300, 128), (4096, 128), (150, 5)]  # (rows, blocks per row)
+    jobs = []
+    for i, (m, bpr) in enumerate(shapes):
+        x = O.quantizeQ8_0(acts(400 + i, 32 * bpr))
+        for j, (fn, ofn, enc) in enumerate(((L.dequantGemvQ8_0Q8, O.dequantGemvQ8_0Q8,
+                                             O.quantizeQ8_0),
+                                            (L.dequantGemvQ4_0Q8, O.dequantGemvQ4_0Q8,
+                                             O.quantizeQ4_0))):
+            w = enc(weights(500 + 10 * i + j, m * 32 * bpr))
+            jobs.append((fn, ofn, w, x, bpr, m, *to_dev(w.reshape(-1), x.reshape(-1))))
+    order = jobs + sorted(jobs, key=lambda j: j[0].__name__)  # alternating, then runs
+    ys = [dev_y(j[5]) for j in order]
+    with L.batch():
+        for j, y in zip(order, ys):
+            j[0](j[6], j[4], j[7], y)
+    for j, y in zip(order, ys):
+        assert_bits(to_host(y), j[1](j[2], j[4], j[3]))
+
+
+def test_batch_chained_calls_read_earlier_outputs():
+    """y of one call is x of the next (a layer chain), and a quantize of an
+    earlier output comes in between: each read sees the finished output."""
+    dims = [4096, 11008, 4096, 4096]
+    ws = [i4_case(600 + i, dims[i + 1], dims[i]) for i in range(3)]
+    wd = [to_dev(w, s) for w, s in ws]
+    x0 = acts(601, dims[0])
+    (x0d,) = to_dev(x0)
+    ys = [dev_y(dims[i + 1]) for i in range(3)]
+    xq = torch.empty(dims[2], dtype=torch.int8, device="cuda")
+    xs = torch.empty(dims[2] // 32, dtype=torch.float32, device="cuda")
+    with L.batch():
+        L.quantizeDequantGemvI4Q8(*wd[0], 32, x0d, ys[0])
+        L.quantizeDequantGemvI4Q8(*wd[1], 32, ys[0], ys[1])
+        L.quantizeQ8_0Split(ys[1], xq, xs)
+        L.dequantGemvI4Q8(*wd[2], 32, xq, xs, ys[2])
+    x = x0
+    for i in range(3):
+        q, s = O.quantizeQ8_0Split(x)
+        want = O.dequantGemvI4Q8(ws[i][0], ws[i][1], 32, q, s)
+        assert_bits(to_host(ys[i]), want)
+        x = want
+
+
+def test_batch_past_64_calls_and_empty_calls():
+    m, k = 64, 256
+    w, s = i4_case(700, m, k)
+    wd, sd = to_dev(w, s)
+    xs = [acts(800 + i, k) for i in range(150)]
+    xds = [to_dev(x)[0] for x in xs]
+    ys = [dev_y(m) for _ in xs]
+    empty = torch.empty(0, dtype=torch.float32, device="cuda")
+    with L.batch():
+        for i, (xd, y) in enumerate(zip(xds, ys)):
+            L.quantizeDequantGemvI4Q8(wd, sd, 32, xd, y)
+            if i == 70:  # no rows: nothing to queue
+                L.quantizeDequantGemvI4Q8(wd[:0], sd[:0], 32, xd, empty)
+    for x, y in zip(xs, ys):
+        q, sc = O.quantizeQ8_0Split(x)
+        assert_bits(to_host(y), O.dequantGemvI4Q8(w, s, 32, q, sc))
+
+
+def test_batch_replayed_from_cuda_graph():
+    """The decode-loop form: a batch captured once (after an eager batch of
+    the same calls), replayed with new activations copied in."""
+    shapes = [(4800, 4096), (512, 11008), (4800, 4096), (512, 11008)]
+    cs = cases(i4_case, shapes, seed=900)
+    ys = [dev_y(c[0]) for c in cs]
+
+    def step():
+        with L.batch():
+            for c, y in zip(cs, ys):
+                L.quantizeDequantGemvI4Q8(c[5], c[6], 32, c[7], y)
+
+    step()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step()
+    new_x = [acts(950 + i, c[1]) for i, c in enumerate(cs)]
+    for c, x in zip(cs, new_x):
+        c[7].copy_(torch.from_numpy(x))
+    for y in ys:
+        y.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    for c, x, y in zip(cs, new_x, ys):
+        q, sc = O.quantizeQ8_0Split(x)
+        assert_bits(to_host(y), O.dequantGemvI4Q8(c[2], c[3], 32, q, sc))
+    del g

@@ -156,6 +156,39 @@ def _rank_main(rank, world, port, q):
                 same(f"group{rep_}-q8", yg[:M], refq8)
                 same(f"group{rep_}-q4_0", yg[M:2 * M], refq4)
                 same(f"group{rep_}-gemm", yg[2 * M:], refgm)
+            # pooled GEMVs queued in batches inside one gather group (the
+            # decode-sweep form): the batch kernels push every call's rows
+            # from their folds, a format change starts a second batch launch,
+            # and the group's receive runs once
+            jobs = []
+            for mj, kj in ((M, K), (300, 1024), (7, 64), (M, K), (1, 32)):
+                wj = rnd(mj * kj, 0.02)
+                sj = torch.empty(mj * kj // 32, device="cuda")
+                L.calibrateSymmetric(wj, 32, 7.0, sj)
+                pj = torch.empty(mj * kj // 2, dtype=torch.uint8, device="cuda")
+                L.quantizeI4Packed(wj, sj, 32, pj)
+                xqj = torch.empty(kj, dtype=torch.int8, device="cuda")
+                xsj = torch.empty(kj // 32, device="cuda")
+                L.quantizeQ8_0Split(rnd(kj), xqj, xsj)
+                rj = torch.empty(mj, device="cuda")
+                L.dequantGemvI4Q8(pj, sj, 32, xqj, xsj, rj)
+                jobs.append((mj, pj, sj, xqj, xsj, rj))
+            tot = sum(j[0] for j in jobs) + M
+            for rep_ in range(2):
+                yb = torch.full((tot,), float("nan"), device="cuda")
+                with L.batch():
+                    npl.group_begin(yb)
+                    off = 0
+                    for mj, pj, sj, xqj, xsj, _ in jobs:
+                        P.parDequantGemvI4Q8(npl, pj, sj, 32, xqj, xsj, yb[off:off + mj])
+                        off += mj
+                    P.parDequantGemvQ8(npl, wq, wd, 32, xq[:K], xd[:K // 32], yb[off:])
+                    npl.group_end()
+                off = 0
+                for i_, (mj, *_r, rj) in enumerate(jobs):
+                    same(f"batch-group{rep_}-{i_}", yb[off:off + mj], rj)
+                    off += mj
+                same(f"batch-group{rep_}-q8", yb[off:], refq8)
         # the library pool gathers over NVLink by default (one GPU per rank);
         # both transports, back-to-back gathers (alternating exchange halves)
         # and CUDA-graph replays give the single-GPU bits
