@@ -877,6 +877,14 @@ def main():
         "clocks": clocks,
     }
     line["config4_per_call"] = per_call
+    # per layer: this GPU's GEMVs alone (the unpooled batched sweep of its
+    # rows, images kernel included) and what the exchange adds on top of them
+    # (pushes from the folds + the sweep's one receive, and any wait for the
+    # slowest GPU)
+    line["config4_layer_split_us"] = {
+        "gemvs": round(kernel_us / LAYERS, 3),
+        "exchange": round(max(0.0, per_step_ms * 1e3 - kernel_us) / LAYERS, 3) if world > 1 else 0.0,
+        "total": round(per_step_ms * 1e3 / LAYERS, 3)}
     if cfg2:
         line["config2_mxfp4_row_sharded"] = cfg2
     line["config1_q4_0_11008x4096"] = cfg1
@@ -886,7 +894,8 @@ def main():
     return 0
 
 
-PROFILE_KERNELS = ("gemv_kernel|k_gemm_tc|k_gemm_fp4|k_quantize_q8_0|k_dequantize_q4_k"
+PROFILE_KERNELS = ("gemv_kernel|gemv_batch_kernel|gemv_images_kernel|k_gemm_tc|k_gemm_fp4"
+                   "|k_quantize_q8_0|k_dequantize_q4_k"
                    "|k_dequantize_q6_k|k_dequantize_batch")
 
 
@@ -964,6 +973,12 @@ def profile_kernels(torch, L):
     run("config4 layer 0: quantizeQ8_0 + dequantGemvI4Q8 38400x4096, then 4096x11008",
         lambda: wl4.layer(None, 0))
     del wl4
+    torch.cuda.empty_cache()
+    # the batched sweep's kernels on two layers (253 MB of weights, above L2):
+    # one gemv_images_kernel, one gemv_batch_kernel over 4 GEMVs
+    wl4b = Cfg4Workload(torch, L, 1, 0, layers=2)
+    run("config4 2 layers batched: images kernel + batch kernel", lambda: wl4b.sweep(None))
+    del wl4b
     torch.cuda.empty_cache()
 
     # k-quant super-block dequantization, 65536 super-blocks (16.7 M values)

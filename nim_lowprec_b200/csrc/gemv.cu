@@ -24,6 +24,7 @@ namespace {
 
 constexpr int kNcw = 16;         // consumer warps per CTA (512 threads)
 constexpr int kMaxStages = 12;
+static_assert(kMaxStages <= 32 && kMaxRing <= 32, "one barrier pair per lane of warp 0");
 constexpr int kTileBytes = 96 * 1024;  // weights + scales of one tile, at most
 // Weight bytes in flight per CTA, at most (but at least two stages): the
 // copies in flight share the SM's part of the HBM stream, so more of them
@@ -152,7 +153,7 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
     sw = std::max(sw, round_up(rt * p.row_bytes, 128));
     ss = std::max(ss, Fmt::kScales ? round_up(rt * p.gpr * 4, 128) : 0);
     tslot = std::max(tslot, round_up(rt * p.tstride, 32));
-    xs = std::max(xs, round_up(p.x_bytes, 128));
+    xs = std::max(xs, round_up(p.x_bytes, 16));
     fbmax = std::max(fbmax, p.fb);
     mmax = std::max(mmax, p.m);
   }
@@ -160,6 +161,9 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   int ring = 2;
   while (ring < 2 * fbmax && 2 * ring * tslot * 4 <= kBatchTerms) ring *= 2;
   for (auto& p : jobs) p.fb = std::min(p.fb, ring / 2);
+  // each image: the staged activations, then the job's parameters
+  const int p_off = round_up(xs, 16);
+  xs = round_up(p_off + static_cast<int>(sizeof(GemvParams)), 128);
   const int per_stage = sw + ss;
   int xbufs = 3, stages = 0;
   for (; xbufs >= 2; --xbufs) {
@@ -176,6 +180,7 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   b.stage_s_bytes = ss;
   b.tslot = tslot;
   b.x_stride = xs;
+  b.p_off = p_off;
   b.off_w = xbufs * xs;
   b.off_s = b.off_w + stages * sw;
   b.off_t = b.off_s + stages * ss;
@@ -204,7 +209,7 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   r = cuda_status(cudaLaunchKernelEx(&cfg, gemv_images_kernel<Fmt>, b));
   if (r == LP_OK) {
     cfg.gridDim = dim3(std::min(mmax, di.sm_count));
-    cfg.blockDim = dim3(32 * (kNcw + 2));
+    cfg.blockDim = dim3(32 * (kNcw + 3));  // + the image loader warp
     cfg.dynamicSmemBytes = smem;
     r = cuda_status(cudaLaunchKernelEx(&cfg, kern, b));
   }

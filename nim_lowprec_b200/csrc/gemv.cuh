@@ -268,16 +268,18 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
   const int row_end = static_cast<int>((static_cast<int64_t>(p.m) * (blockIdx.x + 1)) / gridDim.x);
   const int ntiles = (row_end - row_begin + p.rt - 1) / p.rt;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCW);
+  // one barrier pair per lane of warp 0 (stages <= 12, ring <= 16)
+  if (threadIdx.x < 32) {
+    const int i = threadIdx.x;
+    if (i < p.stages) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NCW);
     }
-    for (int b = 0; b < p.ring; ++b) {
-      mbar_init(&tfull[b], NCW);
-      mbar_init(&tempty[b], 1);
+    if (i < p.ring) {
+      mbar_init(&tfull[i], NCW);
+      mbar_init(&tempty[i], 1);
     }
-    s_abort = 0;
+    if (i == 0) s_abort = 0;
     mbar_fence_init();
   }
   __syncthreads();
@@ -520,7 +522,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
 // folder trails the consumers across job boundaries, and each job's staged
 // activations come from an image a small kernel builds once for the whole
 // batch (byte for byte what the job's consumers would have staged), copied
-// by one bulk copy into one of `xbufs` buffers while earlier jobs compute.
+// by a loader warp into one of `xbufs` buffers while earlier jobs compute.
 //
 // Common layout: every job uses the same weight stages, term slots and
 // activation buffers, so the barriers' phases run on over the whole batch
@@ -535,10 +537,13 @@ struct GemvBatch {
   int stage_w_bytes, stage_s_bytes;
   int tslot;                 // floats per term slot
   int x_stride;              // bytes per activation buffer and per image (128-multiple)
+  int p_off;                 // the job's GemvParams inside its image (after the activations)
   int off_w, off_s, off_t, off_b;  // activation buffers from 0, x_stride apart
   uint8_t* img;              // n images, x_stride apart
   GemvParams job[kMaxBatch];
 };
+
+static_assert(sizeof(GemvParams) % 16 == 0, "job parameters are copied in 16-byte pieces");
 
 // This CTA's rows of a job: [rb, re) in tiles of p.rt (nt = 0: none).
 __device__ __forceinline__ int batch_rows(const GemvParams& p, int& rb, int& nt) {
@@ -556,12 +561,18 @@ __global__ void __launch_bounds__(512) gemv_images_kernel(const __grid_constant_
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int j = blockIdx.x;
-  if (j < b.n)
-    Fmt::stage_x(b.img + static_cast<int64_t>(j) * b.x_stride, b.job[j], threadIdx.x, blockDim.x);
+  if (j >= b.n) return;
+  uint8_t* img = b.img + static_cast<int64_t>(j) * b.x_stride;
+  Fmt::stage_x(img, b.job[j], threadIdx.x, blockDim.x);
+  // the job's own parameters ride along: the consumers read them from
+  // shared memory instead of the kernel's parameter block
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(&b.job[j]);
+  for (int i = threadIdx.x; i < static_cast<int>(sizeof(GemvParams) / 4); i += blockDim.x)
+    reinterpret_cast<uint32_t*>(img + b.p_off)[i] = src[i];
 }
 
 template <class Fmt, int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 2), 1)
+__global__ void __launch_bounds__(32 * (NCW + 3), 1)
     gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
   static_assert(Fmt::kFold != Fold::Tree && !ColsOf<Fmt>::value, "ordered row folds only");
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -574,25 +585,27 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   uint64_t* empty = full + b.stages;
   uint64_t* tfull = empty + b.stages;
   uint64_t* tempty = tfull + b.ring;
-  uint64_t* xfull = tempty + b.ring;  // image landed in buffer i
+  uint64_t* xfull = tempty + b.ring;  // image landed in buffer i (the loader warp's 32 lanes)
   uint64_t* xempty = xfull + b.xbufs; // every consumer warp done with buffer i
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < b.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCW);
+  // one barrier pair per lane of warp 0 (stages <= 12, ring <= 16, xbufs <= 3)
+  if (threadIdx.x < 32) {
+    const int i = threadIdx.x;
+    if (i < b.stages) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NCW);
     }
-    for (int r = 0; r < b.ring; ++r) {
-      mbar_init(&tfull[r], NCW);
-      mbar_init(&tempty[r], 1);
+    if (i < b.ring) {
+      mbar_init(&tfull[i], NCW);
+      mbar_init(&tempty[i], 1);
     }
-    for (int i = 0; i < b.xbufs; ++i) {
-      mbar_init(&xfull[i], 1);
+    if (i < b.xbufs) {
+      mbar_init(&xfull[i], 32);
       mbar_init(&xempty[i], NCW);
     }
-    s_abort = 0;
+    if (i == 0) s_abort = 0;
     mbar_fence_init();
   }
   __syncthreads();
@@ -692,43 +705,18 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       }
       tg += nt;
     }
-  } else {
+  } else if (warp < NCW + 2) {
     // ------------------------------------------------------ consumers
     const int ct = threadIdx.x - 64;
     constexpr int NC = NCW * 32;
-    // The images (and the activations they came from) belong to the kernels
-    // before this one in the stream.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const uint64_t ipol = l2_evict_last();
-    int issued = 0;  // images requested (thread ct == 0 only)
-    auto request = [&](int i) {
-      const int buf = i % b.xbufs;
-      const uint32_t bytes = static_cast<uint32_t>(b.job[i].x_bytes);
-      mbar_arrive_expect_tx(&xfull[buf], bytes);
-      bulk_g2s(smem + buf * b.x_stride, b.img + static_cast<int64_t>(i) * b.x_stride, bytes,
-               &xfull[buf], ipol);
-      ++issued;
-    };
-    if (ct == 0)
-      for (int i = 0; i < min(b.n, b.xbufs - 1); ++i) request(i);
     int tg = 0;
-    int waited = 0;  // images this thread has seen land
     for (int j = 0; j < b.n; ++j) {
-      const GemvParams& p = b.job[j];
-      int rb, nt;
-      const int re = batch_rows(p, rb, nt);
-      // The next image goes into the buffer of job j - 1 once every consumer
-      // warp is done with it.
-      if (ct == 0 && j + b.xbufs - 1 < b.n) {
-        bool ok = true;
-        if (j >= 1) ok = mbar_wait(&xempty[(j - 1) % b.xbufs], ((j - 1) / b.xbufs) & 1, &s_abort);
-        if (ok && !s_abort) request(j + b.xbufs - 1);
-      }
-      __syncwarp();
       const int buf = j % b.xbufs;
       if (!mbar_wait(&xfull[buf], (j / b.xbufs) & 1, &s_abort) || s_abort) break;
-      if (ct == 0) ++waited;
       const uint8_t* xsm = smem + buf * b.x_stride;
+      const GemvParams& p = *reinterpret_cast<const GemvParams*>(xsm + b.p_off);
+      int rb, nt;
+      const int re = batch_rows(p, rb, nt);
       Fmt f;
       const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
       const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
@@ -817,9 +805,36 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&xempty[buf]);
     }
-    // never leave with an image still landing in shared memory
-    if (ct == 0)
-      for (int i = waited; i < issued; ++i) mbar_wait(&xfull[i % b.xbufs], (i / b.xbufs) & 1);
+  } else {
+    // ------------------------------------------------- image loader
+    // Each job's staged activations, copied by this warp's 32 lanes with
+    // 16-byte cp.async (the load path, not the bulk-copy engine: an image
+    // copied in bulk waits behind the weight tiles this SM has in flight)
+    // into the buffer the consumers freed, up to xbufs jobs ahead.  The
+    // images were written by the kernel before this one.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int j = 0; j < b.n; ++j) {
+      const int buf = j % b.xbufs;
+      if (j >= b.xbufs &&
+          !mbar_wait_idle(&xempty[buf], ((j / b.xbufs) - 1) & 1, &s_abort))
+        break;
+      if (s_abort) break;
+      const uint8_t* src = b.img + static_cast<int64_t>(j) * b.x_stride;
+      uint8_t* dst = smem + buf * b.x_stride;
+      for (int o = lane * 16; o < b.job[j].x_bytes; o += 32 * 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst + o)),
+                     "l"(src + o)
+                     : "memory");
+      // and the job's parameters
+      for (int o = lane * 16; o < static_cast<int>(sizeof(GemvParams)); o += 32 * 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst + b.p_off + o)),
+                     "l"(src + b.p_off + o)
+                     : "memory");
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(saddr(&xfull[buf]))
+                   : "memory");
+    }
+    // never leave with a copy still landing in shared memory
+    asm volatile("cp.async.wait_all;" ::: "memory");
   }
 }
 

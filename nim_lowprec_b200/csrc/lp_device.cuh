@@ -121,12 +121,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(saddr(bar)), "l"(policy)
       : "memory");
 }
-// L2 policy for data every CTA reads (staged activations): evict last.
-__device__ __forceinline__ uint64_t l2_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
 // L2 policy for a one-pass weight stream: evict first.
 __device__ __forceinline__ uint64_t l2_evict_first() {
   uint64_t p;

@@ -48,6 +48,15 @@ struct GatherParts {
   int send[kMaxParts];  // 1: the receive kernel also stores this rank's rows of the part
   int n;
 };
+// What this rank receives: every other rank's rows of every part, as
+// segments of the vector laid end to end (start: prefix sums of their
+// lengths; off: each segment's first element in y and in the exchange).
+constexpr int kMaxSegs = kMaxParts * (kMaxP2pRanks - 1);
+struct RecvSegs {
+  int64_t start[kMaxSegs + 1];
+  int64_t off[kMaxSegs];
+  int n;
+};
 }  // namespace
 
 struct lp_pool {
@@ -157,8 +166,10 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 // complete before it reads the gather count: that GEMV had waited for the
 // previous gather in turn, so the count is final, and this gather completes
 // only after its GEMV has.
-__global__ void __launch_bounds__(256) k_gather_p2p(float* y, GatherParts parts, int nranks,
-                                                   int rank, PeerBufs peers, uint32_t* state) {
+__global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_constant__ GatherParts parts,
+                                                   const __grid_constant__ RecvSegs segs,
+                                                   int nranks, int rank, PeerBufs peers,
+                                                   uint32_t* state) {
   __shared__ uint32_t s_e;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t C = gridDim.x;
@@ -185,39 +196,49 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, GatherParts parts,
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(peers.p[rank]) + half;
   bool ok = true;
   const uint64_t t0 = lp::global_ns();
-  for (int pi = 0; pi < parts.n && ok; ++pi) {
-    for (int q = 0; q < nranks && ok; ++q) {
-      if (q == rank) continue;
-      int64_t qb, qe;
-      rows_of(parts.m[pi], nranks, q, &qb, &qe);
-      const int64_t qo = parts.off[pi] + qb * parts.prow[pi];
-      const int64_t ql = (qe - qb) * parts.prow[pi];
-      const int64_t qc = (ql + C - 1) / C;
-      const int64_t qlo = min(ql, blockIdx.x * qc), qhi = min(ql, qlo + qc);
-      // eight words in flight per thread, then wait on any that is not there yet
-      for (int64_t i0 = qlo + tid; i0 < qhi && ok; i0 += 8 * nthr) {
-        uint64_t w[8];
+  // The segments laid end to end, split evenly over the CTAs; each thread
+  // keeps eight words in flight across segment boundaries (one wait for
+  // the whole vector rather than one per part and peer).
+  const int64_t total = segs.start[segs.n];
+  const int64_t per = (total + C - 1) / C;
+  const int64_t lo = min(total, blockIdx.x * per), hi = min(total, lo + per);
+  int sg = 0;  // the segment of index lo + tid, advanced as the index grows
+  {
+    int a = 0, z = segs.n;  // last segment whose start <= lo + tid
+    const int64_t i = lo + tid;
+    while (z - a > 1) {
+      const int mid = (a + z) >> 1;
+      if (segs.start[mid] <= i) a = mid; else z = mid;
+    }
+    sg = a;
+  }
+  for (int64_t i0 = lo + tid; i0 < hi && ok; i0 += 8 * nthr) {
+    uint64_t w[8];
+    int64_t at[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int64_t i = i0 + k * nthr;
-          w[k] = i < qhi ? ld_word(mine + qo + i) : 0;
-        }
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int64_t i = i0 + k * nthr;
-          if (i >= qhi || !ok) continue;
-          for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
-            if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
-              lp::raise_error(LP_ERR_TIMEOUT);
-              ok = false;
-              break;
-            }
-            __nanosleep(64);  // leave the issue slots to the GEMV on this SM
-            w[k] = ld_word(mine + qo + i);
-          }
-          if (ok) y[qo + i] = __uint_as_float(static_cast<uint32_t>(w[k]));
-        }
+    for (int k = 0; k < 8; ++k) {
+      const int64_t i = i0 + k * nthr;
+      at[k] = -1;
+      w[k] = 0;
+      if (i < hi) {
+        while (sg + 1 < segs.n && segs.start[sg + 1] <= i) ++sg;
+        at[k] = segs.off[sg] + (i - segs.start[sg]);
+        w[k] = ld_word(mine + at[k]);
       }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (at[k] < 0 || !ok) continue;
+      for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
+        if ((n & 255u) == 0 && lp::global_ns() - t0 > lp::kWaitLimitNs) {
+          lp::raise_error(LP_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);  // leave the issue slots to the GEMV on this SM
+        w[k] = ld_word(mine + at[k]);
+      }
+      if (ok) y[at[k]] = __uint_as_float(static_cast<uint32_t>(w[k]));
     }
   }
   // the last CTA to finish publishes e as the finished gather count
@@ -233,15 +254,24 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, GatherParts parts,
 }
 
 int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st) {
-  int64_t total = 0, per_rank = 0;
-  for (int i = 0; i < parts.n; ++i) {
-    total += parts.m[i] * parts.prow[i];
-    per_rank += (parts.m[i] / p->nranks + 1) * parts.prow[i];
-  }
-  // CTAs enough for ~1024 received words each, at most 64 (all resident at
-  // once on 148 SMs: a sending CTA waits only after its own stores)
-  const int64_t recv = std::max<int64_t>(0, total - per_rank);
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(64, (recv + 1023) / 1024)));
+  static thread_local RecvSegs segs;
+  segs.n = 0;
+  segs.start[0] = 0;
+  for (int i = 0; i < parts.n; ++i)
+    for (int q = 0; q < p->nranks; ++q) {
+      if (q == p->rank) continue;
+      int64_t b, e;
+      rows_of(parts.m[i], p->nranks, q, &b, &e);
+      if (e == b) continue;
+      segs.off[segs.n] = parts.off[i] + b * parts.prow[i];
+      segs.start[segs.n + 1] = segs.start[segs.n] + (e - b) * parts.prow[i];
+      ++segs.n;
+    }
+  // CTAs enough for ~2048 received words each, at most two per SM (all
+  // resident at once: a sending CTA waits only after its own stores)
+  const int64_t recv = segs.start[segs.n];
+  const int grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(2 * lp::device_info().sm_count, (recv + 2047) / 2048)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(256);
@@ -251,8 +281,8 @@ int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, parts, p->nranks, p->rank,
-                                            p->peers, p->state));
+  return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, parts, segs, p->nranks,
+                                            p->rank, p->peers, p->state));
 }
 
 int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {

@@ -192,8 +192,43 @@ __device__ __forceinline__ float pow2i(int k) {  // exact 2^k, k in [-127, 127]
                    : __uint_as_float(0x00400000u);
 }
 
-// calibrateSymmetric (quant.nim:84-110) and calibrateMX (quant.nim:112-137):
-// one CTA per group.
+// The scale of a group from its max |x| (quant.nim:95-110 symmetric, 125-137 MX).
+__device__ __forceinline__ float group_scale(float v, float qmax, int emax, int mx) {
+  if (mx) {
+    if (v == 0.0f) return 1.0f;
+    int k = floor_log2(v) - emax;
+    k = max(-127, min(127, k));
+    return pow2i(k);
+  }
+  return v == 0.0f ? 1.0f : __fdiv_rn(v, qmax);
+}
+
+// calibrateSymmetric / calibrateMX for groups of 4 * L values, L a power of
+// two <= 32: each thread loads one float4 and L lanes reduce a group with
+// shuffles (max is order-free, fmaxf drops NaN as the scalar scan does).
+// x 16-byte aligned and n % 4 == 0; a ragged last group reads zeros past n.
+template <int L>
+__global__ void __launch_bounds__(256) k_calibrate_vec(const float4* __restrict__ x, int64_t n4,
+                                                       float qmax, int emax, int mx,
+                                                       float* __restrict__ scales, int64_t nscales) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // every lane runs the same number of rounds, so the shuffles stay converged
+  const int64_t total = nscales * L;
+  for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x; t0 < total; t0 += stride) {
+    const int64_t t = t0 + threadIdx.x;
+    float m = 0.0f;
+    if (t < total && t < n4) {
+      const float4 v = __ldg(x + t);
+      m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    }
+#pragma unroll
+    for (int o = L / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & (L - 1)) == 0 && t < total) scales[t / L] = group_scale(m, qmax, emax, mx);
+  }
+}
+
+// calibrateSymmetric (quant.nim:84-110) and calibrateMX (quant.nim:112-137),
+// any group size: one CTA per group.
 __global__ void k_calibrate(const float* __restrict__ x, int64_t n, int64_t gs, float qmax,
                             int emax, int mx, float* __restrict__ scales, int64_t nscales) {
   __shared__ float red[kThreads / 32];
@@ -208,21 +243,7 @@ __global__ void k_calibrate(const float* __restrict__ x, int64_t n, int64_t gs, 
     if (threadIdx.x < 32) {
       float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
       v = warp_max(v);
-      if (threadIdx.x == 0) {
-        float s;
-        if (mx) {
-          if (v == 0.0f) {
-            s = 1.0f;
-          } else {
-            int k = floor_log2(v) - emax;
-            k = max(-127, min(127, k));
-            s = pow2i(k);
-          }
-        } else {
-          s = v == 0.0f ? 1.0f : __fdiv_rn(v, qmax);
-        }
-        scales[g] = s;
-      }
+      if (threadIdx.x == 0) scales[g] = group_scale(v, qmax, emax, mx);
     }
     __syncthreads();
   }
@@ -635,6 +656,24 @@ int launch_quantize_batch(const float* x, int64_t n, const float* scales, const 
 int launch_calibrate(const float* x, int64_t n, int64_t gs, float qmax, int mx_emax, int mx,
                      float* scales, int64_t nscales, cudaStream_t st) {
   if (nscales == 0) return LP_OK;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && n % 4 == 0 && gs % 4 == 0 &&
+                   gs <= 128 && ((gs / 4) & (gs / 4 - 1)) == 0;
+  if (vec) {
+    const int64_t threads = nscales * (gs / 4);
+    const int grid = static_cast<int>(std::min<int64_t>((threads + kThreads - 1) / kThreads,
+                                                        int64_t{device_info().sm_count} * 16));
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int64_t n4 = n / 4;
+    switch (gs / 4) {
+      case 1: k_calibrate_vec<1><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+      case 2: k_calibrate_vec<2><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+      case 4: k_calibrate_vec<4><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+      case 8: k_calibrate_vec<8><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+      case 16: k_calibrate_vec<16><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+      default: k_calibrate_vec<32><<<grid, kThreads, 0, st>>>(x4, n4, qmax, mx_emax, mx, scales, nscales); break;
+    }
+    return cuda_status(cudaGetLastError());
+  }
   const int grid = static_cast<int>(std::min<int64_t>(nscales, device_info().sm_count * 8));
   k_calibrate<<<grid, kThreads, 0, st>>>(x, n, gs, qmax, mx_emax, mx, scales, nscales);
   return cuda_status(cudaGetLastError());

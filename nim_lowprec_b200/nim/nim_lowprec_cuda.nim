@@ -298,3 +298,36 @@ proc parDequantGemvI4Q8*(wpacked: openArray[byte], wScales: openArray[float32],
   check(lph_par_dequant_gemv_i4q8(base(wpacked), wpacked.len, base(wScales), wScales.len,
       groupSize, base(xq), xq.len, base(xScales), xScales.len, base(y), y.len,
       threads.cint), "parDequantGemvI4Q8")
+
+# ---------------------------------------------------- device forms, batched
+# A decode loop whose weights stay on the GPU calls the device forms (device
+# pointers, a CUDA stream) and may bracket a step's GEMVs in one batch: the
+# queued calls run as one persistent launch, each with its own bits
+# (lp_batch_begin / lp_batch_end; no counterpart in the reference).
+
+proc lp_batch_begin(stream: pointer): cint {.importc, dynlib: lpLib.}
+proc lp_batch_end(stream: pointer): cint {.importc, dynlib: lpLib.}
+proc lp_quantize_dequant_gemv_i4q8(w: pointer, wLen: int64, ws: pointer, wsLen: int64,
+    gs: int64, x: pointer, xLen: int64, y: pointer, yLen: int64,
+    stream: pointer): cint {.importc, dynlib: lpLib.}
+proc lp_dequant_gemv_i4q8(w: pointer, wLen: int64, ws: pointer, wsLen: int64, gs: int64,
+    xq: pointer, xqLen: int64, xs: pointer, xsLen: int64, y: pointer, yLen: int64,
+    stream: pointer): cint {.importc, dynlib: lpLib.}
+
+template withBatch*(stream: pointer, body: untyped) =
+  ## The GEMVs `body` issues on `stream` run as batched launches.
+  check(lp_batch_begin(stream), "batchBegin")
+  body
+  check(lp_batch_end(stream), "batchEnd")
+
+proc quantizeDequantGemvI4Q8Dev*(w: pointer, wLen: int, ws: pointer, wsLen: int,
+    x: pointer, xLen: int, y: pointer, yLen: int, stream: pointer) =
+  ## quantizeQ8_0 of device fp32 x, then dequantGemvI4Q8 (group 32), on `stream`.
+  check(lp_quantize_dequant_gemv_i4q8(w, wLen, ws, wsLen, 32, x, xLen, y, yLen, stream),
+      "quantizeDequantGemvI4Q8")
+
+proc dequantGemvI4Q8Dev*(w: pointer, wLen: int, ws: pointer, wsLen: int, groupSize: int,
+    xq: pointer, xqLen: int, xs: pointer, xsLen: int, y: pointer, yLen: int,
+    stream: pointer) =
+  check(lp_dequant_gemv_i4q8(w, wLen, ws, wsLen, groupSize, xq, xqLen, xs, xsLen, y, yLen,
+      stream), "dequantGemvI4Q8")

@@ -175,6 +175,30 @@ def test_quantize_q4_0_sign_keeping_max_ties():
     assert np.array_equal(to_host(blocks), O.quantizeQ4_0(x).reshape(-1))
 
 
+@pytest.mark.parametrize("gs", [4, 8, 16, 32, 64, 128])
+@pytest.mark.parametrize("n", [4096 * 37, 4100, 4])
+def test_calibrate_vector_path_vs_oracle(n, gs):
+    """The float4 form of calibrateSymmetric / calibrateMX (16-byte aligned x,
+    n % 4 == 0, gs / 4 a power of two <= 32): every group size it takes, a
+    ragged last group, all-zero groups, a NaN (dropped by the max, as by the
+    reference's scan) and an infinity."""
+    x = acts(77 + gs, n) * F(3.0)
+    x[: min(n, gs)] = 0.0                      # an all-zero group
+    if n > 3 * gs:
+        x[2 * gs + 1] = np.float32("nan")
+        x[3 * gs] = np.float32("inf")
+    (xd,) = to_dev(x)
+    for qmax in (127.0, 7.0):
+        sc_o = O.calibrateSymmetric(x, gs, qmax)
+        sc = torch.empty(sc_o.size, dtype=torch.float32, device="cuda")
+        L.calibrateSymmetric(xd, gs, qmax, sc)
+        assert_bits(to_host(sc), sc_o)
+    mx_o = O.calibrateMX(x, gs, 2)
+    mx = torch.empty(mx_o.size, dtype=torch.float32, device="cuda")
+    L.calibrateMX(xd, gs, 2, mx)
+    assert_bits(to_host(mx), mx_o)
+
+
 @pytest.mark.parametrize("n,gs", [(4096, 128), (4099, 64), (1000, 0), (4096, 32)])
 def test_quantize_batch_and_calibrate_vs_oracle(n, gs):
     """test_quant_simd.nim:330-355 shapes (per-group, ragged, per-tensor)."""
