@@ -134,10 +134,24 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   });
   static thread_local GemvBatch b;
   b.n = static_cast<int>(jobs.size());
-  int sw = 0, ss = 0, tslot = 0, xs = 0, fbmax = 1, mmax = 0;
+  b.push = nullptr;
+  int sw = 0, ss = 0, tslot = 0, xs = 0, fbmax = 1;
+  // The jobs' rows laid end to end, each weighted by its bytes times the
+  // consumers' slowdown on it: a thread keeps one group of the row, so when
+  // the consumer count is not a multiple of the row's groups some threads
+  // idle (344 groups: 344 of 512 busy, and such rows took 1.46x as long per
+  // byte, measured per CTA).  Equal shares of this weight finish together.
+  constexpr int NC = kNcw * 32;
+  int64_t at = 0;
   for (int j = 0; j < b.n; ++j) {
     GemvParams& p = jobs[j];
     const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
+    const int busy = p.gpr <= NC ? (NC / p.gpr) * p.gpr : NC;
+    const int64_t weight = (static_cast<int64_t>(row_total) * NC + busy - 1) / busy;
+    p.boff = at;
+    p.bend = at + static_cast<int64_t>(p.m) * weight;
+    at = p.bend;
+    if (p.push && !b.push) b.push = p.push;
     // Rows per tile: what fits kBatchTile (at most 32, one folder lane each),
     // in whole row pairs.
     int rt = std::min(32, std::max(1, kBatchTile / std::max(row_total, 1)));
@@ -155,8 +169,8 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
     tslot = std::max(tslot, round_up(rt * p.tstride, 32));
     xs = std::max(xs, round_up(p.x_bytes, 16));
     fbmax = std::max(fbmax, p.fb);
-    mmax = std::max(mmax, p.m);
   }
+  b.total = at;
   // term ring: two passes of the longest fold batch, within kBatchTerms
   int ring = 2;
   while (ring < 2 * fbmax && 2 * ring * tslot * 4 <= kBatchTerms) ring *= 2;
@@ -208,7 +222,7 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   cfg.numAttrs = 1;
   r = cuda_status(cudaLaunchKernelEx(&cfg, gemv_images_kernel<Fmt>, b));
   if (r == LP_OK) {
-    cfg.gridDim = dim3(std::min(mmax, di.sm_count));
+    cfg.gridDim = dim3(di.sm_count);  // one CTA per SM, each a 1/148 share of the bytes
     cfg.blockDim = dim3(32 * (kNcw + 3));  // + the image loader warp
     cfg.dynamicSmemBytes = smem;
     r = cuda_status(cudaLaunchKernelEx(&cfg, kern, b));

@@ -67,6 +67,9 @@ struct GemvParams {
   int ncol;           // activation columns (the small-n GEMM formats); else unused
   const PushCtx* push;  // pooled call: also store every output into the other ranks
   int64_t push_off;     // this slice's first element in the whole y
+  // batched launches: the job's rows in the batch's rows laid end to end,
+  // as a range [boff, bend) of work units (bytes weighted by consumer cost)
+  int64_t boff, bend;
 };
 
 // The pooled form's stores: out value v of y element idx (of this slice) goes
@@ -76,10 +79,10 @@ struct PushTag {
   uint64_t tag = 0;
   int64_t half = 0;
 };
-__device__ __forceinline__ PushTag push_tag(const GemvParams& p) {
+__device__ __forceinline__ PushTag push_tag(const PushCtx* push) {
   PushTag t;
-  if (p.push) {
-    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(p.push->state) + 1u;
+  if (push) {
+    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(push->state) + 1u;
     t.tag = static_cast<uint64_t>(e) << 32;
     t.half = (e & 1u) * kXchgWords;
   }
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
     PushTag pt;
     if (p.push) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      pt = push_tag(p);
+      pt = push_tag(p.push);
     }
     if constexpr (Fmt::kFold == Fold::Tree) {
       for (int t = 0; t < ntiles; ++t) {
@@ -540,17 +543,50 @@ struct GemvBatch {
   int p_off;                 // the job's GemvParams inside its image (after the activations)
   int off_w, off_s, off_t, off_b;  // activation buffers from 0, x_stride apart
   uint8_t* img;              // n images, x_stride apart
+  int64_t total;             // work units of all jobs' rows (job[n - 1].bend)
+  const PushCtx* push;       // the pooled jobs' exchange (one per batch), or null
   GemvParams job[kMaxBatch];
 };
 
 static_assert(sizeof(GemvParams) % 16 == 0, "job parameters are copied in 16-byte pieces");
 
+// Work split.  The jobs' rows, laid end to end in work units (bytes weighted
+// by the consumers' cost per byte, see launch_batch), are cut into one
+// contiguous range per CTA, [cs, ce); a row belongs to the CTA whose range
+// holds its first unit.  So a CTA streams one stretch of HBM and meets only
+// the one to three jobs its range touches, whatever their number or size:
+// a job boundary costs its activations, its parameters and its first tile's
+// latency, which 64 small per-job slices per CTA (a sweep's share on 8 GPUs)
+// would pay 64 times.
+struct CtaRange {
+  int64_t cs, ce;
+};
+__device__ __forceinline__ CtaRange cta_range(int64_t total) {
+  return {total * blockIdx.x / gridDim.x, total * (blockIdx.x + 1) / gridDim.x};
+}
+
 // This CTA's rows of a job: [rb, re) in tiles of p.rt (nt = 0: none).
-__device__ __forceinline__ int batch_rows(const GemvParams& p, int& rb, int& nt) {
-  rb = static_cast<int>((static_cast<int64_t>(p.m) * blockIdx.x) / gridDim.x);
-  const int re = static_cast<int>((static_cast<int64_t>(p.m) * (blockIdx.x + 1)) / gridDim.x);
+__device__ __forceinline__ int batch_rows(const GemvParams& p, const CtaRange& c, int& rb,
+                                          int& nt) {
+  const int64_t rtot = (p.bend - p.boff) / p.m;  // units per row
+  auto first_row = [&](int64_t at) -> int {      // first row starting at or after `at`
+    if (at <= p.boff) return 0;
+    return static_cast<int>(min((at - p.boff + rtot - 1) / rtot, static_cast<int64_t>(p.m)));
+  };
+  rb = first_row(c.cs);
+  const int re = first_row(c.ce);
   nt = (re - rb + p.rt - 1) / p.rt;
   return re;
+}
+
+// The first job whose byte range reaches past cs (jobs are contiguous).
+__device__ __forceinline__ int first_job(const GemvBatch& b, const CtaRange& c) {
+  int lo = 0, hi = b.n;  // first j with job[j].bend > cs
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (b.job[mid].bend > c.cs) hi = mid; else lo = mid + 1;
+  }
+  return lo;
 }
 
 // One block per job: the job's staged activations, written to its image.
@@ -616,12 +652,13 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     // gemv_kernel), so the stream starts before the grid-dependency wait.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint64_t pol = l2_evict_first();
+    const CtaRange cr = cta_range(b.total);
     int tg = 0;
     bool stop = false;
-    for (int j = 0; j < b.n && !stop; ++j) {
+    for (int j = first_job(b, cr); j < b.n && b.job[j].boff < cr.ce && !stop; ++j) {
       const GemvParams& p = b.job[j];
       int rb, nt;
-      const int re = batch_rows(p, rb, nt);
+      const int re = batch_rows(p, cr, rb, nt);
       for (int t = 0; t < nt; ++t, ++tg) {
         const int s = tg % b.stages;
         if (tg >= b.stages && !mbar_wait_idle(&empty[s], ((tg / b.stages) - 1) & 1, &s_abort)) {
@@ -665,18 +702,17 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     // Lane l folds row l % rt of tile l / rt of each pass of fb tiles.  The
     // jobs of a pooled batch share one exchange and one gather number.
     PushTag pt;
-    for (int j = 0; j < b.n; ++j)
-      if (b.job[j].push) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        pt = push_tag(b.job[j]);
-        break;
-      }
+    if (b.push) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      pt = push_tag(b.push);
+    }
+    const CtaRange cr = cta_range(b.total);
     int tg = 0;
     bool stop = false;
-    for (int j = 0; j < b.n && !stop; ++j) {
+    for (int j = first_job(b, cr); j < b.n && b.job[j].boff < cr.ce && !stop; ++j) {
       const GemvParams& p = b.job[j];
       int rb, nt;
-      const int re = batch_rows(p, rb, nt);
+      const int re = batch_rows(p, cr, rb, nt);
       const int ti = lane / p.rt, r = lane - ti * p.rt;
       for (int t0 = 0; t0 < nt; t0 += p.fb) {
         const int nb = min(p.fb, nt - t0);
@@ -709,14 +745,18 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     // ------------------------------------------------------ consumers
     const int ct = threadIdx.x - 64;
     constexpr int NC = NCW * 32;
+    const CtaRange cr = cta_range(b.total);
     int tg = 0;
-    for (int j = 0; j < b.n; ++j) {
-      const int buf = j % b.xbufs;
-      if (!mbar_wait(&xfull[buf], (j / b.xbufs) & 1, &s_abort) || s_abort) break;
+    // The loader fills the buffers with this CTA's jobs in order, then one
+    // whose parameters say m < 0: the end.
+    for (int jl = 0;; ++jl) {
+      const int buf = jl % b.xbufs;
+      if (!mbar_wait(&xfull[buf], (jl / b.xbufs) & 1, &s_abort) || s_abort) break;
       const uint8_t* xsm = smem + buf * b.x_stride;
       const GemvParams& p = *reinterpret_cast<const GemvParams*>(xsm + b.p_off);
+      if (p.m < 0) break;
       int rb, nt;
-      const int re = batch_rows(p, rb, nt);
+      const int re = batch_rows(p, cr, rb, nt);
       Fmt f;
       const int dpr = NC / p.gpr, dg = NC - dpr * p.gpr;
       const int pr0 = ct / p.gpr, g0 = ct - pr0 * p.gpr;
@@ -813,12 +853,24 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     // into the buffer the consumers freed, up to xbufs jobs ahead.  The
     // images were written by the kernel before this one.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int j = 0; j < b.n; ++j) {
-      const int buf = j % b.xbufs;
-      if (j >= b.xbufs &&
-          !mbar_wait_idle(&xempty[buf], ((j / b.xbufs) - 1) & 1, &s_abort))
+    const CtaRange cr = cta_range(b.total);
+    int jl = 0;  // jobs handed to the consumers
+    bool stop = false;
+    for (int j = first_job(b, cr); j < b.n && b.job[j].boff < cr.ce; ++j) {
+      int rb, nt;
+      batch_rows(b.job[j], cr, rb, nt);
+      if (nt == 0) continue;  // the range holds no row start of this job
+      const int buf = jl % b.xbufs;
+      if (jl >= b.xbufs &&
+          !mbar_wait_idle(&xempty[buf], ((jl / b.xbufs) - 1) & 1, &s_abort)) {
+        stop = true;
         break;
-      if (s_abort) break;
+      }
+      if (s_abort) {
+        stop = true;
+        break;
+      }
+      ++jl;
       const uint8_t* src = b.img + static_cast<int64_t>(j) * b.x_stride;
       uint8_t* dst = smem + buf * b.x_stride;
       for (int o = lane * 16; o < b.job[j].x_bytes; o += 32 * 16)
@@ -832,6 +884,15 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
                      : "memory");
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(saddr(&xfull[buf]))
                    : "memory");
+    }
+    // the end marker: a buffer whose parameters say m = -1
+    const int buf = jl % b.xbufs;
+    if (!stop && (jl < b.xbufs ||
+                  mbar_wait_idle(&xempty[buf], ((jl / b.xbufs) - 1) & 1, &s_abort))) {
+      if (lane == 0)
+        reinterpret_cast<GemvParams*>(smem + buf * b.x_stride + b.p_off)->m = -1;
+      __syncwarp();
+      mbar_arrive(&xfull[buf]);  // all 32 lanes: the phase's count
     }
     // never leave with a copy still landing in shared memory
     asm volatile("cp.async.wait_all;" ::: "memory");
