@@ -452,7 +452,11 @@ int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
  * makes the same calls.  On the NVLink transport a pooled call outside the
  * vector, or a 65th part, returns LP_ERR_ARG; begin returns
  * LP_ERR_UNSUPPORTED for a vector larger than the exchange (2^21 floats).
- * On the NCCL transport every call gathers on its own and end does nothing. */
+ * On the NCCL transport every call gathers on its own and end does nothing.
+ * A group of 2^18 floats or more (a whole decode step) has each GEMV publish
+ * its outputs in its own rank's exchange buffer and the receive read the
+ * other ranks' buffers over NVLink; smaller gathers store into every other
+ * rank's buffer from the GEMV.  Same results either way. */
 int lp_pool_group_begin(lp_pool_t pool, float *y, int64_t y_len);
 int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream);
 /* Gather every rank's row slice of y (m rows of per_row floats) in place:

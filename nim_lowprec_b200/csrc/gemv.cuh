@@ -73,8 +73,9 @@ struct GemvParams {
 };
 
 // The pooled form's stores: out value v of y element idx (of this slice) goes
-// to every other rank's exchange buffer as one 8-byte word tagged with the
-// gather number (the receiver polls the word's tag).
+// out as one 8-byte word tagged with the gather number, which the receiver
+// polls (pool.cu): into every other rank's exchange buffer, or, for a large
+// gather, into this rank's own buffer for the others to read.
 struct PushTag {
   uint64_t tag = 0;
   int64_t half = 0;
@@ -88,10 +89,19 @@ __device__ __forceinline__ PushTag push_tag(const PushCtx* push) {
   }
   return t;
 }
+// Pull form: one local store per output, whatever the rank count, so the
+// fold never waits on remote writes (the receivers pay the NVLink reads, in
+// bulk, once per gather).  Push form: the receive is a local read, the better
+// trade for small gathers that come one after another.
 __device__ __forceinline__ void push_out(const GemvParams& p, const PushTag& t, int64_t idx,
                                          float v) {
   const uint64_t w = t.tag | __float_as_uint(v);
   const int nr = p.push->nranks, me = p.push->rank;
+  if (p.push->pull) {
+    uint64_t* a = reinterpret_cast<uint64_t*>(p.push->peers[me]) + t.half + p.push_off + idx;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+    return;
+  }
   for (int q = 0; q < nr; ++q) {
     if (q == me) continue;
     uint64_t* a = reinterpret_cast<uint64_t*>(p.push->peers[q]) + t.half + p.push_off + idx;

@@ -33,6 +33,9 @@ struct PushCtx {
   uint8_t* peers[kMaxPushRanks];  // every rank's exchange buffer as mapped here
   uint32_t* state;                // this rank's finished-gather count (state[0])
   int nranks, rank;
+  // 1: publish each output in this rank's own buffer, the receivers read it
+  // over NVLink (large gathers); 0: store it into every other rank's buffer
+  int pull;
 };
 // Set by the pool around its local call (this thread only): the device copy of
 // the context and the slice's offset in y; launch_gemv reports in g_pushed

@@ -55,6 +55,7 @@ constexpr int kMaxSegs = kMaxParts * (kMaxP2pRanks - 1);
 struct RecvSegs {
   int64_t start[kMaxSegs + 1];
   int64_t off[kMaxSegs];
+  int src[kMaxSegs];  // the rank whose exchange buffer holds the segment
   int n;
 };
 }  // namespace
@@ -67,7 +68,8 @@ struct lp_pool {
   uint8_t* xbuf;   // this rank's exchange buffer: two halves of 8-byte words
   uint32_t* state; // [0] gathers finished, [1] CTAs finished in the current one
   PeerBufs peers;  // every rank's exchange buffer as mapped here
-  lp::PushCtx* push;  // device copy of peers/state for the GEMVs' own stores
+  lp::PushCtx* push;  // device copies of peers/state for the GEMVs' own stores:
+  lp::PushCtx* pull;  // push form, and pull form (large gathers; see gather_parts)
   // gather group (lp_pool_group_begin/end): pooled calls whose outputs are
   // parts of one vector push into it and the group receives once
   bool grp;
@@ -135,9 +137,13 @@ __host__ __device__ inline void rows_of(int64_t m, int nranks, int rank, int64_t
 }
 
 // ------------------------------------------------- NVLink exchange gather
-// Every value crosses as one naturally aligned 8-byte store of (gather number
-// << 32 | value bits), which lands whole; the receiver polls each of its words
-// until the word carries this gather's number.  No fences or counters: a
+// Every value travels as one naturally aligned 8-byte word (gather number <<
+// 32 | value bits), written whole; the receiver polls each word until it
+// carries this gather's number.  Push form: the owner stores the word into
+// every other rank's exchange buffer and each receiver reads its own buffer.
+// Pull form (large gathers, see kPullFloats): the owner stores the word once,
+// into its own buffer, and each receiver reads the owners' buffers over NVLink
+// (every buffer is mapped into every rank).  No fences or counters: a
 // system-scope fence costs microseconds here.
 __device__ __forceinline__ void st_word(uint64_t* a, uint64_t v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
@@ -151,11 +157,12 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 // Gather number e (1, 2, ...) uses exchange half e & 1, so a rank one gather
 // ahead writes the other half while its peers still read this one (two ahead
 // is impossible: finishing a gather needs every peer's words of that gather,
-// and a peer sends them only after finishing the previous one).  e is kept on
+// and a peer sends them only after finishing the previous one, its reads
+// included).  This holds for both forms and for gathers of mixed forms.  e is kept on
 // the device (state[0]) so CUDA-graph replays count too; all ranks make the
 // same gathers, so they agree on it.  Waits are bounded (error word on
 // timeout).
-// send == 0: this rank's words were already stored by the GEMV that made
+// send == 0: this rank's words were already published by the GEMV that made
 // its slice (the fused pooled form); only receive.  The kernel is launched
 // with programmatic stream serialization and releases its dependents at
 // once, so the next kernel (typically the next GEMV) can stage its weights
@@ -169,7 +176,7 @@ __device__ __forceinline__ uint64_t ld_word(const uint64_t* a) {
 __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_constant__ GatherParts parts,
                                                    const __grid_constant__ RecvSegs segs,
                                                    int nranks, int rank, PeerBufs peers,
-                                                   uint32_t* state) {
+                                                   uint32_t* state, int pull) {
   __shared__ uint32_t s_e;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int64_t C = gridDim.x;
@@ -189,11 +196,14 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_const
     const int64_t lo = min(len, blockIdx.x * chunk), hi = min(len, lo + chunk);
     for (int64_t i = lo + tid; i < hi; i += nthr) {
       const uint64_t w = tag | __float_as_uint(y[off + i]);
-      for (int q = 0; q < nranks; ++q)
-        if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
+      if (pull) {
+        st_word(reinterpret_cast<uint64_t*>(peers.p[rank]) + half + off + i, w);
+      } else {
+        for (int q = 0; q < nranks; ++q)
+          if (q != rank) st_word(reinterpret_cast<uint64_t*>(peers.p[q]) + half + off + i, w);
+      }
     }
   }
-  const uint64_t* mine = reinterpret_cast<const uint64_t*>(peers.p[rank]) + half;
   bool ok = true;
   const uint64_t t0 = lp::global_ns();
   // The segments laid end to end, split evenly over the CTAs; each thread
@@ -215,15 +225,19 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_const
   for (int64_t i0 = lo + tid; i0 < hi && ok; i0 += 8 * nthr) {
     uint64_t w[8];
     int64_t at[8];
+    const uint64_t* from[8];  // the word in its owner's exchange buffer
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int64_t i = i0 + k * nthr;
       at[k] = -1;
       w[k] = 0;
+      from[k] = nullptr;
       if (i < hi) {
         while (sg + 1 < segs.n && segs.start[sg + 1] <= i) ++sg;
         at[k] = segs.off[sg] + (i - segs.start[sg]);
-        w[k] = ld_word(mine + at[k]);
+        from[k] = reinterpret_cast<const uint64_t*>(peers.p[pull ? segs.src[sg] : rank]) + half +
+                  at[k];
+        w[k] = ld_word(from[k]);
       }
     }
 #pragma unroll
@@ -236,7 +250,7 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_const
           break;
         }
         __nanosleep(64);  // leave the issue slots to the GEMV on this SM
-        w[k] = ld_word(mine + at[k]);
+        w[k] = ld_word(from[k]);
       }
       if (ok) y[at[k]] = __uint_as_float(static_cast<uint32_t>(w[k]));
     }
@@ -253,7 +267,16 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_const
   }
 }
 
-int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st) {
+// A gather of at least kPullFloats values (a whole decode step in one group)
+// takes the pull form: its GEMVs publish each output with one local store and
+// the receive reads the other ranks' buffers.  Smaller ones take the push
+// form.  Measured on 2 GPUs: the config-4 sweep in one group gains 6 % with
+// pull (0.91 against 1.62 us of exchange per layer); a group per layer loses
+// 18 % (each receive waits on remote reads).  The choice depends on the
+// group's length only, so every rank makes the same one.
+constexpr int64_t kPullFloats = int64_t{1} << 18;
+
+int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st, int pull) {
   static thread_local RecvSegs segs;
   segs.n = 0;
   segs.start[0] = 0;
@@ -264,6 +287,7 @@ int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st
       rows_of(parts.m[i], p->nranks, q, &b, &e);
       if (e == b) continue;
       segs.off[segs.n] = parts.off[i] + b * parts.prow[i];
+      segs.src[segs.n] = q;
       segs.start[segs.n + 1] = segs.start[segs.n] + (e - b) * parts.prow[i];
       ++segs.n;
     }
@@ -282,7 +306,7 @@ int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return lp::cuda_status(cudaLaunchKernelEx(&cfg, k_gather_p2p, y, parts, segs, p->nranks,
-                                            p->rank, p->peers, p->state));
+                                            p->rank, p->peers, p->state, pull));
 }
 
 int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st, int send) {
@@ -292,7 +316,7 @@ int gather_p2p(lp_pool* p, float* y, int64_t m, int64_t per_row, cudaStream_t st
   parts.m[0] = m;
   parts.prow[0] = per_row;
   parts.send[0] = send;
-  return gather_parts(p, y, parts, st);
+  return gather_parts(p, y, parts, st, 0);
 }
 
 // y[0, m*per_row) from every rank's slice of rows.
@@ -324,6 +348,7 @@ void setup_p2p(lp_pool* p) {
   p->xbuf = nullptr;
   p->state = nullptr;
   p->push = nullptr;
+  p->pull = nullptr;
   std::memset(&p->peers, 0, sizeof(p->peers));
   if (p->nranks < 2) return;
   const NcclApi& api = nccl();
@@ -395,11 +420,14 @@ void setup_p2p(lp_pool* p) {
     h.state = p->state;
     h.nranks = p->nranks;
     h.rank = p->rank;
-    if (cudaMalloc(&p->push, sizeof(h)) != cudaSuccess ||
-        cudaMemcpy(p->push, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) {
+    lp::PushCtx hh[2] = {h, h};
+    hh[1].pull = 1;
+    if (cudaMalloc(&p->push, sizeof(hh)) != cudaSuccess ||
+        cudaMemcpy(p->push, hh, sizeof(hh), cudaMemcpyHostToDevice) != cudaSuccess) {
       if (p->push) cudaFree(p->push);
       p->push = nullptr;
     }
+    p->pull = p->push ? p->push + 1 : nullptr;
     cudaGetLastError();
   }
   p->p2p = all_ok;
@@ -412,8 +440,9 @@ void teardown_p2p(lp_pool* p) {
     if (p->peers.p[q] && q != p->rank) cudaIpcCloseMemHandle(p->peers.p[q]);
   if (p->xbuf) cudaFree(p->xbuf);
   if (p->state) cudaFree(p->state);
-  if (p->push) cudaFree(p->push);
+  if (p->push) cudaFree(p->push);  // both contexts (one allocation)
   p->push = nullptr;
+  p->pull = nullptr;
   std::memset(&p->peers, 0, sizeof(p->peers));
   p->xbuf = nullptr;
   p->state = nullptr;
@@ -534,7 +563,7 @@ int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream) {
   if (pool->grp_parts.n == 0 || pool->nranks < 2) return LP_OK;
   int r = lp::cuda_status(cudaSetDevice(pool->device));
   if (r) return r;
-  r = gather_parts(pool, pool->grp_y, pool->grp_parts, S(stream));
+  r = gather_parts(pool, pool->grp_y, pool->grp_parts, S(stream), pool->grp_len >= kPullFloats);
   pool->grp_parts.n = 0;
   return r;
 }
@@ -569,7 +598,8 @@ int lp_pool_gather_rows(lp_pool_t pool, float* y, int64_t m, int64_t per_row, lp
   if (pool->grp && pool->p2p && pool->push && !ingrp_) return LP_ERR_ARG; \
   const bool fuse_ = pool->p2p && pool->push &&                        \
                      (ingrp_ ? pool->grp_len : m_ * (per_row)) <= kXchgFloats; \
-  lp::g_push = fuse_ ? pool->push : nullptr;                          \
+  lp::g_push = !fuse_ ? nullptr                                       \
+               : (ingrp_ && pool->grp_len >= kPullFloats) ? pool->pull : pool->push; \
   lp::g_push_off = goff_ * ingrp_ + b_ * (per_row);                   \
   lp::g_pushed = false;
 

@@ -9,6 +9,7 @@ or an NCCL group) -- and the two must agree bit for bit: sharded == serial
 remainder, and the reference test's own cases (300 / 64 / 1 rows, so some
 ranks hold no rows at all) for every pooled GEMV form.
 """
+import contextlib
 import os
 import socket
 
@@ -189,6 +190,38 @@ def _rank_main(rank, world, port, q):
                     same(f"batch-group{rep_}-{i_}", yb[off:off + mj], rj)
                     off += mj
                 same(f"batch-group{rep_}-q8", yb[off:], refq8)
+            # a group of >= 2^18 floats takes the pull form of the exchange
+            # (outputs published in their owner's buffer, read by the others),
+            # batched and as lone calls, with a part whose kernel does not
+            # publish (the tensor-core GEMM) sent by the receive kernel
+            big = []
+            for mj in (130_003, 120_000, 64):
+                wj = rnd(mj * 64, 0.02)
+                sj = torch.empty(mj * 2, device="cuda")
+                L.calibrateSymmetric(wj, 32, 7.0, sj)
+                pj = torch.empty(mj * 32, dtype=torch.uint8, device="cuda")
+                L.quantizeI4Packed(wj, sj, 32, pj)
+                rj = torch.empty(mj, device="cuda")
+                L.dequantGemvI4Q8(pj, sj, 32, xq[:64], xd[:2], rj)
+                big.append((mj, pj, sj, rj))
+            totb = sum(b_[0] for b_ in big) + M * ng
+            assert totb >= 1 << 18
+            for batched in (True, False):
+                yb = torch.full((totb,), float("nan"), device="cuda")
+                ctx = L.batch() if batched else contextlib.nullcontext()
+                with ctx:
+                    npl.group_begin(yb)
+                    off = 0
+                    for mj, pj, sj, _ in big:
+                        P.parDequantGemvI4Q8(npl, pj, sj, 32, xq[:64], xd[:2], yb[off:off + mj])
+                        off += mj
+                    P.parDequantGemmQ8(npl, wq, wd, 32, xqg, xdg, ng, yb[off:])
+                    npl.group_end()
+                off = 0
+                for i_, (mj, _p, _s, rj) in enumerate(big):
+                    same(f"pull-group-b{int(batched)}-{i_}", yb[off:off + mj], rj)
+                    off += mj
+                same(f"pull-group-b{int(batched)}-gemm", yb[off:], refgm)
         # the library pool gathers over NVLink by default (one GPU per rank);
         # both transports, back-to-back gathers (alternating exchange halves)
         # and CUDA-graph replays give the single-GPU bits
