@@ -167,3 +167,16 @@ def test_local_pool_handles_without_a_gpu():
     if not torch.cuda.is_available():
         assert lib.lph_pool_init(ctypes.byref(h), 2) == N.LP_ERR_NO_DEVICE
         assert lib.lph_par_dequant_gemv(w, 3 * 64, s, 6, 32, x, 64, y, 3, 0) == N.LP_ERR_NO_DEVICE
+
+
+def test_batch_bracket_without_queued_calls():
+    """lp_batch_begin / lp_batch_end with nothing queued launch nothing (no
+    device needed); a nested begin ends the open batch; argument errors of a
+    call made inside a batch return at once, as outside one."""
+    L = N.lib()
+    assert L.lp_batch_begin(NULL) == N.LP_OK
+    assert L.lp_batch_begin(NULL) == N.LP_OK      # ends the open one
+    assert L.lp_quantize_dequant_gemv_i4q8(NULL, 63, NULL, 4, 32, NULL, 64, NULL, 2,
+                                           NULL) == N.LP_ERR_SHAPE
+    assert L.lp_batch_end(NULL) == N.LP_OK
+    assert L.lp_batch_end(NULL) == N.LP_OK        # no open batch: nothing to do
