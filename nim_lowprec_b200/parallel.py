@@ -139,10 +139,13 @@ class NcclPool:
     def call(self, name: str, *args):
         N.check(getattr(N.lib(), name)(self._h, *args), name)
 
-    def group_begin(self, y):
+    def group_begin(self, y, n=None):
         """Pooled calls until group_end write parts of y and are received
-        once (lp_pool_group_begin)."""
-        N.check(N.lib().lp_pool_group_begin(self._h, _dev(y), _numel(y)), "lp_pool_group_begin")
+        once (lp_pool_group_begin).  y: a device tensor, or a device address
+        (e.g. of page-locked host memory, _native.host_device_pointer) with
+        its length n in floats."""
+        ptr, length = (y, n) if n is not None else (_dev(y), _numel(y))
+        N.check(N.lib().lp_pool_group_begin(self._h, ptr, length), "lp_pool_group_begin")
 
     def group_end(self):
         N.check(N.lib().lp_pool_group_end(self._h, _stream()), "lp_pool_group_end")

@@ -196,3 +196,28 @@ def test_batch_replayed_from_cuda_graph():
         q, sc = O.quantizeQ8_0Split(x)
         assert_bits(to_host(y), O.dequantGemvI4Q8(c[2], c[3], 32, q, sc))
     del g
+
+
+def test_batch_on_page_locked_host_buffers():
+    """The decode-loop form: activations and outputs in page-locked host
+    memory, passed by their device addresses (lp_host_device_pointer) to
+    queued calls -- the images kernel reads x over the host link and the
+    folds write y there -- give the device-buffer bits."""
+    shapes = [(4800, 4096), (512, 11008), (300, 4096)]
+    cs = cases(i4_case, shapes, seed=1200)
+    xh = [torch.from_numpy(c[4]).pin_memory() for c in cs]
+    yh = [torch.full((c[0],), float("nan"), dtype=torch.float32).pin_memory() for c in cs]
+    xdev = [N.host_device_pointer(t.data_ptr()) for t in xh]
+    ydev = [N.host_device_pointer(t.data_ptr()) for t in yh]
+    lib = N.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    with L.batch():
+        for c, xa, ya in zip(cs, xdev, ydev):
+            m, k, wd, sd = c[0], c[1], c[5], c[6]
+            N.check(lib.lp_quantize_dequant_gemv_i4q8(wd.data_ptr(), wd.numel(), sd.data_ptr(),
+                                                      sd.numel(), 32, xa, k, ya, m, st), "gemv")
+    torch.cuda.synchronize()
+    for c, y in zip(cs, yh):
+        yd = dev_y(c[0])
+        L.quantizeDequantGemvI4Q8(c[5], c[6], 32, c[7], yd)
+        assert_bits(y.numpy(), to_host(yd))
