@@ -635,6 +635,8 @@ def main():
                     help="launch each hot kernel once (for ncu), no timing")
     ap.add_argument("--sweep-only", action="store_true",
                     help="one GPU: W + K eager config-4 sweeps and nothing else (ncu launch list)")
+    ap.add_argument("--per-call", action="store_true",
+                    help="with --sweep-only: one launch per GEMV instead of one batch per sweep")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -652,7 +654,7 @@ def main():
         wl4 = Cfg4Workload(torch, L, 1, 0)
         torch.cuda.synchronize()
         for _ in range(args.warmup + args.steps):
-            wl4.sweep(None)
+            wl4.sweep(None, batched=not args.per_call)
         torch.cuda.synchronize()
         print(f"swept {args.warmup + args.steps} times", flush=True)
         return 0
