@@ -80,7 +80,20 @@ struct SmemLimits {
 // gemv_images_kernel that stages every job's activations.
 namespace {
 
+// Every row-folded format (the multi-column ones fold virtual rows).
 template <class Fmt> struct Batchable : std::false_type {};
+template <> struct Batchable<FmtI8> : std::true_type {};
+template <> struct Batchable<FmtI4> : std::true_type {};
+template <> struct Batchable<FmtF4> : std::true_type {};
+template <> struct Batchable<FmtQ8_0> : std::true_type {};
+template <> struct Batchable<FmtQ4_0> : std::true_type {};
+template <> struct Batchable<FmtI8F> : std::true_type {};
+template <> struct Batchable<FmtI4F> : std::true_type {};
+template <> struct Batchable<FmtF4F> : std::true_type {};
+template <> struct Batchable<FmtQ8_0F> : std::true_type {};
+template <> struct Batchable<FmtQ4_0F> : std::true_type {};
+template <> struct Batchable<FmtQ4_KF> : std::true_type {};
+template <> struct Batchable<FmtQ6_KF> : std::true_type {};
 template <> struct Batchable<FmtQ8> : std::true_type {};
 template <> struct Batchable<FmtI4Q8> : std::true_type {};
 template <> struct Batchable<FmtQ8FromF32> : std::true_type {};
@@ -114,6 +127,29 @@ struct BatchState {
 };
 thread_local BatchState g_batch;
 
+// The images' memory pool of a device: the library's own (the device's
+// default pool is left as it is), keeping what it has reserved across
+// synchronisations so an eager decode loop does not map memory every step.
+cudaMemPool_t image_pool(int device) {
+  static cudaMemPool_t pools[kMaxDevices];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  cudaMemPool_t& pool = pools[device % kMaxDevices];
+  if (!pool) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      pool = nullptr;
+      return nullptr;
+    }
+    uint64_t keep = 64ull << 20;  // up to 64 MB stays reserved
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  return pool;
+}
+
 // Plan the batch's common layout and launch the images and batch kernels;
 // LP_ERR_UNSUPPORTED when the jobs do not share one layout in shared memory.
 template <class Fmt>
@@ -135,7 +171,6 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   static thread_local GemvBatch b;
   b.n = static_cast<int>(jobs.size());
   b.push = nullptr;
-  int sw = 0, ss = 0, tslot = 0, xs = 0, fbmax = 1;
   // The jobs' rows laid end to end, each weighted by its bytes times the
   // consumers' slowdown on it: a thread keeps one group of the row, so when
   // the consumer count is not a multiple of the row's groups some threads
@@ -152,38 +187,65 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
     p.bend = at + static_cast<int64_t>(p.m) * weight;
     at = p.bend;
     if (p.push && !b.push) b.push = p.push;
-    // Rows per tile: what fits kBatchTile (at most 32, one folder lane each),
-    // in whole row pairs.
-    int rt = std::min(32, std::max(1, kBatchTile / std::max(row_total, 1)));
-    rt = rt >= 2 ? rt & ~1 : 1;
-    p.rt = rt;
-    p.tstride = round_up(p.gpr, 32) + 4;
-    p.fb = std::max(1, std::min(kMaxRing / 2, 32 / rt));
     p.x_bytes = round_up(x_stage_bytes<Fmt>(p), 16);
     const uintptr_t wa = reinterpret_cast<uintptr_t>(p.w);
     const uintptr_t sa = reinterpret_cast<uintptr_t>(p.ws);
     p.bulk = (p.row_bytes % 16 == 0) && (wa % 16 == 0) &&
              (!Fmt::kScales || ((p.gpr % 4 == 0) && (sa % 16 == 0)));
-    sw = std::max(sw, round_up(rt * p.row_bytes, 128));
-    ss = std::max(ss, Fmt::kScales ? round_up(rt * p.gpr * 4, 128) : 0);
-    tslot = std::max(tslot, round_up(rt * p.tstride, 32));
-    xs = std::max(xs, round_up(p.x_bytes, 16));
-    fbmax = std::max(fbmax, p.fb);
   }
   b.total = at;
-  // term ring: two passes of the longest fold batch, within kBatchTerms
-  int ring = 2;
-  while (ring < 2 * fbmax && 2 * ring * tslot * 4 <= kBatchTerms) ring *= 2;
-  for (auto& p : jobs) p.fb = std::min(p.fb, ring / 2);
-  // each image: the staged activations, then the job's parameters
-  const int p_off = round_up(xs, 16);
-  xs = round_up(p_off + static_cast<int>(sizeof(GemvParams)), 128);
-  const int per_stage = sw + ss;
-  int xbufs = 3, stages = 0;
-  for (; xbufs >= 2; --xbufs) {
-    const int fixed = 128 + xbufs * xs + ring * tslot * 4 + 8 * (2 * kMaxStages + 2 * ring + 2 * xbufs);
-    stages = std::min(kMaxStages, (one[slot] - fixed) / per_stage);
-    stages = std::min(stages, std::max(2, kBatchFlight / per_stage));
+  // The common layout, with tiles of at most kBatchTile bytes, or smaller
+  // where the activation buffers (fp32 formats at long rows) leave no room
+  // for two stages of them.
+  int sw = 0, ss = 0, tslot = 0, xs = 0, ring = 2, p_off = 0, xbufs = 0, stages = 0;
+  for (int tile = kBatchTile; tile >= 16 * 1024; tile -= 8 * 1024) {
+    sw = ss = tslot = xs = 0;
+    int fbmax = 1;
+    for (auto& p : jobs) {
+      // Rows per tile: what fits the tile (at most 32, one folder lane
+      // each), in whole row pairs.
+      const int row_total = p.row_bytes + (Fmt::kScales ? p.gpr * 4 : 0);
+      int rt = std::min(32, std::max(1, tile / std::max(row_total, 1)));
+      rt = rt >= 2 ? rt & ~1 : 1;
+      p.rt = rt;
+      p.tstride = round_up(p.gpr, 32) + 4;
+      p.tcols = p.gpr;
+      p.wred = 0;
+      p.fb = std::max(1, std::min(kMaxRing / 2, 32 / rt));
+      if (Fmt::kFold == Fold::Tree) {
+        // the unordered fold goes tile by tile; consumer warps pre-reduce
+        // 32 groups when each warp holds 32 groups of one row pair (as
+        // planned for gemv_kernel)
+        p.fb = 1;
+        if (p.gpr % 32 == 0 && NC % p.gpr == 0) {
+          p.wred = 1;
+          p.tcols = p.gpr / 32;
+          p.tstride = round_up(p.tcols, 4) + 4;
+        }
+      }
+      sw = std::max(sw, round_up(rt * p.row_bytes, 128));
+      ss = std::max(ss, Fmt::kScales ? round_up(rt * p.gpr * 4, 128) : 0);
+      tslot = std::max(tslot, round_up(rt * p.tstride, 32));
+      xs = std::max(xs, round_up(p.x_bytes, 16));
+      fbmax = std::max(fbmax, p.fb);
+    }
+    // term ring: two passes of the longest fold batch (four tiles for the
+    // unordered fold, which lets the consumers run ahead), within kBatchTerms
+    const int want = Fmt::kFold == Fold::Tree ? 4 : 2 * fbmax;
+    ring = 2;
+    while (ring < want && 2 * ring * tslot * 4 <= kBatchTerms) ring *= 2;
+    for (auto& p : jobs) p.fb = std::min(p.fb, ring / 2);
+    // each image: the staged activations, then the job's parameters
+    p_off = round_up(xs, 16);
+    xs = round_up(p_off + static_cast<int>(sizeof(GemvParams)), 128);
+    const int per_stage = sw + ss;
+    for (xbufs = 3; xbufs >= 2; --xbufs) {
+      const int fixed =
+          128 + xbufs * xs + ring * tslot * 4 + 8 * (2 * kMaxStages + 2 * ring + 2 * xbufs);
+      stages = std::min(kMaxStages, (one[slot] - fixed) / per_stage);
+      stages = std::min(stages, std::max(2, kBatchFlight / per_stage));
+      if (stages >= 2) break;
+    }
     if (stages >= 2) break;
   }
   if (stages < 2 || one[slot] <= 0) return LP_ERR_UNSUPPORTED;
@@ -201,12 +263,14 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   b.off_b = b.off_t + ring * tslot * 4;
   const int smem = 128 + b.off_b + 8 * (2 * stages + 2 * ring + 2 * xbufs);
   for (int j = 0; j < b.n; ++j) b.job[j] = jobs[j];
-  // The images live for this launch only: a stream-ordered allocation, freed
-  // in stream order after the batch kernel (graph memory nodes when the
-  // stream is being captured), so batches on other streams or in other
-  // graphs never share them.
+  // The images live for this launch only: a stream-ordered allocation (from
+  // the library's pool), freed in stream order after the batch kernel (graph
+  // memory nodes when the stream is being captured), so batches on other
+  // streams or in other graphs never share them.
   void* img = nullptr;
-  int r = cuda_status(cudaMallocAsync(&img, static_cast<size_t>(b.n) * xs, st));
+  cudaMemPool_t ipool = image_pool(di.ordinal);
+  int r = ipool ? cuda_status(cudaMallocFromPoolAsync(&img, static_cast<size_t>(b.n) * xs, ipool, st))
+                : cuda_status(cudaMallocAsync(&img, static_cast<size_t>(b.n) * xs, st));
   if (r != LP_OK) return r;
   b.img = static_cast<uint8_t*>(img);
 

@@ -541,7 +541,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1) gemv_kernel(const GemvParam
 // activation buffers, so the barriers' phases run on over the whole batch
 // (tile counter tg across jobs).  Per job: rows per tile rt, term stride
 // tstride, fold batch fb (<= ring / 2) and its image's byte count x_bytes.
-// Ordered folds only (the bit-exact paths).
+// Ordered folds go fb tiles per pass; the unordered (block-float) fold goes
+// tile by tile, from the consumer warps' 32-group partial sums where the job
+// allows them (wred), as in gemv_kernel.
 constexpr int kMaxBatch = 64;
 
 struct GemvBatch {
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(512) gemv_images_kernel(const __grid_constant_
 template <class Fmt, int NCW>
 __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
-  static_assert(Fmt::kFold != Fold::Tree && !ColsOf<Fmt>::value, "ordered row folds only");
+  static_assert(!ColsOf<Fmt>::value, "row folds only");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ volatile int s_abort;
   uint8_t* smem = smem_raw + ((128u - (saddr(smem_raw) & 127u)) & 127u);
@@ -709,8 +711,9 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
         mbar_wait(&full[u % b.stages], (u / b.stages) & 1);
   } else if (warp == 1) {
     // --------------------------------------------------------- folder
-    // Lane l folds row l % rt of tile l / rt of each pass of fb tiles.  The
-    // jobs of a pooled batch share one exchange and one gather number.
+    // Lane l folds row l % rt of tile l / rt of each pass of fb tiles (the
+    // unordered fold: all lanes on each tile in turn).  The jobs of a pooled
+    // batch share one exchange and one gather number.
     PushTag pt;
     if (b.push) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -723,6 +726,22 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
       const GemvParams& p = b.job[j];
       int rb, nt;
       const int re = batch_rows(p, cr, rb, nt);
+      if constexpr (Fmt::kFold == Fold::Tree) {
+        for (int t = 0; t < nt; ++t) {
+          const int slot = (tg + t) % b.ring;
+          if (!mbar_wait_idle(&tfull[slot], ((tg + t) / b.ring) & 1, &s_abort) || s_abort) {
+            stop = true;
+            break;
+          }
+          const int r0 = rb + t * p.rt;
+          tree_fold(terms + slot * b.tslot, p.tstride, min(p.rt, re - r0), p.tcols, p.y + r0,
+                    lane, p, pt, r0);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[slot]);
+        }
+        tg += nt;
+        continue;
+      }
       const int ti = lane / p.rt, r = lane - ti * p.rt;
       for (int t0 = 0; t0 < nt; t0 += p.fb) {
         const int nb = min(p.fb, nt - t0);
@@ -806,6 +825,10 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
               f.fix2(p, W + rc * p.row_bytes, W + rd * p.row_bytes, S + rc * p.gpr,
                      S + rd * p.gpr, g, t2, t3);
             }
+            if (Fmt::kFold == Fold::Tree && p.wred) {
+              store_warp_sums(T, p.tstride, rows, ra, rc, t0, t1, t2, t3, g >> 5, lane);
+              continue;
+            }
             T[ra * p.tstride + g] = t0;
             if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
             T[rc * p.tstride + g] = t2;
@@ -820,6 +843,10 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
             if constexpr (Fmt::kFix)
               f.fix2(p, W + ra * p.row_bytes, W + rb2 * p.row_bytes, S + ra * p.gpr,
                      S + rb2 * p.gpr, g, t0, t1);
+            if (Fmt::kFold == Fold::Tree && p.wred) {
+              store_warp_sums(T, p.tstride, rows, ra, -1, t0, t1, 0.0f, 0.0f, g >> 5, lane);
+              continue;
+            }
             T[ra * p.tstride + g] = t0;
             if (ra + 1 < rows) T[(ra + 1) * p.tstride + g] = t1;
           }

@@ -221,3 +221,112 @@ def test_batch_on_page_locked_host_buffers():
         yd = dev_y(c[0])
         L.quantizeDequantGemvI4Q8(c[5], c[6], 32, c[7], yd)
         assert_bits(y.numpy(), to_host(yd))
+
+
+# ---- fp32-activation formats: exact mode bit for bit, fast mode in tolerance
+
+FP32_SHAPES = [(7, 4096), (300, 11008), (4800, 4096), (149, 64), (2, 96), (1000, 2048)]
+
+
+def fp32_jobs(seed, shapes=FP32_SHAPES):
+    """One call per (shape, format): the three group formats (gs 32) and the
+    two ggml block formats, each with its oracle and dequantized values."""
+    from test_gpu_fast_fp32 import vals_blocks, vals_f4, vals_i4, vals_i8
+    jobs = []
+    for i, (m, k) in enumerate(shapes):
+        w = weights(seed + i, m * k)
+        x = acts(seed + 100 + i, k)
+        s8 = O.calibrateSymmetric(w, 32, 127.0)
+        q8 = O.quantize(w, s8, 32, "i8")
+        s4 = O.calibrateSymmetric(w, 32, 7.0)
+        p4 = O.packInt4(O.quantize(w, s4, 32, "i4"))
+        sm = O.calibrateMX(w, 32, 2)
+        pf = O.packF4(O.quantize(w, sm, 32, "f4"))
+        b8 = O.quantizeQ8_0(w).reshape(-1)
+        b4 = O.quantizeQ4_0(w).reshape(-1)
+        xd = to_dev(x)[0]
+        for fn, args, ofn, vals in (
+                (L.dequantGemv, (q8, s8), lambda a=q8, b=s8, x=x: O.dequantGemv(a, b, 32, x),
+                 lambda a=q8, b=s8, k=k: vals_i8(a, b, 32, k)),
+                (L.dequantGemvI4, (p4, s4), lambda a=p4, b=s4, x=x: O.dequantGemvI4(a, b, 32, x),
+                 lambda a=p4, b=s4, k=k: vals_i4(a, b, 32, k)),
+                (L.dequantGemvF4, (pf, sm), lambda a=pf, b=sm, x=x: O.dequantGemvF4(a, b, 32, x),
+                 lambda a=pf, b=sm, k=k: vals_f4(a, b, 32, k)),
+                (L.dequantGemvQ8_0, (b8,), lambda a=b8, x=x, k=k: O.dequantGemvQ8_0(a, k // 32, x),
+                 lambda a=b8, k=k: vals_blocks(a, k, False)),
+                (L.dequantGemvQ4_0, (b4,), lambda a=b4, x=x, k=k: O.dequantGemvQ4_0(a, k // 32, x),
+                 lambda a=b4, k=k: vals_blocks(a, k, True))):
+            dev = to_dev(*args)
+            call = ((lambda y, fn=fn, d=dev, xd=xd: fn(d[0], d[1], 32, xd, y)) if len(dev) == 2
+                    else (lambda y, fn=fn, d=dev, xd=xd, k=k: fn(d[0], k // 32, xd, y)))
+            jobs.append((m, x, call, ofn, vals))
+    return jobs
+
+
+def run_batched(jobs):
+    """Each job's lone result, then all jobs in one batch (formats
+    interleaved, then grouped: every format switch launches the queue)."""
+    lone = []
+    for m, _, call, _, _ in jobs:
+        y = dev_y(m)
+        call(y)
+        lone.append(to_host(y))
+    order = list(range(len(jobs)))
+    order = order + sorted(order, key=lambda i: i % 5)
+    ys = [dev_y(jobs[i][0]) for i in order]
+    with L.batch():
+        for i, y in zip(order, ys):
+            jobs[i][2](y)
+    return lone, [(i, to_host(y)) for i, y in zip(order, ys)]
+
+
+def test_batch_fp32_exact_formats_equal_lone_calls_and_oracle():
+    jobs = fp32_jobs(1500)
+    with L.fp32_mode("exact"):
+        lone, got = run_batched(jobs)
+    for i, y in got:
+        assert_bits(y, lone[i])
+        assert_bits(y, jobs[i][3]())
+
+
+def test_batch_fp32_fast_formats_within_tolerance():
+    """The block-float fold is unordered, and its order follows the launch's
+    tiles, so a batched call may differ from the lone call in the last bits:
+    both are held to the fast-mode bound against the oracle."""
+    from test_gpu_fast_fp32 import assert_close
+    jobs = fp32_jobs(1600)
+    with L.fp32_mode("fast"):
+        lone, got = run_batched(jobs)
+    for i, y in got:
+        m, x, _, ofn, vals = jobs[i]
+        ref, wv = ofn(), vals()
+        assert_close(lone[i], ref, wv, x)
+        assert_close(y, ref, wv, x)
+
+
+@pytest.mark.parametrize("kind", ["q4_k", "q6_k"])
+def test_batch_kquant_gemvs_within_tolerance(kind):
+    from test_gpu_kquant_gemv import q4k_min_magnitude, rand_blocks
+    rng = np.random.default_rng(1700 + (7 if kind == "q6_k" else 0))
+    bb, dpos = (144, (0, 2)) if kind == "q4_k" else (210, (208,))
+    fn = L.dequantGemvQ4_K if kind == "q4_k" else L.dequantGemvQ6_K
+    cs = []
+    for M, sbpr in ((37, 16), (4096, 16), (300, 43), (11008, 16)):
+        raw = rand_blocks(rng, M * sbpr, bb, dpos)
+        K = 256 * sbpr
+        x = rng.standard_normal(K).astype(np.float32)
+        deq = (O.dequantizeQ4_K if kind == "q4_k" else O.dequantizeQ6_K)(raw.reshape(-1))
+        W = deq.reshape(M, K).astype(np.float64)
+        bound = np.abs(W) @ np.abs(x.astype(np.float64))
+        if kind == "q4_k":
+            xg = np.abs(x.astype(np.float64)).reshape(-1, 32).sum(1)
+            bound = bound + q4k_min_magnitude(raw, M, sbpr) @ xg
+        cs.append((M, sbpr, W @ x.astype(np.float64), bound,
+                   torch.from_numpy(raw.reshape(-1)).cuda(), torch.from_numpy(x).cuda()))
+    ys = [dev_y(c[0]) for c in cs]
+    with L.batch():
+        for c, y in zip(cs, ys):
+            fn(c[4], c[1], c[5], y)
+    for c, y in zip(cs, ys):
+        got = to_host(y).astype(np.float64)
+        assert np.all(np.abs(got - c[2]) <= 2e-6 * c[3]), np.max(np.abs(got - c[2]) / c[3])
