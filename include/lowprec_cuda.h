@@ -83,28 +83,33 @@ int lp_host_device_pointer(const void *host, void **dev);
 int lp_copy_in(void *dst, const void *src, int64_t bytes, lp_stream_t stream);
 
 /* Batched GEMV launches (no counterpart in the reference; the reference
- * runs each call on the CPU as it comes).  Device-form GEMVs of the
- * int8-activation formats (lp_dequant_gemv_q8 / _i4q8, the fused
- * lp_quantize_dequant_gemv_q8 / _i4q8, lp_dequant_gemv_q8_0q8 / _q4_0q8,
- * and their pooled forms) that this thread makes on `stream` between begin
- * and end are queued and run as one persistent launch per run of up to 64
- * consecutive same-format calls: the weights of call i+1 stream while call
+ * runs each call on the CPU as it comes).  Device-form GEMVs with one output
+ * per weight row -- every format: the fp32-activation ones (lp_dequant_gemv,
+ * _i4, _f4, _q8_0, _q4_0, _q4_k, _q6_k) in either fp32 mode, the
+ * int8-activation ones (lp_dequant_gemv_q8 / _i4q8, the fused
+ * lp_quantize_dequant_gemv_q8 / _i4q8, lp_dequant_gemv_q8_0q8 / _q4_0q8),
+ * and their pooled forms -- that this thread makes on `stream` between
+ * begin and end are queued and run as one persistent launch per run of up to
+ * 64 consecutive same-format calls: the weights of call i+1 stream while call
  * i's last rows fold, and each call's activations are staged once, by a small
- * kernel, for the whole launch.  A lone GEMV pays about 6 us of launch, staging
- * and fold latency; a decode step of many GEMVs pays it once.
- * Every call keeps its own checks and its results, bit for bit those of the
- * call made on its own.  Argument errors return at once.  Queued calls are
- * launched at end, or earlier when this thread makes any other launch of the
- * library (stream order holds), a call of another format or stream, a call
- * whose x or y meets an earlier queued call's y, or a 65th call; a launch
- * failure is returned by the call that launched, or by end.  y and x
- * pointers are read at launch, so queued buffers must stay allocated until
- * then.  Each launch stages the activations in a stream-ordered allocation
- * (cudaMallocAsync from the device's default pool, a few KB per call, freed
- * in stream order after it; graph memory nodes under stream capture) -- the
- * one allocation of the device forms.  Pooled calls in a gather group may
- * share a launch; the group's receive launches the queue first.  begin on an
- * open batch ends it. */
+ * kernel, for the whole launch.  A lone GEMV pays about 6 us of launch,
+ * staging and fold latency; a decode step of many GEMVs pays it once.
+ * Every call keeps its own checks and its results: bit for bit those of the
+ * call made on its own, except in LP_FP32_FAST mode, whose unordered fold
+ * follows the launch's row tiles, so a batched result may differ from the
+ * lone call's in the last bits (within the same bound).  Argument errors
+ * return at once.  Queued calls are launched at end, or earlier when this
+ * thread makes any other launch of the library (stream order holds), a call
+ * of another format, fp32 mode or stream, a call whose x or y meets an
+ * earlier queued call's y, or a 65th call; a launch failure is returned by
+ * the call that launched, or by end.  y and x pointers are read at launch, so
+ * queued buffers must stay allocated until then.  Each launch stages the
+ * activations in a stream-ordered allocation from a memory pool the library
+ * creates per device (a few KB to 44 KB per call, freed in stream order after
+ * it; up to 64 MB stay reserved for the next batch; graph memory nodes under
+ * stream capture) -- the one allocation of the device forms.  Pooled calls in
+ * a gather group may share a launch; the group's receive launches the queue
+ * first.  begin on an open batch ends it. */
 int lp_batch_begin(lp_stream_t stream);
 int lp_batch_end(lp_stream_t stream);
 
