@@ -1027,7 +1027,17 @@ def profile_kernels(torch, L):
     run("config1 dequantGemvQ4_0 block-float", lambda: L.dequantGemvQ4_0(blocks, K1 // 32, x, y))
     with L.fp32_mode("exact"):
         run("config1 dequantGemvQ4_0 exact", lambda: L.dequantGemvQ4_0(blocks, K1 // 32, x, y))
-    del blocks, x, y
+    # the config-1 call batched: 8 calls on weight copies (203 MB, above L2),
+    # one gemv_images_kernel and one gemv_batch_kernel
+    copies = [blocks] + [blocks.clone() for _ in range(7)]
+    ys8 = [torch.empty(M1, device="cuda") for _ in copies]
+
+    def batch8():
+        with L.batch():
+            for c, yy in zip(copies, ys8):
+                L.dequantGemvQ4_0(c, K1 // 32, x, yy)
+    run("config1 batched: 8 calls on weight copies", batch8)
+    del blocks, x, y, copies, ys8
     torch.cuda.empty_cache()
 
     w = rnd(M2 * K1, 2, 0.02)

@@ -124,6 +124,9 @@ struct BatchState {
   std::vector<GemvParams> jobs;
   std::vector<Range> outs;    // the recorded jobs' y
   int kept = LP_OK;           // first failed flush made on another call's behalf
+  const RecvSegs* recv = nullptr;  // a gather riding in the next launch (batch_flush_recv)
+  float* recv_y = nullptr;
+  bool recv_taken = false;
 };
 thread_local BatchState g_batch;
 
@@ -171,6 +174,8 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   static thread_local GemvBatch b;
   b.n = static_cast<int>(jobs.size());
   b.push = nullptr;
+  b.rs.n = 0;
+  b.ry = nullptr;
   // The jobs' rows laid end to end, each weighted by its bytes times the
   // consumers' slowdown on it: a thread keeps one group of the row, so when
   // the consumer count is not a multiple of the row's groups some threads
@@ -263,6 +268,10 @@ int launch_batch(std::vector<GemvParams>& jobs, cudaStream_t st) {
   b.off_b = b.off_t + ring * tslot * 4;
   const int smem = 128 + b.off_b + 8 * (2 * stages + 2 * ring + 2 * xbufs);
   for (int j = 0; j < b.n; ++j) b.job[j] = jobs[j];
+  if (g_batch.recv && b.push) {
+    b.rs = *g_batch.recv;
+    b.ry = g_batch.recv_y;
+  }
   // The images live for this launch only: a stream-ordered allocation (from
   // the library's pool), freed in stream order after the batch kernel (graph
   // memory nodes when the stream is being captured), so batches on other
@@ -346,6 +355,7 @@ int batch_flush() {
   auto single = bs.single;
   bs.fmt = nullptr;
   int r = launch(jobs, bs.st);
+  bs.recv_taken = r == LP_OK && bs.recv != nullptr;
   if (r == LP_ERR_UNSUPPORTED) {
     // no common layout: one launch per job, planned as a lone call (the
     // recorded jobs keep their push context)
@@ -354,6 +364,27 @@ int batch_flush() {
     for (size_t i = 0; i < jobs.size() && r == LP_OK; ++i) r = single(jobs[i], bs.st);
     bs.open = true;
   }
+  return r;
+}
+
+bool batch_takes_recv(const PushCtx* push, cudaStream_t st) {
+  const BatchState& bs = g_batch;
+  if (!bs.open || st != bs.st || !push) return false;
+  for (const auto& j : bs.jobs)
+    if (j.push == push) return true;  // a batch's jobs share one context (batch_record)
+  return false;
+}
+
+int batch_flush_recv(float* y, const RecvSegs& segs, bool* taken) {
+  BatchState& bs = g_batch;
+  bs.recv = &segs;
+  bs.recv_y = y;
+  bs.recv_taken = false;
+  const int r = batch_flush();
+  *taken = bs.recv_taken;
+  bs.recv = nullptr;
+  bs.recv_y = nullptr;
+  bs.recv_taken = false;
   return r;
 }
 

@@ -558,6 +558,11 @@ struct GemvBatch {
   int64_t total;             // work units of all jobs' rows (job[n - 1].bend)
   const PushCtx* push;       // the pooled jobs' exchange (one per batch), or null
   GemvParams job[kMaxBatch];
+  // A pull-form gather riding in this launch (rs.n > 0): every other rank's
+  // rows of the group's vector ry, read by each CTA once its rows are done;
+  // the launch then completes the gather (see batch_receive).
+  RecvSegs rs;
+  float* ry;
 };
 
 static_assert(sizeof(GemvParams) % 16 == 0, "job parameters are copied in 16-byte pieces");
@@ -619,12 +624,84 @@ __global__ void __launch_bounds__(512) gemv_images_kernel(const __grid_constant_
     reinterpret_cast<uint32_t*>(img + b.p_off)[i] = src[i];
 }
 
+// The receive of a batch that carries a pull-form gather, run by all of a
+// CTA's threads once its GEMV rows are done.  The segments laid end to end
+// are split evenly over the CTAs, in part order, so CTA c reads roughly the
+// parts that the other ranks' CTA c made, which are done about when its own
+// are.  Each thread keeps 8 words in flight; a word whose tag is not yet this
+// gather's is polled again (bounded, with a short sleep).  Only other GPUs'
+// outputs are waited on, and their kernels wait on nothing before making
+// them, so every wait ends.  (One extra warp per CTA reading the same words
+// while the GEMVs still streamed weights made the config-4 sweep on 2 GPUs
+// 1.7x slower; at the tail the exchange costs 0.79 us per layer there,
+// against 0.94 for a receive kernel after the batch.)
+__device__ __forceinline__ uint64_t ld_sys(const uint64_t* a) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+static __device__ __noinline__ void batch_receive(const GemvBatch& b, const PushTag& t, int tid,
+                                                  int nthr) {
+  const RecvSegs& segs = b.rs;
+  const uint32_t e = static_cast<uint32_t>(t.tag >> 32);
+  const int64_t total = segs.start[segs.n];
+  const int64_t C = gridDim.x;
+  const int64_t per = (total + C - 1) / C;
+  const int64_t lo = min(total, static_cast<int64_t>(blockIdx.x) * per), hi = min(total, lo + per);
+  int sg = 0;  // the segment of index lo + tid, advanced as the index grows
+  {
+    int a = 0, z = segs.n;
+    const int64_t i = lo + tid;
+    while (z - a > 1) {
+      const int mid = (a + z) >> 1;
+      if (segs.start[mid] <= i) a = mid; else z = mid;
+    }
+    sg = a;
+  }
+  bool ok = true;
+  const uint64_t t0 = global_ns();
+  constexpr int kF = 8;
+  for (int64_t i0 = lo + tid; i0 < hi && ok; i0 += kF * nthr) {
+    uint64_t w[kF];
+    int64_t at[kF];  // the word's element in ry and in its owner's exchange half
+    int src[kF];     // its owner
+#pragma unroll
+    for (int k = 0; k < kF; ++k) {
+      const int64_t i = i0 + k * nthr;
+      at[k] = -1;
+      w[k] = 0;
+      src[k] = 0;
+      if (i < hi) {
+        while (sg + 1 < segs.n && segs.start[sg + 1] <= i) ++sg;
+        at[k] = segs.off[sg] + (i - segs.start[sg]);
+        src[k] = segs.src[sg];
+        w[k] = ld_sys(reinterpret_cast<const uint64_t*>(b.push->peers[src[k]]) + t.half + at[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kF; ++k) {
+      if (at[k] < 0 || !ok) continue;
+      for (uint32_t n = 1; (w[k] >> 32) != e; ++n) {
+        if ((n & 255u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+          raise_error(LP_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        __nanosleep(128);
+        w[k] = ld_sys(reinterpret_cast<const uint64_t*>(b.push->peers[src[k]]) + t.half + at[k]);
+      }
+      if (ok) b.ry[at[k]] = __uint_as_float(static_cast<uint32_t>(w[k]));
+    }
+  }
+}
+
 template <class Fmt, int NCW>
 __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     gemv_batch_kernel(const __grid_constant__ GemvBatch b) {
   static_assert(!ColsOf<Fmt>::value, "row folds only");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ volatile int s_abort;
+  __shared__ uint32_t s_gather;  // the gather number a carried receive completes
   uint8_t* smem = smem_raw + ((128u - (saddr(smem_raw) & 127u)) & 127u);
   uint8_t* stw = smem + b.off_w;
   uint8_t* sts = smem + b.off_s;
@@ -718,6 +795,7 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     if (b.push) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
       pt = push_tag(b.push);
+      if (lane == 0) s_gather = static_cast<uint32_t>(pt.tag >> 32);
     }
     const CtaRange cr = cta_range(b.total);
     int tg = 0;
@@ -882,7 +960,7 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&xempty[buf]);
     }
-  } else {
+  } else if (warp == NCW + 2) {
     // ------------------------------------------------- image loader
     // Each job's staged activations, copied by this warp's 32 lanes with
     // 16-byte cp.async (the load path, not the bulk-copy engine: an image
@@ -933,6 +1011,27 @@ __global__ void __launch_bounds__(32 * (NCW + 3), 1)
     }
     // never leave with a copy still landing in shared memory
     asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+  if (b.rs.n > 0) {
+    // The other ranks' rows, then the gather is complete on this rank once
+    // every CTA's folds (this rank's rows) and receive are done: the last
+    // CTA to get here publishes its number, which the next gather's kernels
+    // read.  (The folder took the number after its grid-dependency wait.)
+    __syncthreads();
+    PushTag t;
+    t.tag = static_cast<uint64_t>(s_gather) << 32;
+    t.half = (s_gather & 1u) * kXchgWords;
+    batch_receive(b, t, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      uint32_t* state = b.push->state;
+      if (atomicAdd(state + 1, 1u) == gridDim.x - 1) {
+        state[1] = 0;
+        __threadfence();
+        atomicExch(state, s_gather);
+      }
+    }
   }
 }
 

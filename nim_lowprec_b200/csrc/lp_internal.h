@@ -72,6 +72,25 @@ int launch_gemv(GemvParams p, cudaStream_t st);
 // Every other launch of the library flushes first, so stream order holds.
 bool batch_open();
 int batch_flush();
+// What a rank receives in a gather over the exchange: every other rank's rows
+// of every part, as segments of the vector laid end to end (start: prefix
+// sums of their lengths; off: each segment's first element in y and in the
+// exchange; src: the rank whose buffer holds it).
+constexpr int kMaxGatherParts = 64;  // a 32-layer sweep's two GEMVs per layer
+constexpr int kMaxRecvSegs = kMaxGatherParts * (kMaxPushRanks - 1);
+struct RecvSegs {
+  int64_t start[kMaxRecvSegs + 1];
+  int64_t off[kMaxRecvSegs];
+  int src[kMaxRecvSegs];
+  int n;
+};
+// A pull-form gather whose rows were all published by queued GEMVs with
+// context `push` can ride in the open batch's launch on `st`:
+// batch_flush_recv launches the queue with a receive warp per CTA reading
+// segs into y, and says in *taken whether it did (not when the queue fell
+// back to lone launches; the caller then launches the receive kernel).
+bool batch_takes_recv(const PushCtx* push, cudaStream_t st);
+int batch_flush_recv(float* y, const RecvSegs& segs, bool* taken);
 void batch_flush_keep();  // a failure is returned by batch_end
 int batch_begin(cudaStream_t st);
 int batch_end(cudaStream_t st);

@@ -42,22 +42,13 @@ struct PeerBufs {
 };
 // A gathered vector made of up to kMaxParts regions, each m rows of per_row
 // floats at element offset off, its rows sliced over the ranks.
-constexpr int kMaxParts = 64;  // a 32-layer sweep's two GEMVs per layer
+constexpr int kMaxParts = lp::kMaxGatherParts;
 struct GatherParts {
   int64_t off[kMaxParts], m[kMaxParts], prow[kMaxParts];
   int send[kMaxParts];  // 1: the receive kernel also stores this rank's rows of the part
   int n;
 };
-// What this rank receives: every other rank's rows of every part, as
-// segments of the vector laid end to end (start: prefix sums of their
-// lengths; off: each segment's first element in y and in the exchange).
-constexpr int kMaxSegs = kMaxParts * (kMaxP2pRanks - 1);
-struct RecvSegs {
-  int64_t start[kMaxSegs + 1];
-  int64_t off[kMaxSegs];
-  int src[kMaxSegs];  // the rank whose exchange buffer holds the segment
-  int n;
-};
+using lp::RecvSegs;
 }  // namespace
 
 struct lp_pool {
@@ -129,6 +120,7 @@ inline cudaStream_t S(lp_stream_t s) {
   if (lp::batch_open()) lp::batch_flush_keep();
   return static_cast<cudaStream_t>(s);
 }
+inline cudaStream_t SG(lp_stream_t s) { return static_cast<cudaStream_t>(s); }
 
 __host__ __device__ inline void rows_of(int64_t m, int nranks, int rank, int64_t* b, int64_t* e) {
   const int64_t per = m / nranks;
@@ -276,8 +268,8 @@ __global__ void __launch_bounds__(256) k_gather_p2p(float* y, const __grid_const
 // group's length only, so every rank makes the same one.
 constexpr int64_t kPullFloats = int64_t{1} << 18;
 
-int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st, int pull) {
-  static thread_local RecvSegs segs;
+// Every other rank's rows of every part, in part order, then rank order.
+void build_segs(const lp_pool* p, const GatherParts& parts, RecvSegs& segs) {
   segs.n = 0;
   segs.start[0] = 0;
   for (int i = 0; i < parts.n; ++i)
@@ -291,6 +283,11 @@ int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st
       segs.start[segs.n + 1] = segs.start[segs.n] + (e - b) * parts.prow[i];
       ++segs.n;
     }
+}
+
+int gather_parts(lp_pool* p, float* y, const GatherParts& parts, cudaStream_t st, int pull) {
+  static thread_local RecvSegs segs;
+  build_segs(p, parts, segs);
   // CTAs enough for ~2048 received words each, at most two per SM (all
   // resident at once: a sending CTA waits only after its own stores)
   const int64_t recv = segs.start[segs.n];
@@ -563,7 +560,25 @@ int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream) {
   if (pool->grp_parts.n == 0 || pool->nranks < 2) return LP_OK;
   int r = lp::cuda_status(cudaSetDevice(pool->device));
   if (r) return r;
-  r = gather_parts(pool, pool->grp_y, pool->grp_parts, S(stream), pool->grp_len >= kPullFloats);
+  const int pull = pool->grp_len >= kPullFloats;
+  const GatherParts& gp = pool->grp_parts;
+  bool published = pull != 0;
+  for (int i = 0; i < gp.n && published; ++i) published = gp.send[i] == 0;
+  // A pull-form group whose rows were all published by the GEMVs' folds,
+  // with GEMVs of it still queued in an open batch: the receive rides in that
+  // batch's launch, its reads of the other ranks' rows overlapping the
+  // weight stream, instead of a receive kernel after it.
+  if (published && lp::batch_takes_recv(pool->pull, SG(stream))) {
+    static thread_local RecvSegs segs;
+    build_segs(pool, gp, segs);
+    bool taken = false;
+    r = lp::batch_flush_recv(pool->grp_y, segs, &taken);
+    if (r != LP_OK || taken) {
+      pool->grp_parts.n = 0;
+      return r;
+    }
+  }
+  r = gather_parts(pool, pool->grp_y, gp, S(stream), pull);
   pool->grp_parts.n = 0;
   return r;
 }

@@ -222,6 +222,44 @@ def _rank_main(rank, world, port, q):
                     same(f"pull-group-b{int(batched)}-{i_}", yb[off:off + mj], rj)
                     off += mj
                 same(f"pull-group-b{int(batched)}-gemm", yb[off:], refgm)
+            # a pull-form group whose every part is published by a queued
+            # GEMV's fold: the receive rides in the last batch launch (one
+            # receive warp per CTA reads the other ranks' rows while the
+            # GEMVs run), the parts in two formats (two batch launches, the
+            # receive in whichever comes last), three times in a row with a
+            # lone pooled call (its own gather) in between
+            with L.fp32_mode("exact"):
+                refq4x = torch.empty(M, device="cuda")
+                L.dequantGemvQ4_0(blk, K // 32, x[:K], refq4x)
+                nq4 = 13
+                totf = sum(b_[0] for b_ in big) + nq4 * M
+                assert totf >= 1 << 18
+                for rep_ in range(3):
+                    yf = torch.full((totf,), float("nan"), device="cuda")
+                    q4_first = rep_ == 1
+                    with L.batch():
+                        npl.group_begin(yf)
+                        off = 0
+                        spans = []
+                        order = ["q4", "i4"] if q4_first else ["i4", "q4"]
+                        for kind in order:
+                            if kind == "i4":
+                                for mj, pj, sj, rj in big:
+                                    P.parDequantGemvI4Q8(npl, pj, sj, 32, xq[:64], xd[:2],
+                                                         yf[off:off + mj])
+                                    spans.append((off, mj, rj))
+                                    off += mj
+                            else:
+                                for _ in range(nq4):
+                                    P.parDequantGemvQ4_0(npl, blk, K // 32, x[:K], yf[off:off + M])
+                                    spans.append((off, M, refq4x))
+                                    off += M
+                        npl.group_end()
+                    for i_, (o_, mj, rj) in enumerate(spans):
+                        same(f"fused-recv{rep_}-{i_}", yf[o_:o_ + mj], rj)
+                    y1 = torch.full((M,), float("nan"), device="cuda")
+                    P.parDequantGemvQ8(npl, wq, wd, 32, xq[:K], xd[:K // 32], y1)
+                    same(f"fused-recv{rep_}-lone", y1, refq8)
         # the library pool gathers over NVLink by default (one GPU per rank);
         # both transports, back-to-back gathers (alternating exchange halves)
         # and CUDA-graph replays give the single-GPU bits
