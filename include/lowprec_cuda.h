@@ -461,9 +461,9 @@ int lp_pool_get_p2p(lp_pool_t pool, int *enabled);
  * A group of 2^18 floats or more (a whole decode step) has each GEMV publish
  * its outputs in its own rank's exchange buffer and the receive read the
  * other ranks' buffers over NVLink; smaller gathers store into every other
- * rank's buffer from the GEMV.  When such a group's parts are all GEMVs and
- * some are still queued in an open batch (lp_batch_begin) at end, the receive
- * runs at the end of that batch's launch, in each CTA once its rows are done,
+ * rank's buffer from the GEMV.  When a group's parts are all GEMVs and some
+ * are still queued in an open batch (lp_batch_begin) at end, the receive runs
+ * at the end of that batch's launch, in each CTA once its rows are done,
  * instead of in a kernel of its own.  Same results either way. */
 int lp_pool_group_begin(lp_pool_t pool, float *y, int64_t y_len);
 int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream);

@@ -558,7 +558,7 @@ struct GemvBatch {
   int64_t total;             // work units of all jobs' rows (job[n - 1].bend)
   const PushCtx* push;       // the pooled jobs' exchange (one per batch), or null
   GemvParams job[kMaxBatch];
-  // A pull-form gather riding in this launch (rs.n > 0): every other rank's
+  // A gather riding in this launch (rs.n > 0): every other rank's
   // rows of the group's vector ry, read by each CTA once its rows are done;
   // the launch then completes the gather (see batch_receive).
   RecvSegs rs;
@@ -624,8 +624,8 @@ __global__ void __launch_bounds__(512) gemv_images_kernel(const __grid_constant_
     reinterpret_cast<uint32_t*>(img + b.p_off)[i] = src[i];
 }
 
-// The receive of a batch that carries a pull-form gather, run by all of a
-// CTA's threads once its GEMV rows are done.  The segments laid end to end
+// The receive of a batch that carries a gather, run by all of a CTA's
+// threads once its GEMV rows are done.  The segments laid end to end
 // are split evenly over the CTAs, in part order, so CTA c reads roughly the
 // parts that the other ranks' CTA c made, which are done about when its own
 // are.  Each thread keeps 8 words in flight; a word whose tag is not yet this
@@ -658,6 +658,9 @@ static __device__ __noinline__ void batch_receive(const GemvBatch& b, const Push
     }
     sg = a;
   }
+  // pull form: the words wait in their owner's buffer; push form: the
+  // owners stored them into this rank's buffer from their folds
+  const int pull = b.push->pull, me = b.push->rank;
   bool ok = true;
   const uint64_t t0 = global_ns();
   constexpr int kF = 8;
@@ -674,7 +677,7 @@ static __device__ __noinline__ void batch_receive(const GemvBatch& b, const Push
       if (i < hi) {
         while (sg + 1 < segs.n && segs.start[sg + 1] <= i) ++sg;
         at[k] = segs.off[sg] + (i - segs.start[sg]);
-        src[k] = segs.src[sg];
+        src[k] = pull ? segs.src[sg] : me;
         w[k] = ld_sys(reinterpret_cast<const uint64_t*>(b.push->peers[src[k]]) + t.half + at[k]);
       }
     }

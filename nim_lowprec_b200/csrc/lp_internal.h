@@ -84,8 +84,8 @@ struct RecvSegs {
   int src[kMaxRecvSegs];
   int n;
 };
-// A pull-form gather whose rows were all published by queued GEMVs with
-// context `push` can ride in the open batch's launch on `st`:
+// A gather whose rows were all published by queued GEMVs with context
+// `push` can ride in the open batch's launch on `st`:
 // batch_flush_recv launches the queue with a receive warp per CTA reading
 // segs into y, and says in *taken whether it did (not when the queue fell
 // back to lone launches; the caller then launches the receive kernel).

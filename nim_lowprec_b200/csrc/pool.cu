@@ -562,13 +562,12 @@ int lp_pool_group_end(lp_pool_t pool, lp_stream_t stream) {
   if (r) return r;
   const int pull = pool->grp_len >= kPullFloats;
   const GatherParts& gp = pool->grp_parts;
-  bool published = pull != 0;
+  bool published = pool->p2p != 0;
   for (int i = 0; i < gp.n && published; ++i) published = gp.send[i] == 0;
-  // A pull-form group whose rows were all published by the GEMVs' folds,
-  // with GEMVs of it still queued in an open batch: the receive rides in that
-  // batch's launch, its reads of the other ranks' rows overlapping the
-  // weight stream, instead of a receive kernel after it.
-  if (published && lp::batch_takes_recv(pool->pull, SG(stream))) {
+  // A group whose rows were all published by the GEMVs' folds, with GEMVs of
+  // it still queued in an open batch: the receive rides at the end of that
+  // batch's launch instead of in a receive kernel after it.
+  if (published && lp::batch_takes_recv(pull ? pool->pull : pool->push, SG(stream))) {
     static thread_local RecvSegs segs;
     build_segs(pool, gp, segs);
     bool taken = false;
