@@ -78,7 +78,9 @@ def element_codecs():
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NIM_LOWPREC_REF", "/root/reference")
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NIM_LOWPREC_REF")
+    if not ref_root:
+        sys.exit("usage: make_golden.py <nim-lowprec checkout> (or set NIM_LOWPREC_REF)")
     gen = load_reference_generator(ref_root)
     gen.emit_ggml_schemes()
     gen.emit_mx_schemes()
